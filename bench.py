@@ -1,0 +1,462 @@
+#!/usr/bin/env python3
+"""bench.py -- throughput of the mcke sm_100a kernel path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mcke|reference] [--ops LIST]
+
+N > 1 is launched by torchrun (one process per GPU, NCCL); rank 0 prints ONE
+JSON line.
+
+Headline (``value``): BASELINE config 2, row softmax fp32 over logits
+[32768 x 1024] ~ N(0, 4^2) with every 64th row shifted by +80.  A step is one
+softmax pass over the whole batch, inputs already resident in HBM.  Bytes per
+step are algorithmic, 2 * 32768 * 1024 * 4 = 268,435,456 (one read of x, one
+write of y).  L2 is flushed (a 256 MiB write) between timed steps, outside the
+timed region; each step is timed with CUDA events on the launching stream.
+At N GPUs every rank processes its own full batch (weak scaling) and
+``value`` = N * bytes / (max over ranks of the summed step time).
+
+``e2e``: the same step through the public API with HOST buffers: the pinned
+host logits are copied in, softmax runs, the probabilities are copied back,
+all inside the timed region.
+
+``ops``: the other BASELINE configs at their full sizes (bias+GELU fp32,
+full reduce fp32 sum/max/argmax, bf16 and fp32 GEMM 8192^3), each as an
+absolute number and a roofline fraction; at N > 1 these are sharded across
+ranks over a fixed total (strong scaling): rows, contiguous ranges with one
+NCCL all-gather of 24-byte partials, and output columns respectively.
+
+``--impl reference`` times the reference's own CPU implementation
+(tests/reference.hpp compiled into oracle/_ref; the C restatement if that
+library is absent) on the host cores, on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mini-cuda-kernel-engine_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "GEMM TFLOP/s; softmax/reduce/bias-GELU GB/s as % of B200 peak at 1/2/4/8 GPU"
+ROWS, COLS = 32768, 1024
+SOFTMAX_BYTES = 2 * ROWS * COLS * 4
+BIAS_ROWS, BIAS_COLS = 4096, 4096
+BIAS_BYTES = (2 * BIAS_ROWS * BIAS_COLS + BIAS_COLS) * 4
+REDUCE_N = 1 << 28
+REDUCE_BYTES = REDUCE_N * 4
+GEMM_N = 8192
+GEMM_FLOPS = 2 * GEMM_N ** 3
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic() -> dict:
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this GPU while the timed work runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.path = os.path.join("/tmp", f"mcke_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "samples_under_load": 0}
+        if self.proc is None or not os.path.exists(self.path):
+            out["note"] = "nvidia-smi unavailable"
+            return out
+        rows = []
+        with open(self.path) as f:
+            for ln in f:
+                parts = [p.strip() for p in ln.split(",")]
+                if len(parts) < 10:
+                    continue
+                if self.uuid and self.uuid not in parts[0]:
+                    continue
+                rows.append(parts)
+        out["samples"] = len(rows)
+        load = [r for r in rows if r[4].replace(".", "").isdigit() and float(r[4]) >= 50.0]
+        out["samples_under_load"] = len(load)
+        use = load or rows
+        try:
+            if use:
+                out["sm_mhz"] = statistics.median(float(r[1]) for r in use)
+                out["sm_max_mhz"] = max(float(r[2]) for r in use)
+                out["power_w_max"] = max(float(r[3]) for r in use)
+        except ValueError:
+            pass
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for k, name in enumerate(names):
+            if any(r[6 + k].lower().startswith("active") for r in use):
+                out["reasons"].append(name)
+        if not load:
+            out["note"] = "no sample caught the GPU busy (timed region shorter than the 200 ms sampling period)"
+        return out
+
+
+# --------------------------------------------------------------- helpers
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, torch, backend="nccl"):
+        if self.world > 1:
+            import datetime
+            import torch.distributed as td
+            td.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                  device_id=torch.device("cuda", self.local) if backend == "nccl" else None)
+            self.pg = td
+
+    def barrier(self, torch):
+        if self.pg is not None:
+            t = torch.zeros(1, device="cuda")
+            self.pg.all_reduce(t)
+            torch.cuda.synchronize()
+
+    def max(self, torch, v: float) -> float:
+        if self.pg is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def timed_steps(torch, dist, launch, steps: int, warmup: int, flush=None, per_launch_kernels=1):
+    """Warm up, then time exactly `steps` launches, each bracketed by CUDA events on
+    the current stream, with an L2 flush between steps outside the events.
+    Returns (total_ms max over ranks, list of per-step ms on this rank)."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush()
+        ev[i][0].record(stream)
+        launch()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    torch.cuda.synchronize()
+    per = [a.elapsed_time(b) for a, b in ev]
+    return dist.max(torch, sum(per)), per
+
+
+# ------------------------------------------------------------ reference arm
+
+def run_reference(args, dist) -> None:
+    if dist.rank != 0:
+        return
+    import oracle
+    impl = "reference" if oracle.have_reference() else "port"
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    rows_per_step = ROWS  # full batch per step; a step takes ~1 s of CPU work per thread-second budget
+    x = oracle.softmax_config_input(ROWS, COLS, seed=2)
+    y = np.empty_like(x)
+
+    def step():
+        oracle.parallel_rows(lambda xs, ys: ys.__setitem__(slice(None), oracle.row_softmax(xs, impl=impl)),
+                             x[:rows_per_step], y[:rows_per_step], threads)
+
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    # keep the whole --steps/--warmup run within ~2 minutes
+    budget = 120.0
+    if one * (args.steps + args.warmup) > budget:
+        rows_per_step = max(64, int(ROWS * budget / (one * (args.steps + args.warmup))) // 64 * 64)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    bytes_per_step = 2 * rows_per_step * COLS * 4
+    value = bytes_per_step * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows": ROWS, "cols": COLS,
+                   "rows_per_step": rows_per_step},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "reference" if impl == "reference" else "port",
+                         "sample": f"{rows_per_step} of {ROWS} rows x {COLS} per step, tests/reference.hpp "
+                                   f"reference_row_softmax on {threads} host threads over disjoint row blocks"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- our arm
+
+def cpu_baseline_softmax() -> dict:
+    import oracle
+    impl = "reference" if oracle.have_reference() else "port"
+    threads = max(1, min(os.cpu_count() or 1, 64))
+    x = oracle.softmax_config_input(ROWS, COLS, seed=2)
+    y = np.empty_like(x)
+    fn = lambda xs, ys: ys.__setitem__(slice(None), oracle.row_softmax(xs, impl=impl))  # noqa: E731
+    reps, t_total = 0, 0.0
+    while reps < 3 or (t_total * threads < 10.0 and reps < 20):
+        t0 = time.perf_counter()
+        oracle.parallel_rows(fn, x, y, threads)
+        t_total += time.perf_counter() - t0
+        reps += 1
+    v = SOFTMAX_BYTES * reps / t_total / 1e9
+    return {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": impl,
+            "sample": f"full {ROWS}x{COLS} batch x {reps} passes on {threads} host threads "
+                      f"(reference_row_softmax over disjoint row blocks)"}
+
+
+def run_mcke(args, dist) -> None:
+    import torch
+    torch.cuda.set_device(dist.local)
+    dist.init(torch)
+    import mcke
+    mcke.lib()
+    dev = torch.device("cuda", dist.local)
+    peaks, peak_kind = load_peaks()
+    traffic = load_traffic()
+    g = dist.world
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)  # noqa: E731
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2 + dist.rank)
+    x = torch.randn(ROWS, COLS, generator=gen, device=dev) * 4.0
+    x[::64] += 80.0
+    y = torch.empty_like(x)
+
+    result: dict = {}
+    with ClockSampler(uuid) as clocks:
+        total_ms, per = timed_steps(torch, dist, lambda: mcke.softmax(x, out=y), args.steps, args.warmup, flush)
+        kernel_ms = statistics.mean(per)
+        achieved = SOFTMAX_BYTES / (kernel_ms * 1e-3) / 1e9
+        value = g * SOFTMAX_BYTES * args.steps / (total_ms * 1e-3) / 1e9
+
+        # e2e: host buffers, H2D + kernel + D2H inside the timed region
+        xh = x.cpu().pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(x)
+        yd = torch.empty_like(x)
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            mcke.softmax(xd, out=yd)
+            yh.copy_(yd, non_blocking=True)
+
+        e2e_ms, _ = timed_steps(torch, dist, e2e_step, max(3, min(args.steps, 20)), 2)
+        e2e_steps = max(3, min(args.steps, 20))
+        e2e_value = g * SOFTMAX_BYTES * e2e_steps / (e2e_ms * 1e-3) / 1e9
+
+        ops = {}
+        if args.ops:
+            ops = run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic)
+    del flush_buf
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": g, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (torch.randn * 4 on device, seed 2 + rank; every 64th row +80)",
+        "config": {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows_per_gpu": ROWS,
+                   "cols": COLS, "l2": "flushed between timed steps (256 MiB write)",
+                   "parallelism": f"rows, weak scaling, {g} x full batch"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs"),
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_kind": f"{peak_kind} hbm_gbs",
+                     "traffic": traffic.get("softmax_warp_row_kernel"),
+                     "algorithmic_bytes_per_launch": SOFTMAX_BYTES, "kernel_ms": round(kernel_ms, 5)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": SOFTMAX_BYTES // 2,
+                "d2h_bytes_per_step": SOFTMAX_BYTES // 2, "ms_per_step": round(e2e_ms / e2e_steps, 4)},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "ops": ops,
+    }
+    if dist.rank == 0 and g == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline_softmax()
+    dist.close()
+    if dist.rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
+    g, r = dist.world, dist.rank
+    want = set(args.ops.split(","))
+    out = {}
+    steps = max(3, min(args.steps, 50))
+    warm = max(3, min(args.warmup, 5))
+
+    def shard(n):
+        return n * r // g, n * (r + 1) // g
+
+    if "bias_gelu" in want:
+        r0, r1 = shard(BIAS_ROWS)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        xb = torch.randn(BIAS_ROWS, BIAS_COLS, generator=gen, device=dev)[r0:r1].contiguous()
+        bb = torch.rand(BIAS_COLS, generator=gen, device=dev) * 2 - 1
+        yb = torch.empty_like(xb)
+        ms, per = timed_steps(torch, dist, lambda: mcke.bias_act(xb, bb, "gelu_tanh", out=yb), steps, warm, flush)
+        kms = statistics.mean(per)
+        loc = (2 * (r1 - r0) * BIAS_COLS + BIAS_COLS) * 4
+        ach = loc / (kms * 1e-3) / 1e9
+        out["bias_gelu_fp32_4096x4096"] = {
+            "value": round(BIAS_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
+            "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
+            "kernel_ms": round(kms, 5), "algorithmic_bytes": BIAS_BYTES,
+            "traffic": traffic.get("bias_act_f32_kernel")}
+        del xb, yb
+
+    if "reduce" in want:
+        r0, r1 = shard(REDUCE_N)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1)
+        xr = (torch.rand(r1 - r0, generator=gen, device=dev) * 2 - 1)
+        ws = torch.empty(mcke.reduce_full_workspace_bytes(r1 - r0), dtype=torch.uint8, device=dev)
+        res = torch.empty(16, dtype=torch.uint8, device=dev)
+        part = torch.empty(24, dtype=torch.uint8, device=dev)
+        parts = torch.empty(24 * g, dtype=torch.uint8, device=dev)
+        if g == 1:
+            launch = lambda: mcke.reduce_full(xr, out=res, workspace=ws)  # noqa: E731
+        else:
+            def launch():
+                mcke.reduce_full_partial(xr, r0, out=part, workspace=ws)
+                dist.pg.all_gather_into_tensor(parts, part)
+                mcke.reduce_combine(parts, g, out=res)
+        ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
+        kms = statistics.mean(per)
+        ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9
+        out["reduce_full_fp32_2^28"] = {
+            "value": round(REDUCE_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
+            "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
+            "step_ms": round(kms, 5), "collective": "nccl all_gather of 24-byte partials" if g > 1 else None,
+            "traffic": traffic.get("reduce_full_pass1_kernel")}
+        del xr
+
+    if "gemm_bf16" in want:
+        n0, n1 = shard(GEMM_N)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(2)
+        a = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
+        gen.manual_seed(3)
+        b = ((torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1)[:, n0:n1]).to(torch.bfloat16).contiguous()
+        c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
+        ms, per = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c, variant="tcgen05"), steps, warm, flush)
+        mcke.check_device_errors()
+        kms = statistics.mean(per)
+        loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
+        ach = loc_flops / (kms * 1e-3) / 1e12
+        out["gemm_bf16_8192^3"] = {
+            "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
+            "per_gpu_achieved": round(ach, 1), "frac_of_bf16_peak": round(ach / peaks["bf16_tflops"], 4),
+            "peak": peaks["bf16_tflops"], "kernel_ms": round(kms, 4), "parallelism": f"columns of B and C over {g}"}
+        del a, b, c
+
+    if "gemm_f32" in want:
+        n0, n1 = shard(GEMM_N)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(2)
+        a = torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1
+        gen.manual_seed(3)
+        b = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1)[:, n0:n1].contiguous()
+        c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
+        fs = max(2, min(steps, 5))
+        ms, per = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c), fs, 1, None)
+        kms = statistics.mean(per)
+        loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
+        out["gemm_f32_8192^3"] = {
+            "value": round(GEMM_FLOPS * fs / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "scaling": "strong",
+            "per_gpu_achieved": round(loc_flops / (kms * 1e-3) / 1e12, 2), "kernel_ms": round(kms, 3),
+            "note": "fp32 FFMA (CUDA cores); bf16 tensor-core peak does not apply"}
+        del a, b, c
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mcke", "reference"], default="mcke")
+    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,gemm_f32",
+                    help="comma list of extra configs to report under 'ops' ('' for none)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist()
+    if args.impl == "reference":
+        run_reference(args, dist)
+    else:
+        run_mcke(args, dist)
+
+
+if __name__ == "__main__":
+    main()

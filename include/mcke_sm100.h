@@ -1,0 +1,182 @@
+/*
+ * mcke_sm100.h -- C-ABI of libmcke_sm100a.so, the B200 (sm_100a) kernel library
+ * that replaces mini-cuda-kernel-engine's kernel layer (its kernels/*.cu).
+ *
+ * Every entry point is a plain C function over caller-owned device pointers,
+ * int64 extents and enum ints, enqueued on an explicit CUDA stream.  None
+ * synchronises, none allocates device memory (scratch is caller-provided and
+ * sized by a *_workspace_bytes query), and each returns an mcke_status code:
+ * the numbering is the reference's StatusCode (include/mcke/core/status.hpp:42).
+ * The message of the last failing call on the calling thread is available from
+ * mcke_sm100_last_error_string().
+ *
+ * Error behaviour follows the reference launchers: empty extents return OK
+ * without a launch; negative extents, null pointers, an output aliasing an
+ * input, an illegal vector width, misalignment and extents beyond launch limits
+ * return MCKE_INVALID_ARGUMENT; an unsupported variant is rejected, never
+ * silently downgraded.  A failed CUDA launch returns MCKE_CUDA_ERROR.
+ *
+ * Each declaration names the reference interface it replaces (path:line within
+ * mini-cuda-kernel-engine).  The C++ launchers of include/mcke/kernels/kernels.hpp
+ * become thin wrappers over these; the wrapper source is shown in INTEGRATION.md.
+ */
+#ifndef MCKE_SM100_H_
+#define MCKE_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t (struct CUstream_st*), declared without CUDA headers. */
+typedef struct CUstream_st* mcke_stream_t;
+
+/* include/mcke/core/status.hpp:42 StatusCode, same values. */
+typedef enum {
+  MCKE_OK = 0,
+  MCKE_OUT_OF_MEMORY = 1,
+  MCKE_INVALID_ARGUMENT = 2,
+  MCKE_FAILED_PRECONDITION = 3,
+  MCKE_UNIMPLEMENTED = 4,
+  MCKE_INTERNAL = 5,
+  MCKE_CUDA_ERROR = 6
+} mcke_status;
+
+/* include/mcke/kernels/kernels.hpp:65 Activation, same values. */
+typedef enum { MCKE_ACT_NONE = 0, MCKE_ACT_RELU = 1, MCKE_ACT_GELU_ERF = 2, MCKE_ACT_GELU_TANH = 3 } mcke_activation;
+/* include/mcke/kernels/kernels.hpp:153 ReduceKind, same values. */
+typedef enum { MCKE_REDUCE_SUM = 0, MCKE_REDUCE_MAX = 1, MCKE_REDUCE_MEAN = 2 } mcke_reduce_kind;
+/* include/mcke/kernels/kernels.hpp:180 ReduceVariant, same values. */
+typedef enum { MCKE_REDUCE_SMEM_TREE = 0, MCKE_REDUCE_WARP_SHUFFLE = 1, MCKE_REDUCE_TWO_PASS = 2 } mcke_reduce_variant;
+/* include/mcke/kernels/kernels.hpp:218 SoftmaxVariant, same values.  ONLINE
+ * selects the single-read register-resident kernel whenever a row fits
+ * (cols % 4 == 0, 16-byte aligned rows, cols <= 16384), else the two-read
+ * online kernel. */
+typedef enum { MCKE_SOFTMAX_THREE_PASS = 0, MCKE_SOFTMAX_ONLINE = 1 } mcke_softmax_variant;
+/* GEMM kernels of this library (the reference's ladder is
+ * include/mcke/kernels/gemm_tile.hpp:209 GemmVariant; its kernels are replaced,
+ * so its values are not reused).  AUTO picks TCGEN05 for bf16 when the shape
+ * meets the TMA rules (K % 8 == 0, N % 8 == 0, 16-byte aligned A and B),
+ * else SIMT; for f32 it picks SIMT. */
+typedef enum { MCKE_GEMM_AUTO = 0, MCKE_GEMM_SIMT = 1, MCKE_GEMM_TCGEN05 = 2 } mcke_gemm_variant;
+/* Element type of a GEMM output. */
+typedef enum { MCKE_DTYPE_F32 = 0, MCKE_DTYPE_BF16 = 2 } mcke_dtype;
+
+/* Result of a full-vector reduce: 16 bytes, device memory. */
+typedef struct {
+  float sum;      /* sum of all elements, accumulated in double, rounded once */
+  float max;      /* largest non-NaN element (-inf if none), bit pattern of x[argmax] */
+  int64_t argmax; /* lowest index holding max; -1 when n == 0 or every element is NaN */
+} mcke_reduce_result;
+
+/* One shard's partial of a full-vector reduce: 24 bytes, device memory.
+ * Partials from several shards are combined, in shard order, by
+ * mcke_sm100_reduce_combine. */
+typedef struct {
+  double sum;
+  float max;
+  int32_t reserved;
+  int64_t argmax; /* global index (index_base already added), -1 if none */
+} mcke_reduce_partial;
+
+/* What ptxas produced for one GEMM kernel (include/mcke/kernels/kernels.hpp:293). */
+typedef struct {
+  int regs_per_thread;
+  size_t static_smem_bytes;
+  size_t dynamic_smem_bytes;
+  size_t local_bytes; /* > 0 means spilling */
+  int threads_per_block;
+  int max_blocks_per_sm_api;
+} mcke_gemm_attrs;
+
+/* ---- library ------------------------------------------------------------ */
+
+/* Version of this ABI (major * 10000 + minor * 100 + patch). */
+int mcke_sm100_version(void);
+/* Message of the last failing call on this thread ("" if none). */
+const char* mcke_sm100_last_error_string(void);
+/* Synchronises `stream`, then reads and clears the device-side watchdog word of
+ * the current device: 0 if no kernel of this library gave up on a bounded wait
+ * since the last call, else MCKE_INTERNAL with the site in the message. */
+int mcke_sm100_check_device_errors(mcke_stream_t stream);
+
+/* ---- bias + activation: y[r][c] = act(x[r][c] + bias[c]) ---------------- */
+
+/* Replaces kernels.hpp:102 launch_bias_act_f32 (kernels/bias_act.cu:269).
+ * vector_width in {1,2,4}; cols % vector_width == 0; x, y, bias aligned to
+ * 4*vector_width bytes; x != y.  max_row_blocks > 0 caps the row-direction
+ * grid (the reference's starvation knob); 0 = automatic. */
+int mcke_sm100_bias_act_f32(const float* x, const float* bias, float* y, int64_t rows,
+                            int64_t cols, int act, int vector_width, int max_row_blocks,
+                            mcke_stream_t stream);
+/* Replaces kernels.hpp:129 launch_bias_add_f32 (bias_act with MCKE_ACT_NONE). */
+int mcke_sm100_bias_add_f32(const float* x, const float* bias, float* y, int64_t rows,
+                            int64_t cols, int vector_width, mcke_stream_t stream);
+/* Replaces kernels.hpp:133 launch_activation_f32 (n % vector_width == 0). */
+int mcke_sm100_activation_f32(const float* x, float* y, int64_t n, int act, int vector_width,
+                              mcke_stream_t stream);
+/* New (bf16 path of the same op): x, y bfloat16 [rows, cols] (raw 16-bit
+ * patterns), bias float32 [cols]; math in float, one round-to-nearest-even on
+ * store.  cols % 8 == 0 and 16-byte aligned x, y take the 8-wide path; any
+ * other shape takes a scalar path. */
+int mcke_sm100_bias_act_bf16(const uint16_t* x, const float* bias, uint16_t* y, int64_t rows,
+                             int64_t cols, int act, mcke_stream_t stream);
+
+/* ---- row softmax over the last dim -------------------------------------- */
+
+/* Replaces kernels.hpp:220 launch_row_softmax_f32 (kernels/softmax.cu:177). */
+int mcke_sm100_softmax_f32(const float* x, float* y, int64_t rows, int64_t cols, int variant,
+                           mcke_stream_t stream);
+
+/* ---- reductions ---------------------------------------------------------- */
+
+/* Replaces kernels.hpp:198 row_reduce_workspace_bytes. */
+size_t mcke_sm100_reduce_row_workspace_bytes(int64_t rows, int64_t cols, int variant);
+/* Replaces kernels.hpp:204/209 launch_row_reduce_f32 (both overloads; pass
+ * workspace = NULL, workspace_bytes = 0 for the 7-argument form, which makes
+ * MCKE_REDUCE_TWO_PASS return MCKE_UNIMPLEMENTED as the reference does). */
+int mcke_sm100_reduce_row_f32(const float* x, float* out, int64_t rows, int64_t cols, int kind,
+                              int variant, void* workspace, size_t workspace_bytes,
+                              mcke_stream_t stream);
+
+/* Full-vector reduce (new; the reference's nearest interface is the rows = 1
+ * case of kernels.hpp:209).  Workspace size for n elements. */
+size_t mcke_sm100_reduce_full_workspace_bytes(int64_t n);
+/* sum, max and argmax of x[0..n) in one read of x.  Deterministic: the combine
+ * order depends on n only. */
+int mcke_sm100_reduce_full_f32(const float* x, int64_t n, mcke_reduce_result* out,
+                               void* workspace, size_t workspace_bytes, mcke_stream_t stream);
+/* The same over one shard x[0..n) whose first element has global index
+ * index_base; writes one mcke_reduce_partial. */
+int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_base,
+                                       mcke_reduce_partial* out, void* workspace,
+                                       size_t workspace_bytes, mcke_stream_t stream);
+/* Combines `count` partials (device memory, shard order) into one result. */
+int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count,
+                              mcke_reduce_result* out, mcke_stream_t stream);
+
+/* ---- GEMM: C[M,N] = alpha * A[M,K] @ B[K,N] + beta * C, row-major -------- */
+
+/* Replaces kernels.hpp:265 launch_gemm_f32 (kernels/gemm.cu:829).  beta == 0
+ * never reads C; k == 0 writes beta * C.  variant: AUTO or SIMT. */
+int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int64_t n,
+                        int64_t k, float alpha, float beta, int variant, mcke_stream_t stream);
+/* New: bf16 inputs (raw 16-bit patterns), float32 accumulation and output. */
+int mcke_sm100_gemm_bf16(const uint16_t* a, const uint16_t* b, float* c, int64_t m, int64_t n,
+                         int64_t k, float alpha, float beta, int variant, mcke_stream_t stream);
+/* New: bf16 GEMM with a fused epilogue, c = act(alpha * A@B + beta * C + bias[col]),
+ * c of type c_dtype (float32, or bfloat16 rounded once).  bias may be NULL;
+ * beta must be 0 for a bf16 output. */
+int mcke_sm100_gemm_bf16_ex(const uint16_t* a, const uint16_t* b, void* c, int c_dtype,
+                            int64_t m, int64_t n, int64_t k, float alpha, float beta,
+                            const float* bias, int act, int variant, mcke_stream_t stream);
+/* Replaces kernels.hpp:301 gemm_kernel_attrs: attributes of the kernel that
+ * (variant, dtype) selects for a large aligned shape. */
+int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm_attrs* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MCKE_SM100_H_ */

@@ -1,0 +1,285 @@
+// bias_act.cu -- fused bias + activation, y[r][c] = act(x[r][c] + bias[c]).
+//
+// Replaces mini-cuda-kernel-engine kernels/bias_act.cu (launchers :269 :296
+// :307; validation :208).  One read of x, one write of y, bias read once per
+// thread: the op is HBM-bound, so the design is about bytes in flight.
+//
+// Layout: block = 256 threads over 256*VW consecutive columns (blockIdx.x),
+// each thread owning ROWS rows of that column strip per step (blockIdx.y,
+// grid-strided).  All ROWS loads of a step are issued before any arithmetic,
+// so a resident block keeps ROWS * 256 * 4*VW bytes in flight; the bias vector
+// is loaded once per thread for the whole kernel.  Loads bypass L1
+// (ld.global.nc.L1::no_allocate) and stores are evict-first (st.global.cs):
+// every byte is touched exactly once.
+#include "mcke_common.cuh"
+
+namespace mcke_sm100 {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kRows = 4;  // rows per thread per step
+
+template <int VW>
+struct Vec;
+template <>
+struct Vec<1> {
+  using T = float;
+  static __device__ __forceinline__ T load(const float* p) { return __ldg(p); }
+  static __device__ __forceinline__ void store(float* p, T v) { __stcs(p, v); }
+  template <class F>
+  static __device__ __forceinline__ T act_bias(T v, T b) { return F::apply(v + b); }
+  template <class F>
+  static __device__ __forceinline__ T act(T v) { return F::apply(v); }
+};
+template <>
+struct Vec<2> {
+  using T = float2;
+  static __device__ __forceinline__ T load(const float* p) {
+    return __ldg(reinterpret_cast<const float2*>(p));
+  }
+  static __device__ __forceinline__ void store(float* p, T v) {
+    __stcs(reinterpret_cast<float2*>(p), v);
+  }
+  template <class F>
+  static __device__ __forceinline__ T act_bias(T v, T b) {
+    return make_float2(F::apply(v.x + b.x), F::apply(v.y + b.y));
+  }
+  template <class F>
+  static __device__ __forceinline__ T act(T v) { return make_float2(F::apply(v.x), F::apply(v.y)); }
+};
+template <>
+struct Vec<4> {
+  using T = float4;
+  static __device__ __forceinline__ T load(const float* p) { return ld_stream_f4(p); }
+  static __device__ __forceinline__ void store(float* p, T v) { st_stream_f4(p, v); }
+  template <class F>
+  static __device__ __forceinline__ T act_bias(T v, T b) {
+    return make_float4(F::apply(v.x + b.x), F::apply(v.y + b.y), F::apply(v.z + b.z),
+                       F::apply(v.w + b.w));
+  }
+  template <class F>
+  static __device__ __forceinline__ T act(T v) { return apply4<F>(v); }
+};
+
+template <int VW, class F>
+__global__ void __launch_bounds__(kThreads) bias_act_f32_kernel(const float* __restrict__ x,
+                                                                const float* __restrict__ bias,
+                                                                float* __restrict__ y,
+                                                                int64_t rows, int64_t cols) {
+  using V = Vec<VW>;
+  const int64_t col = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * VW;
+  if (col >= cols) return;
+  const typename V::T b = V::load(bias + col);
+  const int64_t step = static_cast<int64_t>(gridDim.y) * kRows;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRows; r0 < rows; r0 += step) {
+    typename V::T v[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (r0 + i < rows) v[i] = V::load(x + (r0 + i) * cols + col);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (r0 + i < rows) V::store(y + (r0 + i) * cols + col, V::template act_bias<F>(v[i], b));
+  }
+}
+
+// Activation only (the unfused half): flat grid-stride over n / VW vectors.
+template <int VW, class F>
+__global__ void __launch_bounds__(kThreads) activation_f32_kernel(const float* __restrict__ x,
+                                                                  float* __restrict__ y,
+                                                                  int64_t n) {
+  using V = Vec<VW>;
+  const int64_t nv = n / VW;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < nv; i += stride)
+    V::store(y + i * VW, V::template act<F>(V::load(x + i * VW)));
+}
+
+// bf16 x/y, float bias and math.  8 elements (16 bytes) per thread per row.
+template <class F>
+__global__ void __launch_bounds__(kThreads) bias_act_bf16x8_kernel(const uint16_t* __restrict__ x,
+                                                                   const float* __restrict__ bias,
+                                                                   uint16_t* __restrict__ y,
+                                                                   int64_t rows, int64_t cols) {
+  const int64_t col = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) * 8;
+  if (col >= cols) return;
+  float b[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) b[j] = __ldg(bias + col + j);
+  const int64_t step = static_cast<int64_t>(gridDim.y) * kRows;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRows; r0 < rows; r0 += step) {
+    uint4 v[kRows];
+#pragma unroll
+    for (int i = 0; i < kRows; ++i)
+      if (r0 + i < rows) v[i] = ld_stream_u4(x + (r0 + i) * cols + col);
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      if (r0 + i >= rows) continue;
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = pack_bf16x2(F::apply(bf16_lo(w[j]) + b[2 * j]), F::apply(bf16_hi(w[j]) + b[2 * j + 1]));
+      st_stream_u4(y + (r0 + i) * cols + col, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+  }
+}
+
+// Any shape: one element per thread, grid-stride over rows*cols.
+template <class F>
+__global__ void __launch_bounds__(kThreads) bias_act_bf16_scalar_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ bias, uint16_t* __restrict__ y,
+    int64_t rows, int64_t cols) {
+  const int64_t n = rows * cols;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride)
+    y[i] = to_bf16(F::apply(from_bf16(x[i]) + bias[i % cols]));
+}
+
+int validate_2d(const char* who, const void* x, const void* y, int64_t rows, int64_t cols, int vw) {
+  if (!x || !y) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (rows < 0 || cols < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (vw != 1 && vw != 2 && vw != 4)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: vector_width must be 1, 2 or 4, got %d", who, vw);
+  if (cols % vw != 0)
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: cols (%lld) must be a multiple of vector_width (%d); the launcher refuses "
+                "rather than silently running narrower",
+                who, static_cast<long long>(cols), vw);
+  const std::size_t a = sizeof(float) * static_cast<std::size_t>(vw);
+  if (!aligned(x, a) || !aligned(y, a))
+    return fail(MCKE_INVALID_ARGUMENT, "%s: pointer not %zu-byte aligned", who, a);
+  return MCKE_OK;
+}
+
+// Grid: columns across blockIdx.x; row steps across blockIdx.y, at most enough
+// blocks for ~8 resident per SM x 8 waves, at most 65535, at least 1.
+dim3 grid_2d(int64_t rows, int64_t cols_vec, int max_row_blocks) {
+  const int64_t gx = (cols_vec + kThreads - 1) / kThreads;
+  int64_t gy = (rows + kRows - 1) / kRows;
+  const int64_t cap = (static_cast<int64_t>(sm_count()) * 64 + gx - 1) / (gx > 0 ? gx : 1);
+  if (gy > cap) gy = cap;
+  if (gy > 65535) gy = 65535;
+  if (max_row_blocks > 0 && gy > max_row_blocks) gy = max_row_blocks;
+  if (gy < 1) gy = 1;
+  return dim3(static_cast<unsigned>(gx > 0 ? gx : 1), static_cast<unsigned>(gy), 1u);
+}
+
+template <int VW>
+void launch_bias_act(int act, dim3 g, cudaStream_t s, const float* x, const float* b, float* y,
+                     int64_t rows, int64_t cols) {
+  switch (act) {
+    case MCKE_ACT_RELU: bias_act_f32_kernel<VW, ActRelu><<<g, kThreads, 0, s>>>(x, b, y, rows, cols); break;
+    case MCKE_ACT_GELU_ERF: bias_act_f32_kernel<VW, ActGeluErf><<<g, kThreads, 0, s>>>(x, b, y, rows, cols); break;
+    case MCKE_ACT_GELU_TANH: bias_act_f32_kernel<VW, ActGeluTanh><<<g, kThreads, 0, s>>>(x, b, y, rows, cols); break;
+    default: bias_act_f32_kernel<VW, ActNone><<<g, kThreads, 0, s>>>(x, b, y, rows, cols); break;
+  }
+}
+
+bool act_ok(int act) { return act >= MCKE_ACT_NONE && act <= MCKE_ACT_GELU_TANH; }
+
+}  // namespace
+}  // namespace mcke_sm100
+
+using namespace mcke_sm100;
+
+extern "C" int mcke_sm100_bias_act_f32(const float* x, const float* bias, float* y, int64_t rows,
+                                       int64_t cols, int act, int vector_width,
+                                       int max_row_blocks, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_bias_act_f32";
+  clear_error();
+  if (rows == 0 || cols == 0) return MCKE_OK;
+  if (!bias) return fail(MCKE_INVALID_ARGUMENT, "%s: null bias", who);
+  MCKE_RETURN_IF(validate_2d(who, x, y, rows, cols, vector_width));
+  if (!aligned(bias, sizeof(float) * static_cast<std::size_t>(vector_width)))
+    return fail(MCKE_INVALID_ARGUMENT, "%s: bias pointer not aligned", who);
+  if (x == y) return fail(MCKE_INVALID_ARGUMENT, "%s: in-place (x == y) is not supported", who);
+  if (!act_ok(act)) return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  const dim3 g = grid_2d(rows, cols / vector_width, max_row_blocks);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (vector_width) {
+    case 4: launch_bias_act<4>(act, g, s, x, bias, y, rows, cols); break;
+    case 2: launch_bias_act<2>(act, g, s, x, bias, y, rows, cols); break;
+    default: launch_bias_act<1>(act, g, s, x, bias, y, rows, cols); break;
+  }
+  return check_launch(who);
+}
+
+extern "C" int mcke_sm100_bias_add_f32(const float* x, const float* bias, float* y, int64_t rows,
+                                       int64_t cols, int vector_width, mcke_stream_t stream) {
+  return mcke_sm100_bias_act_f32(x, bias, y, rows, cols, MCKE_ACT_NONE, vector_width, 0, stream);
+}
+
+namespace mcke_sm100 {
+namespace {
+template <int VW>
+void launch_activation(int act, int blocks, cudaStream_t s, const float* x, float* y, int64_t n) {
+  switch (act) {
+    case MCKE_ACT_RELU: activation_f32_kernel<VW, ActRelu><<<blocks, kThreads, 0, s>>>(x, y, n); break;
+    case MCKE_ACT_GELU_ERF: activation_f32_kernel<VW, ActGeluErf><<<blocks, kThreads, 0, s>>>(x, y, n); break;
+    case MCKE_ACT_GELU_TANH: activation_f32_kernel<VW, ActGeluTanh><<<blocks, kThreads, 0, s>>>(x, y, n); break;
+    default: activation_f32_kernel<VW, ActNone><<<blocks, kThreads, 0, s>>>(x, y, n); break;
+  }
+}
+}  // namespace
+}  // namespace mcke_sm100
+
+extern "C" int mcke_sm100_activation_f32(const float* x, float* y, int64_t n, int act,
+                                         int vector_width, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_activation_f32";
+  clear_error();
+  if (n == 0) return MCKE_OK;
+  if (!x || !y) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (n < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (vector_width != 1 && vector_width != 2 && vector_width != 4)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: vector_width must be 1, 2 or 4", who);
+  if (n % vector_width != 0)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: n must be a multiple of vector_width", who);
+  const std::size_t a = sizeof(float) * static_cast<std::size_t>(vector_width);
+  if (!aligned(x, a) || !aligned(y, a)) return fail(MCKE_INVALID_ARGUMENT, "%s: pointer not aligned", who);
+  if (!act_ok(act)) return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  const int64_t nv = n / vector_width;
+  int64_t blocks = (nv + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (vector_width) {
+    case 4: launch_activation<4>(act, static_cast<int>(blocks), s, x, y, n); break;
+    case 2: launch_activation<2>(act, static_cast<int>(blocks), s, x, y, n); break;
+    default: launch_activation<1>(act, static_cast<int>(blocks), s, x, y, n); break;
+  }
+  return check_launch(who);
+}
+
+extern "C" int mcke_sm100_bias_act_bf16(const uint16_t* x, const float* bias, uint16_t* y,
+                                        int64_t rows, int64_t cols, int act,
+                                        mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_bias_act_bf16";
+  clear_error();
+  if (rows == 0 || cols == 0) return MCKE_OK;
+  if (!x || !y || !bias) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (rows < 0 || cols < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (x == y) return fail(MCKE_INVALID_ARGUMENT, "%s: in-place (x == y) is not supported", who);
+  if (!act_ok(act)) return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cols % 8 == 0 && aligned(x, 16) && aligned(y, 16)) {
+    const dim3 g = grid_2d(rows, cols / 8, 0);
+    switch (act) {
+      case MCKE_ACT_RELU: bias_act_bf16x8_kernel<ActRelu><<<g, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      case MCKE_ACT_GELU_ERF: bias_act_bf16x8_kernel<ActGeluErf><<<g, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      case MCKE_ACT_GELU_TANH: bias_act_bf16x8_kernel<ActGeluTanh><<<g, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      default: bias_act_bf16x8_kernel<ActNone><<<g, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+    }
+  } else {
+    int64_t blocks = (rows * cols + kThreads - 1) / kThreads;
+    const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+    if (blocks > cap) blocks = cap;
+    const unsigned gb = static_cast<unsigned>(blocks);
+    switch (act) {
+      case MCKE_ACT_RELU: bias_act_bf16_scalar_kernel<ActRelu><<<gb, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      case MCKE_ACT_GELU_ERF: bias_act_bf16_scalar_kernel<ActGeluErf><<<gb, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      case MCKE_ACT_GELU_TANH: bias_act_bf16_scalar_kernel<ActGeluTanh><<<gb, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+      default: bias_act_bf16_scalar_kernel<ActNone><<<gb, kThreads, 0, s>>>(x, bias, y, rows, cols); break;
+    }
+  }
+  return check_launch(who);
+}

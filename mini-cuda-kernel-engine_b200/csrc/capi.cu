@@ -1,0 +1,173 @@
+// capi.cu -- library-wide entry points of libmcke_sm100a.so and the GEMM
+// front door (validation + kernel selection).  The GEMM launchers mirror
+// mini-cuda-kernel-engine kernels/gemm.cu:829 launch_gemm_f32: empty M or N is
+// OK without a launch, k == 0 is a legal GEMM (C = beta * C), negative
+// extents, nulls and an output aliasing an input are rejected.
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemm_epilogue.cuh"
+
+namespace mcke_sm100 {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int read_tc_watchdog(uint32_t* site);
+
+namespace {
+
+int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m, int64_t n,
+               int64_t k, bool bf16_in, int c_dtype, float alpha, float beta, const float* bias,
+               int act, int variant, mcke_stream_t stream) {
+  clear_error();
+  if (m < 0 || n < 0 || k < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (m == 0 || n == 0) return MCKE_OK;
+  if (!a || !b || !c) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (a == c || b == c)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: output aliases an input, which violates the __restrict__ contract", who);
+  if (m > 2147483647LL || n > 2147483647LL || k > 2147483647LL)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: extent exceeds INT32_MAX", who);
+  if (c_dtype != MCKE_DTYPE_F32 && c_dtype != MCKE_DTYPE_BF16)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown output dtype %d", who, c_dtype);
+  const bool out_bf16 = (c_dtype == MCKE_DTYPE_BF16);
+  if (out_bf16 && beta != 0.0f)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: beta must be 0 for a bf16 output", who);
+  if (act < MCKE_ACT_NONE || act > MCKE_ACT_GELU_TANH)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  if (variant != MCKE_GEMM_AUTO && variant != MCKE_GEMM_SIMT && variant != MCKE_GEMM_TCGEN05)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
+  if (!bf16_in && variant == MCKE_GEMM_TCGEN05)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands; no fallback is applied", who);
+
+  EpilogueParams ep;
+  ep.alpha = alpha;
+  ep.beta = beta;
+  ep.bias = bias;
+  ep.act = act;
+  ep.out_bf16 = out_bf16 ? 1 : 0;
+  ep.vec_ok = (n % 4 == 0) && aligned(c, out_bf16 ? 8 : 16) ? 1 : 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  const bool tc_ok = bf16_in && tcgen05_shape_ok(a, b, c, m, n, k, out_bf16);
+  if (variant == MCKE_GEMM_TCGEN05 && !tc_ok)
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: the tcgen05 kernel needs k > 0, K %% 8 == 0, N %% 8 == 0 and 16-byte aligned "
+                "A and B (TMA); no fallback is applied",
+                who);
+  if (tc_ok && variant != MCKE_GEMM_SIMT) {
+    MCKE_RETURN_IF(launch_gemm_tcgen05(static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b),
+                                       c, m, n, k, ep, s, nullptr, nullptr));
+  } else {
+    MCKE_RETURN_IF(launch_gemm_simt(a, b, c, m, n, k, bf16_in, ep, s, nullptr));
+  }
+  return check_launch(who);
+}
+
+}  // namespace
+}  // namespace mcke_sm100
+
+using namespace mcke_sm100;
+
+extern "C" int mcke_sm100_version(void) { return 100; }
+
+extern "C" const char* mcke_sm100_last_error_string(void) { return g_last_error.c_str(); }
+
+extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
+  clear_error();
+  const cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "check_device_errors: %s", cudaGetErrorString(e));
+  uint32_t site = 0;
+  MCKE_RETURN_IF(read_tc_watchdog(&site));
+  if (site != 0)
+    return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u); the kernel stopped early",
+                site);
+  return MCKE_OK;
+}
+
+extern "C" int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int64_t n,
+                                   int64_t k, float alpha, float beta, int variant,
+                                   mcke_stream_t stream) {
+  return gemm_front("mcke_sm100_gemm_f32", a, b, c, m, n, k, false, MCKE_DTYPE_F32, alpha, beta,
+                    nullptr, MCKE_ACT_NONE, variant, stream);
+}
+
+extern "C" int mcke_sm100_gemm_bf16(const uint16_t* a, const uint16_t* b, float* c, int64_t m,
+                                    int64_t n, int64_t k, float alpha, float beta, int variant,
+                                    mcke_stream_t stream) {
+  return gemm_front("mcke_sm100_gemm_bf16", a, b, c, m, n, k, true, MCKE_DTYPE_F32, alpha, beta,
+                    nullptr, MCKE_ACT_NONE, variant, stream);
+}
+
+extern "C" int mcke_sm100_gemm_bf16_ex(const uint16_t* a, const uint16_t* b, void* c, int c_dtype,
+                                       int64_t m, int64_t n, int64_t k, float alpha, float beta,
+                                       const float* bias, int act, int variant,
+                                       mcke_stream_t stream) {
+  return gemm_front("mcke_sm100_gemm_bf16_ex", a, b, c, m, n, k, true, c_dtype, alpha, beta, bias,
+                    act, variant, stream);
+}
+
+extern "C" int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm_attrs* out) {
+  static const char* who = "mcke_sm100_gemm_kernel_attrs";
+  clear_error();
+  if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
+  if (in_dtype != MCKE_DTYPE_F32 && in_dtype != MCKE_DTYPE_BF16)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown dtype %d", who, in_dtype);
+  const bool bf16 = (in_dtype == MCKE_DTYPE_BF16);
+  const void* kernel = nullptr;
+  std::size_t dyn = 0;
+  int threads = 0;
+  EpilogueParams ep{1.0f, 0.0f, nullptr, 0, 0, 1};
+  if (bf16 && variant != MCKE_GEMM_SIMT) {
+    launch_gemm_tcgen05(nullptr, nullptr, nullptr, 0, 0, 0, ep, nullptr, &kernel, &dyn);
+    threads = 192;
+  } else if (variant == MCKE_GEMM_TCGEN05) {
+    return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands", who);
+  } else {
+    // Aligned operands select the float4 instantiation for f32.
+    alignas(16) static float dummy[4];
+    launch_gemm_simt(dummy, dummy, nullptr, 0, 0, 4, bf16, ep, nullptr, &kernel);
+    threads = 256;
+  }
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
+  out->regs_per_thread = fa.numRegs;
+  out->static_smem_bytes = fa.sharedSizeBytes;
+  out->dynamic_smem_bytes = dyn;
+  out->local_bytes = fa.localSizeBytes;
+  out->threads_per_block = threads;
+  if (dyn > 0) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn));
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&out->max_blocks_per_sm_api, kernel, threads, dyn);
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
+  return MCKE_OK;
+}

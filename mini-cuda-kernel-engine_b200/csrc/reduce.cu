@@ -1,0 +1,402 @@
+// reduce.cu -- full-vector sum/max/argmax and row-wise sum/max/mean.
+//
+// Replaces mini-cuda-kernel-engine kernels/reduce.cu (launchers :224 and :285,
+// row_reduce_workspace_bytes :213, two_pass_split :65) and the primitives of
+// kernels/reduce_ops.cuh (SumOp/MaxOp :38-53, warp_reduce :83, block_reduce
+// :103).  Both reductions read their input once with 128-bit streaming loads.
+//
+// Numerics.  The reference's CPU oracle accumulates sums serially in double and
+// rounds once (tests/reference.hpp:154-172); these kernels also accumulate in
+// double -- each thread over its own elements, then a fixed-shape combine tree
+// -- and round once, so the float result is the oracle's unless the two double
+// sums straddle a float rounding boundary.  The combine tree depends only on
+// the extents (never on the device or on timing), so results are bitwise
+// reproducible run to run.  Max is the std::max fold of the oracle: NaN never
+// replaces the running maximum, the identity is -inf.  Argmax is the lowest
+// index holding the maximum; each thread visits its elements in increasing
+// index order and the combine breaks value ties by index.
+#include <cfloat>
+
+#include "mcke_common.cuh"
+
+namespace mcke_sm100 {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;
+// Pass-1 grid cap: 8 resident 256-thread blocks on each of a B200's 148 SMs.
+// A constant, not a device query, so the combine tree (and therefore every
+// bit of the sum) is the same on any GPU.
+constexpr int64_t kMaxBlocks = 8 * 148;
+
+struct Part {
+  double s;
+  float m;
+  int32_t reserved;
+  long long i;
+};
+static_assert(sizeof(Part) == sizeof(mcke_reduce_partial), "partial layout");
+
+__device__ __forceinline__ Part part_identity() { return Part{0.0, -INFINITY, 0, -1}; }
+
+__device__ __forceinline__ void part_add(Part& p, float v, long long idx) {
+  p.s += static_cast<double>(v);
+  if (v > p.m || (p.i < 0 && v == p.m)) {
+    p.m = v;
+    p.i = idx;
+  }
+}
+
+__device__ __forceinline__ Part part_combine(const Part& a, const Part& b) {
+  Part r;
+  r.s = a.s + b.s;
+  r.reserved = 0;
+  const bool take_b = (b.i >= 0) && (a.i < 0 || b.m > a.m || (b.m == a.m && b.i < a.i));
+  r.m = take_b ? b.m : a.m;
+  r.i = take_b ? b.i : a.i;
+  return r;
+}
+
+__device__ __forceinline__ Part part_shfl_xor(const Part& p, int o) {
+  Part q;
+  q.s = __shfl_xor_sync(0xffffffffu, p.s, o);
+  q.m = __shfl_xor_sync(0xffffffffu, p.m, o);
+  q.i = __shfl_xor_sync(0xffffffffu, p.i, o);
+  q.reserved = 0;
+  return q;
+}
+
+// Fixed-shape block combine: xor butterfly in each warp (every lane ends with
+// the same bits), then warp 0 folds the kWarps warp results in warp order.
+__device__ __forceinline__ Part block_combine(Part p, Part* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) p = part_combine(p, part_shfl_xor(p, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = p;
+  __syncthreads();
+  Part t = red[0];
+  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) t = part_combine(t, red[w]);
+  return t;
+}
+
+int64_t full_blocks(int64_t n) {
+  const int64_t per_block = static_cast<int64_t>(kThreads) * kUnroll * 4;
+  int64_t g = (n + per_block - 1) / per_block;
+  if (g > kMaxBlocks) g = kMaxBlocks;
+  return g < 1 ? 1 : g;
+}
+
+// Pass 1: each block writes one Part for its grid-strided share of x.
+// Elements before the first 16-byte boundary and after the last whole float4
+// go to global thread 0 (head first, tail last), keeping its visit order
+// increasing.
+__global__ void __launch_bounds__(kThreads) reduce_full_pass1_kernel(const float* __restrict__ x,
+                                                                     int64_t n, int64_t head,
+                                                                     long long base,
+                                                                     Part* __restrict__ parts) {
+  __shared__ Part red[kWarps];
+  Part p = part_identity();
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
+  if (tid == 0)
+    for (int64_t i = 0; i < head; ++i) part_add(p, x[i], base + i);
+  const float* xa = x + head;
+  const int64_t nv = (n - head) / 4;
+  for (int64_t v0 = tid; v0 < nv; v0 += nthreads * kUnroll) {
+    float4 q[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + u * nthreads;
+      if (v < nv) q[u] = ld_stream_f4(xa + 4 * v);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + u * nthreads;
+      if (v < nv) {
+        const long long g = base + head + 4 * v;
+        part_add(p, q[u].x, g);
+        part_add(p, q[u].y, g + 1);
+        part_add(p, q[u].z, g + 2);
+        part_add(p, q[u].w, g + 3);
+      }
+    }
+  }
+  if (tid == 0)
+    for (int64_t i = head + 4 * nv; i < n; ++i) part_add(p, x[i], base + i);
+  p = block_combine(p, red);
+  if (threadIdx.x == 0) parts[blockIdx.x] = p;
+}
+
+// Pass 2 (and the cross-shard combine): one block folds `count` Parts in a
+// fixed order and writes either a final result or one Part.
+template <bool kFinal>
+__global__ void __launch_bounds__(1024) reduce_full_combine_kernel(const Part* __restrict__ parts,
+                                                                   int64_t count, void* out) {
+  __shared__ Part red[32];
+  Part p = part_identity();
+  for (int64_t j = threadIdx.x; j < count; j += blockDim.x) p = part_combine(p, parts[j]);
+  p = block_combine(p, red);
+  if (threadIdx.x == 0) {
+    if (kFinal) {
+      mcke_reduce_result r;
+      r.sum = static_cast<float>(p.s);
+      r.max = p.m;
+      r.argmax = p.i;
+      *static_cast<mcke_reduce_result*>(out) = r;
+    } else {
+      *static_cast<Part*>(out) = p;
+    }
+  }
+}
+
+// ---- row reduce ----------------------------------------------------------
+
+// One warp per row.  Sum/mean accumulate in double, max is the std::max fold.
+template <bool kMax, bool kVec>
+__global__ void __launch_bounds__(kThreads) row_reduce_warp_kernel(const float* __restrict__ x,
+                                                                   float* __restrict__ out,
+                                                                   int64_t rows, int64_t cols,
+                                                                   double divisor) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  double s = 0.0;
+  float m = -INFINITY;
+  if (kVec) {
+    const int64_t nv = cols / 4;
+    for (int64_t v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+      float4 q[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (v0 + 32 * u < nv) q[u] = ld_stream_f4(xr + 4 * (v0 + 32 * u));
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (v0 + 32 * u >= nv) continue;
+        if (kMax) {
+          m = (m < q[u].x) ? q[u].x : m;
+          m = (m < q[u].y) ? q[u].y : m;
+          m = (m < q[u].z) ? q[u].z : m;
+          m = (m < q[u].w) ? q[u].w : m;
+        } else {
+          s += static_cast<double>(q[u].x);
+          s += static_cast<double>(q[u].y);
+          s += static_cast<double>(q[u].z);
+          s += static_cast<double>(q[u].w);
+        }
+      }
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float v = xr[c];
+      if (kMax) m = (m < v) ? v : m;
+      else s += static_cast<double>(v);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    if (kMax) {
+      const float t = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (m < t) ? t : m;
+    } else {
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+  }
+  if (lane == 0) out[row] = kMax ? m : static_cast<float>(s / divisor);
+}
+
+// Two-pass for few long rows: pass 1 splits each row over `split` blocks and
+// stores one double per (row, segment); pass 2 folds a row's segments in order.
+template <bool kMax>
+__global__ void __launch_bounds__(kThreads) row_reduce_split_kernel(const float* __restrict__ x,
+                                                                    double* __restrict__ ws,
+                                                                    int64_t cols, int64_t split) {
+  __shared__ double red[kWarps];
+  const int64_t row = blockIdx.y;
+  const int64_t seg = blockIdx.x;
+  const int64_t len = (cols + split - 1) / split;
+  const int64_t c0 = seg * len;
+  const int64_t c1 = (c0 + len < cols) ? c0 + len : cols;
+  const float* xr = x + row * cols;
+  double s = 0.0;
+  float m = -INFINITY;
+  for (int64_t c = c0 + threadIdx.x; c < c1; c += kThreads) {
+    const float v = xr[c];
+    if (kMax) m = (m < v) ? v : m;
+    else s += static_cast<double>(v);
+  }
+  double a = kMax ? static_cast<double>(m) : s;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double t = __shfl_xor_sync(0xffffffffu, a, o);
+    a = kMax ? ((a < t) ? t : a) : a + t;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = red[0];
+    for (int w = 1; w < kWarps; ++w) t = kMax ? ((t < red[w]) ? red[w] : t) : t + red[w];
+    ws[row * split + seg] = t;
+  }
+}
+
+template <bool kMax>
+__global__ void __launch_bounds__(kThreads) row_reduce_fold_kernel(const double* __restrict__ ws,
+                                                                   float* __restrict__ out,
+                                                                   int64_t rows, int64_t split,
+                                                                   double divisor) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (row >= rows) return;
+  double t = kMax ? -INFINITY : 0.0;
+  for (int64_t j = 0; j < split; ++j) {
+    const double v = ws[row * split + j];
+    t = kMax ? ((t < v) ? v : t) : t + v;
+  }
+  out[row] = kMax ? static_cast<float>(t) : static_cast<float>(t / divisor);
+}
+
+// Segments per row for the two-pass path: enough blocks to fill the machine
+// (the reference's rule, kernels/reduce.cu:60-72, retargeted to 8 x 148), at
+// most 64, and never segments shorter than one block's width.
+int64_t two_pass_split(int64_t rows, int64_t cols) {
+  if (rows <= 0) return 1;
+  int64_t s = (kMaxBlocks + rows - 1) / rows;
+  if (s > 64) s = 64;
+  const int64_t by_len = (cols + kThreads - 1) / kThreads;
+  if (s > by_len) s = by_len;
+  return s < 1 ? 1 : s;
+}
+
+}  // namespace
+}  // namespace mcke_sm100
+
+using namespace mcke_sm100;
+
+extern "C" size_t mcke_sm100_reduce_full_workspace_bytes(int64_t n) {
+  if (n <= 0) return 0;
+  return static_cast<size_t>(full_blocks(n)) * sizeof(Part);
+}
+
+namespace {
+int full_common(const char* who, const float* x, int64_t n, int64_t index_base, void* out,
+                void* workspace, size_t workspace_bytes, bool final_result, mcke_stream_t stream) {
+  if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
+  if (n < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (n > 0 && !x) return fail(MCKE_INVALID_ARGUMENT, "%s: null input", who);
+  if (index_base < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative index_base", who);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    // The empty reduction still defines its output: sum 0, max -inf, argmax -1.
+    if (final_result) reduce_full_combine_kernel<true><<<1, 32, 0, s>>>(nullptr, 0, out);
+    else reduce_full_combine_kernel<false><<<1, 32, 0, s>>>(nullptr, 0, out);
+    return check_launch(who);
+  }
+  if (!aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
+  const size_t need = mcke_sm100_reduce_full_workspace_bytes(n);
+  if (!workspace || workspace_bytes < need)
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: needs %zu bytes of workspace (got %zu); query "
+                "mcke_sm100_reduce_full_workspace_bytes() first",
+                who, need, workspace_bytes);
+  if (!aligned(workspace, 16)) return fail(MCKE_INVALID_ARGUMENT, "%s: workspace not 16-byte aligned", who);
+  const int64_t g = full_blocks(n);
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+  int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
+  if (head > n) head = n;
+  Part* parts = static_cast<Part*>(workspace);
+  reduce_full_pass1_kernel<<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, index_base, parts);
+  MCKE_RETURN_IF(check_launch(who));
+  if (final_result) reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
+  else reduce_full_combine_kernel<false><<<1, 1024, 0, s>>>(parts, g, out);
+  return check_launch(who);
+}
+}  // namespace
+
+extern "C" int mcke_sm100_reduce_full_f32(const float* x, int64_t n, mcke_reduce_result* out,
+                                          void* workspace, size_t workspace_bytes,
+                                          mcke_stream_t stream) {
+  clear_error();
+  return full_common("mcke_sm100_reduce_full_f32", x, n, 0, out, workspace, workspace_bytes, true,
+                     stream);
+}
+
+extern "C" int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_base,
+                                                  mcke_reduce_partial* out, void* workspace,
+                                                  size_t workspace_bytes, mcke_stream_t stream) {
+  clear_error();
+  return full_common("mcke_sm100_reduce_full_partial_f32", x, n, index_base, out, workspace,
+                     workspace_bytes, false, stream);
+}
+
+extern "C" int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count,
+                                         mcke_reduce_result* out, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_combine";
+  clear_error();
+  if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
+  if (count < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative count", who);
+  if (count > 0 && !partials) return fail(MCKE_INVALID_ARGUMENT, "%s: null partials", who);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(reinterpret_cast<const Part*>(partials), count,
+                                                      out);
+  return check_launch(who);
+}
+
+extern "C" size_t mcke_sm100_reduce_row_workspace_bytes(int64_t rows, int64_t cols, int variant) {
+  if (variant != MCKE_REDUCE_TWO_PASS || rows <= 0 || cols <= 0) return 0;
+  return static_cast<size_t>(rows * two_pass_split(rows, cols)) * sizeof(double);
+}
+
+extern "C" int mcke_sm100_reduce_row_f32(const float* x, float* out, int64_t rows, int64_t cols,
+                                         int kind, int variant, void* workspace,
+                                         size_t workspace_bytes, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_row_f32";
+  clear_error();
+  if (rows == 0 || cols == 0) return MCKE_OK;
+  if (rows < 0 || cols < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (!x || !out) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (kind < MCKE_REDUCE_SUM || kind > MCKE_REDUCE_MEAN)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown kind %d", who, kind);
+  if (variant < MCKE_REDUCE_SMEM_TREE || variant > MCKE_REDUCE_TWO_PASS)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
+  if (rows > 2147483647LL) return fail(MCKE_INVALID_ARGUMENT, "%s: rows exceeds the grid limit", who);
+  const bool is_max = (kind == MCKE_REDUCE_MAX);
+  const double divisor = (kind == MCKE_REDUCE_MEAN) ? static_cast<double>(cols) : 1.0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (variant == MCKE_REDUCE_TWO_PASS) {
+    if (workspace == nullptr && workspace_bytes == 0)
+      return fail(MCKE_UNIMPLEMENTED,
+                  "%s: the two-pass variant needs a workspace; query "
+                  "mcke_sm100_reduce_row_workspace_bytes() and pass one",
+                  who);
+    const size_t need = mcke_sm100_reduce_row_workspace_bytes(rows, cols, variant);
+    if (!workspace || workspace_bytes < need)
+      return fail(MCKE_INVALID_ARGUMENT, "%s: two-pass needs %zu bytes of workspace (got %zu)", who,
+                  need, workspace_bytes);
+    if (!aligned(workspace, 8)) return fail(MCKE_INVALID_ARGUMENT, "%s: workspace not 8-byte aligned", who);
+    if (rows > 65535) return fail(MCKE_INVALID_ARGUMENT, "%s: two-pass supports at most 65535 rows", who);
+    const int64_t split = two_pass_split(rows, cols);
+    double* ws = static_cast<double*>(workspace);
+    const dim3 g1(static_cast<unsigned>(split), static_cast<unsigned>(rows), 1u);
+    const unsigned g2 = static_cast<unsigned>((rows + kThreads - 1) / kThreads);
+    if (is_max) {
+      row_reduce_split_kernel<true><<<g1, kThreads, 0, s>>>(x, ws, cols, split);
+      MCKE_RETURN_IF(check_launch(who));
+      row_reduce_fold_kernel<true><<<g2, kThreads, 0, s>>>(ws, out, rows, split, divisor);
+    } else {
+      row_reduce_split_kernel<false><<<g1, kThreads, 0, s>>>(x, ws, cols, split);
+      MCKE_RETURN_IF(check_launch(who));
+      row_reduce_fold_kernel<false><<<g2, kThreads, 0, s>>>(ws, out, rows, split, divisor);
+    }
+    return check_launch(who);
+  }
+  const bool vec = (cols % 4 == 0) && aligned(x, 16);
+  const unsigned g = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
+  if (is_max) {
+    if (vec) row_reduce_warp_kernel<true, true><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+    else row_reduce_warp_kernel<true, false><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+  } else {
+    if (vec) row_reduce_warp_kernel<false, true><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+    else row_reduce_warp_kernel<false, false><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+  }
+  return check_launch(who);
+}

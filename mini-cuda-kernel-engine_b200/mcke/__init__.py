@@ -1,0 +1,290 @@
+"""Python binding of libmcke_sm100a.so (include/mcke_sm100.h) over ctypes.
+
+Tensors are torch CUDA tensors: torch supplies device memory and streams, the
+arithmetic is this library's CUDA kernels.  Every call enqueues on the current
+torch stream of the tensor's device (or an explicit ``stream``) and never
+synchronises.  A non-OK status raises :class:`MckeError` carrying the
+library's message.  There is no CPU or library fallback: if the shared
+library is missing the first call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import struct
+
+import torch
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libmcke_sm100a.so")
+HEADER = os.path.join(ROOT, "include", "mcke_sm100.h")
+
+OK, OUT_OF_MEMORY, INVALID_ARGUMENT, FAILED_PRECONDITION, UNIMPLEMENTED, INTERNAL, CUDA_ERROR = range(7)
+ACT = {"none": 0, "relu": 1, "gelu_erf": 2, "gelu_tanh": 3}
+REDUCE_KIND = {"sum": 0, "max": 1, "mean": 2}
+REDUCE_VARIANT = {"smem_tree": 0, "warp_shuffle": 1, "two_pass": 2}
+SOFTMAX_VARIANT = {"three_pass": 0, "online": 1}
+GEMM_VARIANT = {"auto": 0, "simt": 1, "tcgen05": 2}
+DTYPE = {"f32": 0, "bf16": 2}
+RESULT_BYTES = 16   # mcke_reduce_result
+PARTIAL_BYTES = 24  # mcke_reduce_partial
+
+
+class MckeError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[mcke status {code}] {message}")
+        self.code = code
+        self.message = message
+
+
+_lib = None
+
+
+def declared_symbols() -> list[str]:
+    """Every mcke_sm100_* function declared in include/mcke_sm100.h."""
+    with open(HEADER) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"\b(mcke_sm100_\w+)\s*\(", text)))
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is not built; run __graft_entry__.build() "
+                               "(there is no fallback path)")
+        l = ctypes.CDLL(LIB_PATH)
+        i64, i32, vp, f32, sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
+        sigs = {
+            "mcke_sm100_version": (i32, []),
+            "mcke_sm100_last_error_string": (ctypes.c_char_p, []),
+            "mcke_sm100_check_device_errors": (i32, [vp]),
+            "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
+            "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),
+            "mcke_sm100_activation_f32": (i32, [vp, vp, i64, i32, i32, vp]),
+            "mcke_sm100_bias_act_bf16": (i32, [vp, vp, vp, i64, i64, i32, vp]),
+            "mcke_sm100_softmax_f32": (i32, [vp, vp, i64, i64, i32, vp]),
+            "mcke_sm100_reduce_row_workspace_bytes": (sz, [i64, i64, i32]),
+            "mcke_sm100_reduce_row_f32": (i32, [vp, vp, i64, i64, i32, i32, vp, sz, vp]),
+            "mcke_sm100_reduce_full_workspace_bytes": (sz, [i64]),
+            "mcke_sm100_reduce_full_f32": (i32, [vp, i64, vp, vp, sz, vp]),
+            "mcke_sm100_reduce_full_partial_f32": (i32, [vp, i64, i64, vp, vp, sz, vp]),
+            "mcke_sm100_reduce_combine": (i32, [vp, i64, vp, vp]),
+            "mcke_sm100_gemm_f32": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
+            "mcke_sm100_gemm_bf16": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
+            "mcke_sm100_gemm_bf16_ex": (i32, [vp, vp, vp, i32, i64, i64, i64, f32, f32, vp, i32, i32, vp]),
+            "mcke_sm100_gemm_kernel_attrs": (i32, [i32, i32, vp]),
+        }
+        for name, (res, args) in sigs.items():
+            fn = getattr(l, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = l
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != OK:
+        raise MckeError(rc, lib().mcke_sm100_last_error_string().decode())
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(t: torch.Tensor | None, stream) -> int | None:
+    if stream is not None:
+        return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    dev = t.device if t is not None else torch.device("cuda")
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _need(t: torch.Tensor, dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _act(a) -> int:
+    return ACT[a] if isinstance(a, str) else int(a)
+
+
+# ---- bias + activation -------------------------------------------------------
+
+def bias_act(x, bias, act="gelu_tanh", vector_width: int = 4, out=None, max_row_blocks: int = 0,
+             stream=None):
+    """y = act(x + bias) over the last dim, x [rows, cols] float32 or bfloat16."""
+    rows, cols = (x.shape[0], x.shape[1]) if x.dim() == 2 else (x.numel() // x.shape[-1], x.shape[-1])
+    y = torch.empty_like(x) if out is None else out
+    _need(bias, torch.float32, "bias")
+    if x.dtype == torch.bfloat16:
+        _need(x, torch.bfloat16, "x"); _need(y, torch.bfloat16, "out")
+        _check(lib().mcke_sm100_bias_act_bf16(_ptr(x), _ptr(bias), _ptr(y), rows, cols, _act(act),
+                                              _stream(x, stream)))
+    else:
+        _need(x, torch.float32, "x"); _need(y, torch.float32, "out")
+        _check(lib().mcke_sm100_bias_act_f32(_ptr(x), _ptr(bias), _ptr(y), rows, cols, _act(act),
+                                             vector_width, max_row_blocks, _stream(x, stream)))
+    return y
+
+
+def bias_add(x, bias, vector_width: int = 4, out=None, stream=None):
+    rows, cols = x.shape
+    y = torch.empty_like(x) if out is None else out
+    _check(lib().mcke_sm100_bias_add_f32(_ptr(x), _ptr(bias), _ptr(y), rows, cols, vector_width,
+                                         _stream(x, stream)))
+    return y
+
+
+def activation(x, act="gelu_tanh", vector_width: int = 4, out=None, stream=None):
+    y = torch.empty_like(x) if out is None else out
+    _need(x, torch.float32, "x")
+    _check(lib().mcke_sm100_activation_f32(_ptr(x), _ptr(y), x.numel(), _act(act), vector_width,
+                                           _stream(x, stream)))
+    return y
+
+
+# ---- softmax -------------------------------------------------------------------
+
+def softmax(x, variant="online", out=None, stream=None):
+    _need(x, torch.float32, "x")
+    rows, cols = x.shape
+    y = torch.empty_like(x) if out is None else out
+    v = SOFTMAX_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    _check(lib().mcke_sm100_softmax_f32(_ptr(x), _ptr(y), rows, cols, v, _stream(x, stream)))
+    return y
+
+
+# ---- reductions ----------------------------------------------------------------
+
+def reduce_full_workspace_bytes(n: int) -> int:
+    return lib().mcke_sm100_reduce_full_workspace_bytes(n)
+
+
+def reduce_full(x, out=None, workspace=None, stream=None):
+    """sum/max/argmax of a float32 vector; returns a 16-byte uint8 device tensor
+    holding one mcke_reduce_result (decode with :func:`decode_result`)."""
+    _need(x, torch.float32, "x")
+    n = x.numel()
+    dev = x.device
+    if out is None:
+        out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=dev)
+    need = reduce_full_workspace_bytes(n)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
+    _check(lib().mcke_sm100_reduce_full_f32(_ptr(x), n, _ptr(out), _ptr(workspace),
+                                            workspace.numel(), _stream(x, stream)))
+    return out
+
+
+def reduce_full_partial(x, index_base: int, out=None, workspace=None, stream=None):
+    _need(x, torch.float32, "x")
+    n = x.numel()
+    if out is None:
+        out = torch.empty(PARTIAL_BYTES, dtype=torch.uint8, device=x.device)
+    need = reduce_full_workspace_bytes(n)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+    _check(lib().mcke_sm100_reduce_full_partial_f32(_ptr(x), n, index_base, _ptr(out),
+                                                    _ptr(workspace), workspace.numel(),
+                                                    _stream(x, stream)))
+    return out
+
+
+def reduce_combine(partials, count: int, out=None, stream=None):
+    if out is None:
+        out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=partials.device)
+    _check(lib().mcke_sm100_reduce_combine(_ptr(partials), count, _ptr(out), _stream(partials, stream)))
+    return out
+
+
+def decode_result(buf) -> tuple[float, float, int]:
+    """(sum, max, argmax) from an mcke_reduce_result (device or host bytes)."""
+    raw = bytes(buf.cpu().numpy().tobytes()) if hasattr(buf, "cpu") else bytes(buf)
+    s, m, i = struct.unpack("<ffq", raw[:16])
+    return s, m, i
+
+
+def decode_partial(buf) -> tuple[float, float, int]:
+    raw = bytes(buf.cpu().numpy().tobytes()) if hasattr(buf, "cpu") else bytes(buf)
+    s, m, _, i = struct.unpack("<dfiq", raw[:24])
+    return s, m, i
+
+
+def reduce_row_workspace_bytes(rows: int, cols: int, variant="warp_shuffle") -> int:
+    v = REDUCE_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    return lib().mcke_sm100_reduce_row_workspace_bytes(rows, cols, v)
+
+
+def reduce_row(x, kind="sum", variant="warp_shuffle", out=None, workspace=None, stream=None):
+    _need(x, torch.float32, "x")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.float32, device=x.device)
+    v = REDUCE_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    k = REDUCE_KIND[kind] if isinstance(kind, str) else int(kind)
+    if workspace is None and v == 2:
+        need = reduce_row_workspace_bytes(rows, cols, v)
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+    wsz = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check(lib().mcke_sm100_reduce_row_f32(_ptr(x), _ptr(out), rows, cols, k, v, _ptr(workspace),
+                                           wsz, _stream(x, stream)))
+    return out
+
+
+# ---- GEMM ------------------------------------------------------------------------
+
+def gemm(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, variant="auto", bias=None,
+         act="none", out_dtype=None, stream=None):
+    """C = act(alpha * A @ B + beta * C + bias); A, B float32 or bfloat16 (row-major)."""
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError("inner dimensions differ")
+    v = GEMM_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    s = _stream(a, stream)
+    if a.dtype == torch.float32:
+        _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
+        if bias is not None or _act(act) != 0:
+            raise ValueError("bias/activation epilogues are offered on the bf16 entry point")
+        if c is None:
+            c = torch.zeros((m, n), dtype=torch.float32, device=a.device)
+        _need(c, torch.float32, "c")
+        _check(lib().mcke_sm100_gemm_f32(_ptr(a), _ptr(b), _ptr(c), m, n, k, alpha, beta, v, s))
+        return c
+    _need(a, torch.bfloat16, "a"); _need(b, torch.bfloat16, "b")
+    odt = out_dtype or (c.dtype if c is not None else torch.float32)
+    if c is None:
+        c = torch.zeros((m, n), dtype=odt, device=a.device)
+    if bias is None and _act(act) == 0 and odt == torch.float32:
+        _check(lib().mcke_sm100_gemm_bf16(_ptr(a), _ptr(b), _ptr(c), m, n, k, alpha, beta, v, s))
+    else:
+        if bias is not None:
+            _need(bias, torch.float32, "bias")
+        _check(lib().mcke_sm100_gemm_bf16_ex(_ptr(a), _ptr(b), _ptr(c),
+                                             DTYPE["bf16" if odt == torch.bfloat16 else "f32"],
+                                             m, n, k, alpha, beta, _ptr(bias), _act(act), v, s))
+    return c
+
+
+class GemmAttrs(ctypes.Structure):
+    _fields_ = [("regs_per_thread", ctypes.c_int), ("static_smem_bytes", ctypes.c_size_t),
+                ("dynamic_smem_bytes", ctypes.c_size_t), ("local_bytes", ctypes.c_size_t),
+                ("threads_per_block", ctypes.c_int), ("max_blocks_per_sm_api", ctypes.c_int)]
+
+
+def gemm_kernel_attrs(variant="auto", dtype="bf16") -> dict:
+    out = GemmAttrs()
+    v = GEMM_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    _check(lib().mcke_sm100_gemm_kernel_attrs(v, DTYPE[dtype], ctypes.byref(out)))
+    return {f: getattr(out, f) for f, _ in GemmAttrs._fields_}
+
+
+def check_device_errors(stream=None) -> None:
+    _check(lib().mcke_sm100_check_device_errors(_stream(None, stream)))

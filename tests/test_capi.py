@@ -1,0 +1,70 @@
+"""The C-ABI library on the CPU: it loads, exports every symbol include/mcke_sm100.h
+declares, and rejects bad arguments before touching a device (no compute)."""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "mini-cuda-kernel-engine_b200")
+
+
+@pytest.fixture(scope="module")
+def mcke():
+    import mcke as m
+    if not os.path.exists(m.LIB_PATH):
+        subprocess.run([sys.executable, os.path.join(PKG, "build.py")], check=True)
+    return m
+
+
+def test_library_exports_every_declared_symbol(mcke):
+    names = mcke.declared_symbols()
+    assert len(names) >= 18
+    l = ctypes.CDLL(mcke.LIB_PATH)
+    missing = [n for n in names if not hasattr(l, n)]
+    assert not missing, missing
+    # and exports nothing under the prefix that the header does not declare
+    out = subprocess.run(["nm", "-D", "--defined-only", mcke.LIB_PATH], capture_output=True, text=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T mcke_sm100_" in ln}
+    assert exported == set(names)
+
+
+def test_argument_validation_needs_no_device(mcke):
+    l = mcke.lib()
+    assert l.mcke_sm100_version() >= 100
+    bogus = ctypes.c_void_p(0x1000)
+    # null pointer / negative extent / bad width / aliasing -> INVALID_ARGUMENT, with a message
+    assert l.mcke_sm100_bias_act_f32(None, bogus, bogus, 4, 4, 3, 4, 0, None) == mcke.INVALID_ARGUMENT
+    assert b"null" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_bias_act_f32(bogus, bogus, ctypes.c_void_p(0x2000), 4, 6, 3, 4, 0, None) == mcke.INVALID_ARGUMENT
+    assert b"multiple of vector_width" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_bias_act_f32(bogus, bogus, bogus, 4, 8, 3, 4, 0, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_softmax_f32(bogus, bogus, 4, 4, 1, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_softmax_f32(bogus, ctypes.c_void_p(0x2000), -1, 4, 1, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_gemm_f32(bogus, ctypes.c_void_p(0x2000), bogus, 4, 4, 4, 1.0, 0.0, 0, None) == mcke.INVALID_ARGUMENT
+    assert b"aliases" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_gemm_f32(bogus, bogus, ctypes.c_void_p(0x3000), 4, 4, 4, 1.0, 0.0, 2, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_gemm_bf16(bogus, ctypes.c_void_p(0x2000), ctypes.c_void_p(0x3000), 4, 5, 7, 1.0, 0.0, 2, None) == mcke.INVALID_ARGUMENT
+    assert b"no fallback" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_gemm_bf16_ex(bogus, ctypes.c_void_p(0x2000), ctypes.c_void_p(0x3000), 2, 8, 8, 8, 1.0, 1.0, None, 0, 0, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_reduce_row_f32(bogus, ctypes.c_void_p(0x2000), 4, 64, 0, 2, None, 0, None) == mcke.UNIMPLEMENTED
+    assert l.mcke_sm100_reduce_full_f32(bogus, 1000, ctypes.c_void_p(0x2000), None, 0, None) == mcke.INVALID_ARGUMENT
+    assert b"workspace" in l.mcke_sm100_last_error_string()
+    # empty extents are OK with no launch
+    assert l.mcke_sm100_softmax_f32(None, None, 0, 16, 1, None) == mcke.OK
+    assert l.mcke_sm100_bias_act_f32(None, None, None, 0, 0, 3, 4, 0, None) == mcke.OK
+    assert l.mcke_sm100_gemm_f32(None, None, None, 0, 4, 4, 1.0, 0.0, 0, None) == mcke.OK
+
+
+def test_workspace_queries(mcke):
+    l = mcke.lib()
+    assert l.mcke_sm100_reduce_full_workspace_bytes(0) == 0
+    assert l.mcke_sm100_reduce_full_workspace_bytes(1) == 24
+    # the combine grid is capped at 8 blocks x 148 SMs, whatever the device
+    assert l.mcke_sm100_reduce_full_workspace_bytes(1 << 28) == 8 * 148 * 24
+    assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 1) == 0
+    assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 2) == 64 * 19 * 8

@@ -1,0 +1,444 @@
+"""Parity of the sm_100a kernels with the CPU oracle (B200 only).
+
+Every test runs a CUDA kernel of libmcke_sm100a.so through its C-ABI (via the
+ctypes binding in mini-cuda-kernel-engine_b200/mcke) and compares with the
+oracle (oracle/, the restatement of the reference's tests/reference.hpp) on
+the same seeded inputs:
+
+* integer / index / max results: bit for bit;
+* float results: the reference's mixed tolerance |got - want| <= abs + rel*|want|
+  (tests/reference.hpp:249) with the tolerances written next to each check,
+  plus the max relative error over |want| above a stated floor.
+"""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover - CPU container
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import mcke  # noqa: E402
+
+DEV = torch.device("cuda:0")
+HEX = lambda h: np.array([int(t, 16) for t in h], dtype=np.uint32).view(np.float32)  # noqa: E731
+
+# Tolerances (north star: <=1e-5 relative for fp32 softmax and bias-GELU,
+# <=1e-4 for fp32 GEMM vs an fp64-accumulated reference, <=1e-2 for bf16 GEMM;
+# bit-exact for max/argmax).  Absolute floors are the reference's
+# (tests/reference.hpp:327-328, :370) for outputs that are near zero by chance.
+REL_ELEMWISE, ABS_ELEMWISE = 1e-5, 1e-6
+REL_SOFTMAX, ABS_SOFTMAX = 1e-5, 1e-8
+
+
+def dev(a, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dtype)
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def assert_close(got, want, rel, abs_, what="", floor=1e-3, max_rel=None):
+    r = oracle.compare(got, want, rel, abs_)
+    assert r["mismatches"] == 0 and not r["nan"] and not r["inf"], (what, r)
+    if max_rel is not None:
+        g = np.asarray(got, np.float64).ravel()
+        w = np.asarray(want, np.float64).ravel()
+        sel = np.abs(w) > floor
+        if sel.any():
+            worst = float(np.max(np.abs(g[sel] - w[sel]) / np.abs(w[sel])))
+            assert worst <= max_rel, (what, worst)
+
+
+@pytest.fixture(scope="module")
+def vectors():
+    with open(os.path.join(os.path.dirname(__file__), "golden", "reference_vectors.json")) as f:
+        return json.load(f)["cases"]
+
+
+@pytest.fixture(scope="module")
+def fixtures():
+    return dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_fixtures.npz")))
+
+
+# ---------------------------------------------------------------- bias + act
+
+def test_bias_act_golden_vectors(vectors):
+    for c in vectors:
+        if c["kind"] != "bias_act":
+            continue
+        rows, cols, act = c["ints"]["rows"], c["ints"]["cols"], c["ints"]["act"]
+        x = HEX(c["arrays"]["x"]).reshape(rows, cols)
+        b = HEX(c["arrays"]["bias"])
+        want = HEX(c["arrays"]["expect"]).reshape(rows, cols)
+        for vw in (1, 2):
+            got = host(mcke.bias_act(dev(x), dev(b), act, vector_width=vw))
+            # the reference's own bar for these vectors: 1e-6 rel, 1e-7 abs
+            assert_close(got, want, 1e-6, 1e-7, c["name"])
+
+
+def test_bias_act_reference_fixtures(fixtures):
+    x, b = fixtures["bias_act_x"], fixtures["bias_act_bias"]
+    for name in ("none", "relu", "gelu_erf", "gelu_tanh"):
+        for vw in (1, 2, 4):
+            got = host(mcke.bias_act(dev(x), dev(b), name, vector_width=vw))
+            assert_close(got, fixtures[f"bias_act_{name}"], REL_ELEMWISE, ABS_ELEMWISE, name,
+                         max_rel=REL_ELEMWISE)
+
+
+def test_bias_gelu_config1_shape_slice():
+    # Config 1 distribution (X ~ N(0,1), bias ~ U(-1,1)); 1024 of the 4096 rows.
+    x = oracle.fill_normal(1024 * 4096, 0).reshape(1024, 4096)
+    b = oracle.fill_random(4096, 1000)
+    want = oracle.bias_act(x, b, "gelu_tanh")
+    got = host(mcke.bias_act(dev(x), dev(b), "gelu_tanh"))
+    assert_close(got, want, REL_ELEMWISE, ABS_ELEMWISE, "config1", max_rel=REL_ELEMWISE)
+    # the starvation knob changes the launch geometry, never the result
+    got2 = host(mcke.bias_act(dev(x), dev(b), "gelu_tanh", max_row_blocks=7))
+    assert np.array_equal(got.view(np.uint32), got2.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,cols,vw", [(1, 1, 1), (3, 17, 1), (5, 6, 2), (70000, 4, 4), (9, 4100, 4)])
+def test_bias_act_odd_shapes(rows, cols, vw):
+    x = oracle.fill_random(rows * cols, 3, -5, 5).reshape(rows, cols)
+    b = oracle.fill_random(cols, 4)
+    for act in range(4):
+        got = host(mcke.bias_act(dev(x), dev(b), act, vector_width=vw))
+        assert_close(got, oracle.bias_act(x, b, act), REL_ELEMWISE, ABS_ELEMWISE, (rows, cols, act))
+
+
+def test_bias_add_and_activation_unfused():
+    x = oracle.fill_random(64 * 256, 5, -4, 4).reshape(64, 256)
+    b = oracle.fill_random(256, 6)
+    t = mcke.bias_add(dev(x), dev(b))
+    y = host(mcke.activation(t, "gelu_erf"))
+    want_add = oracle.bias_act(x, b, "none")
+    assert np.array_equal(host(t).view(np.uint32), want_add.view(np.uint32))  # one fp32 add: exact
+    assert_close(y, oracle.bias_act(want_add, np.zeros(256, np.float32), "gelu_erf"), REL_ELEMWISE,
+                 ABS_ELEMWISE)
+
+
+def test_bias_act_bf16():
+    rows, cols = 96, 1024
+    xb = oracle.to_bf16(oracle.fill_normal(rows * cols, 7).reshape(rows, cols))
+    b = oracle.fill_random(cols, 8)
+    xt = torch.from_numpy(xb.view(np.int16)).to(DEV).view(torch.bfloat16)
+    for act in ("gelu_tanh", "relu", "none"):
+        got = host(mcke.bias_act(xt, dev(b), act).view(torch.int16)).view(np.uint16)
+        want = oracle.to_bf16(oracle.bias_act(oracle.bf16_to_f32(xb), b, act))
+        # one rounding to bf16 from a float that may differ by a few ulp: at most 1 bf16 ulp
+        diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        assert diff.max() <= 1, act
+        assert (diff == 0).mean() > 0.99
+    # scalar path (cols % 8 != 0)
+    xb2 = oracle.to_bf16(oracle.fill_normal(7 * 13, 9).reshape(7, 13))
+    b2 = oracle.fill_random(13, 10)
+    xt2 = torch.from_numpy(xb2.view(np.int16)).to(DEV).view(torch.bfloat16)
+    got = host(mcke.bias_act(xt2, dev(b2), "gelu_tanh").view(torch.int16)).view(np.uint16)
+    want = oracle.to_bf16(oracle.bias_act(oracle.bf16_to_f32(xb2), b2, "gelu_tanh"))
+    assert np.abs(got.astype(np.int32) - want.astype(np.int32)).max() <= 1
+
+
+def test_bias_act_rejects_like_the_reference():
+    x = torch.zeros(4, 6, device=DEV)
+    b = torch.zeros(6, device=DEV)
+    with pytest.raises(mcke.MckeError) as e:
+        mcke.bias_act(x, b, vector_width=4)  # cols % 4 != 0
+    assert e.value.code == mcke.INVALID_ARGUMENT
+    with pytest.raises(mcke.MckeError):
+        mcke.bias_act(x, b, vector_width=2, out=x)  # in place
+    with pytest.raises(mcke.MckeError):
+        mcke.bias_act(x[:, 1:].contiguous()[:, :4].contiguous(), b[1:5].contiguous(), vector_width=3)
+    # empty extents: OK, no launch
+    e0 = torch.zeros(0, 8, device=DEV)
+    mcke.bias_act(e0, torch.zeros(8, device=DEV))
+
+
+# -------------------------------------------------------------------- softmax
+
+def test_softmax_golden_vector(vectors):
+    for c in vectors:
+        if c["kind"] != "row_softmax":
+            continue
+        rows, cols = c["ints"]["rows"], c["ints"]["cols"]
+        x = HEX(c["arrays"]["x"]).reshape(rows, cols)
+        want = HEX(c["arrays"]["expect"]).reshape(rows, cols)
+        for variant in ("online", "three_pass"):
+            got = host(mcke.softmax(dev(x), variant))
+            assert_close(got, want, 1e-6, 1e-7, (c["name"], variant))
+
+
+def test_softmax_reference_fixture(fixtures):
+    x, want = fixtures["row_softmax_x"], fixtures["row_softmax_y"]
+    for variant in ("online", "three_pass"):
+        got = host(mcke.softmax(dev(x), variant))
+        assert_close(got, want, REL_SOFTMAX, REL_SOFTMAX * 1e-3, variant, floor=1e-30, max_rel=REL_SOFTMAX)
+
+
+def test_softmax_config2_slice():
+    # Config 2: N(0, 4^2) logits, every 64th row shifted by +80; 2048 of 32768 rows.
+    x = oracle.softmax_config_input(2048, 1024, seed=2)
+    want = oracle.row_softmax(x)
+    got = host(mcke.softmax(dev(x)))
+    assert_close(got, want, REL_SOFTMAX, ABS_SOFTMAX, "config2", floor=1e-30, max_rel=REL_SOFTMAX)
+    assert np.allclose(got.sum(axis=1), 1.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1), (5, 17), (33, 128), (9, 1000), (17, 1536), (4, 2048),
+                                       (6, 3000), (3, 5000), (2, 16384), (2, 20000)])
+def test_softmax_every_path(rows, cols):
+    x = oracle.fill_random(rows * cols, 11, -30, 30).reshape(rows, cols)
+    want = oracle.row_softmax(x)
+    for variant in ("online", "three_pass"):
+        got = host(mcke.softmax(dev(x), variant))
+        assert_close(got, want, REL_SOFTMAX, 1e-12, (rows, cols, variant))
+
+
+def test_softmax_unaligned_rows_take_the_generic_path():
+    base = torch.from_numpy(oracle.fill_random(8 * 256 + 1, 12, -8, 8)).to(DEV)
+    x = base[1:].view(8, 256)  # 4-byte offset: rows are not 16-byte aligned
+    assert x.data_ptr() % 16 != 0
+    got = host(mcke.softmax(x))
+    want = oracle.row_softmax(host(x))
+    assert_close(got, want, REL_SOFTMAX, 1e-12)
+
+
+# ----------------------------------------------------------------- reductions
+
+def test_reduce_full_matches_oracle_bitwise_for_max_and_argmax():
+    n = (1 << 22) + 3
+    x = oracle.fill_random(n, 1)
+    x[123456] = x[3999999] = np.float32(1.5)  # a tie: the lower index must win
+    s, m, i = mcke.decode_result(mcke.reduce_full(dev(x)))
+    ws, wm, wi = oracle.full_reduce(x)
+    assert np.float32(m).view(np.uint32) == np.float32(wm).view(np.uint32)
+    assert i == wi == 123456
+    # sum: double accumulation rounded once, like the oracle -> equal to 1 ulp
+    assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))
+
+
+def test_reduce_full_is_deterministic_and_alignment_independent():
+    n = 3_000_001
+    base = dev(oracle.fill_random(n + 3, 2))
+    r1 = host(mcke.reduce_full(base[:n]))
+    r2 = host(mcke.reduce_full(base[:n]))
+    assert r1.tobytes() == r2.tobytes()
+    for off in (1, 2, 3):
+        x = base[off:off + n]
+        s, m, i = mcke.decode_result(mcke.reduce_full(x))
+        ws, wm, wi = oracle.full_reduce(host(x))
+        assert (m, i) == (wm, wi)
+        assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))
+
+
+@pytest.mark.parametrize("vals,expect", [
+    ([], (0.0, -np.inf, -1)),
+    ([2.0], (2.0, 2.0, 0)),
+    ([np.nan, 3.0, np.nan, 3.0, 1.0], (np.nan, 3.0, 1)),
+    ([np.nan, np.nan], (np.nan, -np.inf, -1)),
+    ([-np.inf, -np.inf, -np.inf], (-np.inf, -np.inf, 0)),
+    ([-0.0, 0.0, -1.0], (-1.0, -0.0, 0)),
+])
+def test_reduce_full_edge_cases(vals, expect):
+    x = torch.tensor(np.array(vals, np.float32), device=DEV)
+    s, m, i = mcke.decode_result(mcke.reduce_full(x))
+    es, em, ei = expect
+    assert i == ei
+    assert (np.isnan(s) and np.isnan(es)) or s == es
+    assert np.float32(m).view(np.uint32) == np.float32(em).view(np.uint32)
+
+
+def test_reduce_sharded_partials_combine_to_the_full_answer():
+    n = 1 << 21
+    x = oracle.fill_random(n, 3)
+    x[n - 1] = np.float32(2.0)
+    x[17] = np.float32(2.0)
+    xt = dev(x)
+    full = mcke.decode_result(mcke.reduce_full(xt))
+    for g in (2, 3, 8):
+        bounds = [n * r // g for r in range(g + 1)]
+        parts = torch.empty(g * mcke.PARTIAL_BYTES, dtype=torch.uint8, device=DEV)
+        for r in range(g):
+            mcke.reduce_full_partial(xt[bounds[r]:bounds[r + 1]], bounds[r],
+                                     out=parts[r * 24:(r + 1) * 24])
+        s, m, i = mcke.decode_result(mcke.reduce_combine(parts, g))
+        assert (m, i) == (full[1], full[2]) == (2.0, 17)
+        ws = oracle.full_reduce(x)[0]
+        assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))
+
+
+def test_reduce_row_golden_vectors(vectors):
+    for c in vectors:
+        if c["kind"] != "row_reduce":
+            continue
+        rows, cols, kind = c["ints"]["rows"], c["ints"]["cols"], c["ints"]["kind"]
+        x = HEX(c["arrays"]["x"]).reshape(rows, cols)
+        want = HEX(c["arrays"]["expect"])
+        for variant in ("smem_tree", "warp_shuffle", "two_pass"):
+            got = host(mcke.reduce_row(dev(x), kind, variant))
+            if c["mode"] == "exact":
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (c["name"], variant)
+            else:
+                assert_close(got, want, 1e-6, 1e-7, (c["name"], variant))
+
+
+@pytest.mark.parametrize("rows,cols", [(7, 333), (256, 4096), (64, 65536), (3, 1), (5, 17)])
+def test_reduce_row_matches_oracle(rows, cols):
+    x = oracle.fill_random(rows * cols, 13).reshape(rows, cols)
+    for kind in ("sum", "max", "mean"):
+        want = oracle.row_reduce(x, kind)
+        for variant in ("warp_shuffle", "two_pass"):
+            got = host(mcke.reduce_row(dev(x), kind, variant))
+            if kind == "max":
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+            else:  # double accumulation: within one float ulp of the oracle
+                assert np.all(np.abs(got - want) <= np.spacing(np.abs(want)) + 1e-30), (kind, variant)
+
+
+def test_reduce_row_two_pass_needs_workspace():
+    x = torch.zeros(4, 64, device=DEV)
+    out = torch.zeros(4, device=DEV)
+    rc = mcke.lib().mcke_sm100_reduce_row_f32(x.data_ptr(), out.data_ptr(), 4, 64, 0, 2, None, 0,
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == mcke.UNIMPLEMENTED
+
+
+# ----------------------------------------------------------------------- GEMM
+
+def test_gemm_f32_golden_vectors_bit_exact(vectors):
+    n_exact = 0
+    for c in vectors:
+        if c["kind"] != "gemm":
+            continue
+        m, n, k = c["ints"]["m"], c["ints"]["n"], c["ints"]["k"]
+        a = HEX(c["arrays"]["a"]).reshape(m, k)
+        b = HEX(c["arrays"]["b"]).reshape(k, n)
+        c0 = HEX(c["arrays"]["c"]).reshape(m, n)
+        alpha = float(HEX([c["floats"]["alpha"]])[0])
+        beta = float(HEX([c["floats"]["beta"]])[0])
+        want = HEX(c["arrays"]["expect"]).reshape(m, n)
+        got = host(mcke.gemm(dev(a), dev(b), dev(c0), alpha, beta))
+        assert c["mode"] == "exact"
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), c["name"]
+        n_exact += 1
+    assert n_exact == 11
+
+
+def test_gemm_f32_reference_fixture(fixtures):
+    a, b, c0 = fixtures["gemm_a"], fixtures["gemm_b"], fixtures["gemm_c"]
+    got = host(mcke.gemm(dev(a), dev(b), dev(c0), 1.5, 0.5))
+    k = a.shape[1]
+    assert_close(got, fixtures["gemm_out"], oracle.tol_gemm(k), oracle.abs_tol_gemm(k, 1.5))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (3, 7, 5), (129, 131, 257), (512, 384, 1000), (300, 260, 3)])
+def test_gemm_f32_matches_oracle(m, n, k):
+    a = oracle.fill_random(m * k, 2).reshape(m, k)
+    b = oracle.fill_random(k * n, 3).reshape(k, n)
+    want = oracle.gemm(a, b)
+    got = host(mcke.gemm(dev(a), dev(b)))
+    # north star: <= 1e-4 relative against the fp64-accumulated reference; the
+    # reference's K-scaled tolerance (tests/reference.hpp:344,:370) is tighter
+    assert_close(got, want, oracle.tol_gemm(k), oracle.abs_tol_gemm(k), (m, n, k), max_rel=1e-4,
+                 floor=1e-2)
+
+
+def test_gemm_f32_k_zero_and_beta():
+    c0 = oracle.fill_random(6 * 5, 9).reshape(6, 5)
+    ct = dev(c0)
+    scratch = torch.zeros(64, device=DEV)  # k == 0 still needs non-null A and B, as in the reference
+    for fn in (mcke.lib().mcke_sm100_gemm_f32, mcke.lib().mcke_sm100_gemm_bf16):
+        c1 = ct.clone()
+        assert fn(scratch.data_ptr(), scratch.data_ptr(), c1.data_ptr(), 6, 5, 0, 1.0, 0.5, 0,
+                  torch.cuda.current_stream().cuda_stream) == mcke.OK
+        assert np.array_equal(host(c1), (c0 * np.float32(0.5)).astype(np.float32))
+    # beta == 0 never reads C: NaN in C must not leak
+    cn = torch.full((4, 4), float("nan"), device=DEV)
+    got = host(mcke.gemm(torch.ones(4, 2, device=DEV), torch.ones(2, 4, device=DEV), cn))
+    assert np.all(got == 2.0)
+
+
+def test_gemm_f32_spot_check_2048():
+    m = n = k = 2048
+    a = oracle.fill_random(m * k, 2).reshape(m, k)
+    b = oracle.fill_random(k * n, 3).reshape(k, n)
+    got = host(mcke.gemm(dev(a), dev(b)))
+    r = oracle.spot_check_gemm(a, b, got, samples=1024, seed=7)
+    assert r["mismatches"] == 0 and r["checked"] == 1024, r
+
+
+def _bf16(a):
+    return torch.from_numpy(oracle.to_bf16(a).view(np.int16)).to(DEV).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 128), (1000, 700, 520), (129, 264, 8),
+                                   (2048, 1024, 1024)])
+def test_gemm_bf16_tcgen05_matches_oracle(m, n, k):
+    a = oracle.fill_random(m * k, 2).reshape(m, k)
+    b = oracle.fill_random(k * n, 3).reshape(k, n)
+    ar, br = oracle.round_bf16(a), oracle.round_bf16(b)
+    got = host(mcke.gemm(_bf16(a), _bf16(b), variant="tcgen05"))
+    mcke.check_device_errors()
+    # (1) against the oracle on the same bf16 inputs: fp32-accumulation tolerance
+    if m * n * k <= 600 * 1000 * 1000:
+        want = oracle.gemm(ar, br)
+        assert_close(got, want, 4 * oracle.tol_gemm(k), 4 * oracle.abs_tol_gemm(k), (m, n, k))
+        # (2) north star: <= 1e-2 against the fp32-input reference
+        want32 = oracle.gemm(a, b)
+        # abs floor ~10 sigma of the bf16 input-rounding error; max rel checked
+        # over outputs above their RMS, sqrt(k/9)*3
+        assert_close(got, want32, 1e-2, 4 * np.sqrt(k) * 2.0 ** -8 / 3, (m, n, k), max_rel=1e-2,
+                     floor=float(np.sqrt(k / 3.0)))
+    else:
+        r = oracle.spot_check_gemm(ar, br, got, samples=512, seed=1, rel_tol=4 * oracle.tol_gemm(k),
+                                   abs_tol=4 * oracle.abs_tol_gemm(k))
+        assert r["mismatches"] == 0, r
+
+
+def test_gemm_bf16_fused_epilogue():
+    m, n, k = 256, 512, 192
+    a = oracle.fill_normal(m * k, 4).reshape(m, k)
+    b = oracle.fill_normal(k * n, 5, 0.0, 0.02 * 8).reshape(k, n)
+    bias = oracle.fill_random(n, 6)
+    ar, br = oracle.round_bf16(a), oracle.round_bf16(b)
+    lin = oracle.gemm(ar, br)
+    want = oracle.to_bf16(oracle.bias_act(lin, bias, "gelu_tanh"))
+    for variant in ("tcgen05", "simt"):
+        out = mcke.gemm(_bf16(a), _bf16(b), bias=dev(bias), act="gelu_tanh",
+                        out_dtype=torch.bfloat16, variant=variant)
+        got = host(out.view(torch.int16)).view(np.uint16)
+        diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
+        assert diff.max() <= 1, variant
+    # fp32 output with alpha/beta/bias
+    c0 = oracle.fill_random(m * n, 7).reshape(m, n)
+    got = host(mcke.gemm(_bf16(a), _bf16(b), dev(c0), 0.5, 2.0, bias=dev(bias), variant="tcgen05"))
+    want = oracle.bias_act((np.float64(0.5) * lin + 2.0 * c0).astype(np.float32), bias, "none")
+    assert_close(got, want, 1e-5, 1e-5)
+
+
+def test_gemm_bf16_simt_fallback_for_tma_incompatible_shapes():
+    m, n, k = 37, 5, 7  # K, N not multiples of 8: TMA cannot describe them
+    a = oracle.fill_random(m * k, 2).reshape(m, k)
+    b = oracle.fill_random(k * n, 3).reshape(k, n)
+    got = host(mcke.gemm(_bf16(a), _bf16(b)))
+    assert_close(got, oracle.gemm(oracle.round_bf16(a), oracle.round_bf16(b)), oracle.tol_gemm(k),
+                 oracle.abs_tol_gemm(k))
+    with pytest.raises(mcke.MckeError):
+        mcke.gemm(_bf16(a), _bf16(b), variant="tcgen05")
+
+
+def test_gemm_kernel_attrs_report_no_spills():
+    for variant, dt in (("tcgen05", "bf16"), ("simt", "f32"), ("simt", "bf16")):
+        at = mcke.gemm_kernel_attrs(variant, dt)
+        assert at["local_bytes"] == 0 and at["regs_per_thread"] > 0, (variant, at)
+        assert at["max_blocks_per_sm_api"] >= 1

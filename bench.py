@@ -439,6 +439,53 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
     return out
 
 
+def run_profile(args) -> None:
+    """One full-size launch of each named kernel after two warm-ups, for ncu
+    (`ncu -k regex:... -s 2 -c 1 python bench.py --profile NAME`).  Sizes are
+    the BASELINE configs: at most ~1 GiB on the device, each launch < 2 ms."""
+    import torch
+    import mcke
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    names = args.profile.split(",")
+    for name in names:
+        if name == "softmax":
+            x = torch.randn(ROWS, COLS, generator=gen, device=dev) * 4.0
+            x[::64] += 80.0
+            y = torch.empty_like(x)
+            fn = lambda: mcke.softmax(x, out=y)  # noqa: E731
+        elif name == "bias_gelu":
+            x = torch.randn(BIAS_ROWS, BIAS_COLS, generator=gen, device=dev)
+            b = torch.rand(BIAS_COLS, generator=gen, device=dev) * 2 - 1
+            y = torch.empty_like(x)
+            fn = lambda: mcke.bias_act(x, b, "gelu_tanh", out=y)  # noqa: E731
+        elif name == "reduce":
+            x = torch.rand(REDUCE_N, generator=gen, device=dev) * 2 - 1
+            ws = torch.empty(mcke.reduce_full_workspace_bytes(REDUCE_N), dtype=torch.uint8, device=dev)
+            res = torch.empty(16, dtype=torch.uint8, device=dev)
+            fn = lambda: mcke.reduce_full(x, out=res, workspace=ws)  # noqa: E731
+        elif name == "gemm_bf16":
+            a = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
+            b = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
+            c = torch.empty(GEMM_N, GEMM_N, device=dev)
+            fn = lambda: mcke.gemm(a, b, c, variant="tcgen05")  # noqa: E731
+        elif name == "gemm_f32":
+            n = 4096
+            a = torch.rand(n, n, generator=gen, device=dev) * 2 - 1
+            b = torch.rand(n, n, generator=gen, device=dev) * 2 - 1
+            c = torch.empty(n, n, device=dev)
+            fn = lambda: mcke.gemm(a, b, c)  # noqa: E731
+        else:
+            raise SystemExit(f"unknown profile case {name}")
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+    mcke.check_device_errors()
+    print("profile cases done:", ",".join(names))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -448,7 +495,11 @@ def main() -> None:
     ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,gemm_f32",
                     help="comma list of extra configs to report under 'ops' ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", default="", help="run one small case per named kernel for ncu and exit")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     dist = Dist()

@@ -1,0 +1,75 @@
+/*
+ * mcke_host.h -- C-ABI of libmcke_host.so, the C++ host layer (Graph, Op,
+ * GraphExecutor with the multi-GPU sharding pass) over libmcke_sm100a.so.
+ *
+ * The reference exposes this layer only as C++ (mini-cuda-kernel-engine
+ * include/mcke/graph/graph.hpp:109 Graph, include/mcke/graph/op.hpp:99 Op and
+ * :180-303 GemmOp/BiasActOp/ReduceOp/SoftmaxOp, include/mcke/graph/executor.hpp:283
+ * GraphExecutor); the C++ headers under mini-cuda-kernel-engine_b200/host/include
+ * keep those names.  These C entry points wrap them for callers without a C++
+ * toolchain (Python's ctypes in this repository's tests and bench).  Objects
+ * are opaque handles; every function returns an mcke_status code and the
+ * message of the last failure on the calling thread is available from
+ * mcke_host_last_error_string().
+ */
+#ifndef MCKE_HOST_H_
+#define MCKE_HOST_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mcke_graph mcke_graph;
+typedef struct mcke_executor mcke_executor;
+
+/* Tensor placement hints for graph inputs (mcke::Placement). */
+enum { MCKE_PLACE_REPLICATED = 0, MCKE_PLACE_ROW_SPLIT = 1, MCKE_PLACE_COL_SPLIT = 2 };
+/* Element types (mcke::DType): 0 f32, 2 bf16, 4 u8. */
+
+const char* mcke_host_last_error_string(void);
+
+/* Graph construction (graph.hpp:109 add_input / add_node / mark_output / finalize). */
+mcke_graph* mcke_graph_create(void);
+void mcke_graph_destroy(mcke_graph* g);
+int mcke_graph_add_input(mcke_graph* g, const char* name, const int64_t* dims, int rank, int dtype,
+                         int placement, uint32_t* id_out);
+/* GemmOp (op.hpp:180): bias < 0 for none; act is mcke_activation; out_dtype 0 f32 / 2 bf16;
+ * variant is the reference's GemmVariant value (8 = kTcgen05Bf16, ignored for bf16 operands). */
+int mcke_graph_add_gemm(mcke_graph* g, const char* name, uint32_t a, uint32_t b, int64_t bias, float alpha,
+                        int act, int out_dtype, int variant, uint32_t* out);
+/* BiasActOp (op.hpp:230): vector_width 0 = widest legal. */
+int mcke_graph_add_bias_act(mcke_graph* g, const char* name, uint32_t x, uint32_t bias, int act,
+                            int vector_width, uint32_t* out);
+/* SoftmaxOp (op.hpp:290). */
+int mcke_graph_add_softmax(mcke_graph* g, const char* name, uint32_t x, int variant, uint32_t* out);
+/* ReduceOp (op.hpp:260). */
+int mcke_graph_add_reduce_row(mcke_graph* g, const char* name, uint32_t x, int kind, int variant, uint32_t* out);
+/* FullReduceOp (new): 16-byte result {float sum; float max; int64 argmax}. */
+int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint32_t* out);
+int mcke_graph_mark_output(mcke_graph* g, uint32_t t);
+int mcke_graph_finalize(mcke_graph* g);
+
+/* GraphExecutor (executor.hpp:283) over `num_devices` GPUs. */
+mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device);
+void mcke_executor_destroy(mcke_executor* e);
+/* Planning only (placement, streams, memory): touches no GPU. */
+int mcke_executor_plan_dry(mcke_executor* e);
+int mcke_executor_plan(mcke_executor* e);
+int mcke_executor_set_input(mcke_executor* e, uint32_t t, const void* host, size_t bytes);
+int mcke_executor_run_async(mcke_executor* e);
+int mcke_executor_synchronize(mcke_executor* e);
+int mcke_executor_copy_output(mcke_executor* e, uint32_t t, void* host, size_t bytes);
+/* Writes a NUL-terminated plan description (placements, streams, waits, arena sizes). */
+int mcke_executor_describe(mcke_executor* e, char* buf, size_t len);
+/* Placement of tensor t after planning (MCKE_PLACE_*), its stream (node output), arena bytes. */
+int mcke_executor_placement(mcke_executor* e, uint32_t t, int* placement_out);
+int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_out);
+int mcke_executor_num_events(mcke_executor* e, size_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MCKE_HOST_H_ */

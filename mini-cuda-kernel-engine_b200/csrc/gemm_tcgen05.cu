@@ -239,9 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_parity[STAGES];
-      bool issued[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued[s] = false, issued_parity[s] = 0;
+      // Stages that have had a load issued, and the parity of their latest
+      // phase, as bit masks (registers, not a local array).
+      uint32_t issued_mask = 0, parity_mask = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mb, nb;
@@ -258,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < BN / 64; ++j)
             tma_load_2d(smem_u32(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES), &tmap_b, fb,
                         nb * BN + 64 * j, kb * BK);
-          issued[stage] = true;
-          issued_parity[stage] = phase;
+          issued_mask |= 1u << stage;
+          parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -269,7 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         // Do not leave with bulk copies still writing this CTA's shared memory.
         for (int s = 0; s < STAGES; ++s)
-          if (issued[s]) wait_bounded(full_bar(s), issued_parity[s], abort_flag, kSiteDrain, false);
+          if (issued_mask & (1u << s))
+            wait_bounded(full_bar(s), (parity_mask >> s) & 1u, abort_flag, kSiteDrain, false);
       }
     }
     __syncwarp();

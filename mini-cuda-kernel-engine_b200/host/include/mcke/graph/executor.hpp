@@ -1,0 +1,106 @@
+// mcke/graph/executor.hpp -- plans and replays a Graph over one or more GPUs.
+//
+// Mirrors mini-cuda-kernel-engine include/mcke/graph/executor.hpp:283-372
+// (GraphExecutor: plan / set_input / run_async / synchronize, ExecutorOptions
+// :115) and adds the sharding pass of a B200 box:
+//
+//   plan()  1. placement: every tensor is Replicated, RowSplit or ColSplit over
+//              the executor's D devices, decided in topological order --
+//                GEMM     A row-split            -> C row-split (B replicated)
+//                         A replicated           -> C column-split (B, bias
+//                                                   stored column-sliced)
+//                BiasAct  follows X (a column-split X slices the bias)
+//                Softmax / Reduce(row)  row-split (a replicated input is split)
+//                FullReduce  each device reduces its contiguous range; the
+//                         24-byte partials are all-gathered with NCCL and
+//                         combined in device order on every device
+//              so no collective moves activations: the only exchange is the
+//              reduction's partials;
+//           2. streams: per device, a node inherits the stream of its first
+//              producer unless a sibling already did (chain-greedy), else the
+//              least-recently-used stream; an event is recorded after a
+//              producer and waited on by each consumer on another stream;
+//           3. memory: per device one arena; graph inputs and outputs own
+//              their bytes, intermediates reuse a freed block of the same
+//              stream (stream order makes that reuse race-free), scratch is
+//              one block per stream sized by the largest workspace_bytes();
+//           4. allocation (one cudaMalloc per device), NCCL communicators
+//              (only if some node exchanges), streams and events.
+//   run_async()  enqueues every node on every device; never synchronises.
+//
+// plan_dry() runs steps 1-3 without touching CUDA, for tests on a host with
+// no GPU.
+#pragma once
+
+#include <cstddef>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "mcke/graph/graph.hpp"
+
+namespace mcke {
+
+struct ExecutorOptions {
+  std::vector<int> devices{0};
+  int streams_per_device = 4;
+  bool poison_buffers = false;  // fill intermediates with 0xFF before each run
+};
+
+struct TensorPlan {
+  Placement placement = Placement::kReplicated;
+  std::vector<std::int64_t> offset;      // per device, bytes into that device's arena
+  std::vector<Shape> local_shape;        // per device
+  std::vector<std::int64_t> row_begin;   // per device (RowSplit) / column begin (ColSplit)
+  std::size_t local_bytes(int d) const;
+  DType dtype = DType::kF32;
+};
+
+class GraphExecutor {
+ public:
+  explicit GraphExecutor(Graph& g, ExecutorOptions opts = {});
+  ~GraphExecutor();
+  GraphExecutor(const GraphExecutor&) = delete;
+  GraphExecutor& operator=(const GraphExecutor&) = delete;
+
+  [[nodiscard]] Status plan_dry();
+  [[nodiscard]] Status plan();
+  // Host data of the WHOLE tensor (row-major); the executor scatters the
+  // slice each device owns.  Synchronous copies (setup, not the hot path).
+  [[nodiscard]] Status set_input(TensorId t, const void* host, std::size_t bytes);
+  [[nodiscard]] Status run_async();
+  [[nodiscard]] Status synchronize();
+  // Gathers a graph output's shards into host memory (whole tensor).
+  [[nodiscard]] Status copy_output_to_host(TensorId t, void* host, std::size_t bytes);
+
+  [[nodiscard]] const TensorPlan& tensor_plan(TensorId t) const { return tplan_.at(t); }
+  [[nodiscard]] int stream_of(NodeId n) const { return node_stream_.at(n); }
+  [[nodiscard]] std::size_t arena_bytes(int device_index) const { return arena_bytes_.at(device_index); }
+  [[nodiscard]] int num_devices() const { return static_cast<int>(opts_.devices.size()); }
+  [[nodiscard]] std::size_t num_events() const { return event_edges_; }
+  [[nodiscard]] std::string describe() const;
+
+ private:
+  struct Impl;
+  [[nodiscard]] Status place();
+  [[nodiscard]] Status assign_streams();
+  [[nodiscard]] Status plan_memory();
+  [[nodiscard]] Tensor local_tensor(TensorId t, int d) const;
+
+  Graph& g_;
+  ExecutorOptions opts_;
+  std::vector<TensorPlan> tplan_;
+  std::vector<int> node_stream_;                 // same stream index on every device
+  std::vector<std::vector<int>> waits_;          // per node: producer nodes on other streams
+  std::vector<bool> record_after_;               // per node: record an event after it
+  std::vector<std::size_t> arena_bytes_;         // per device
+  std::vector<std::vector<std::int64_t>> scratch_offset_;   // [device][stream index]
+  std::vector<std::size_t> scratch_bytes_;                   // per stream index
+  std::vector<std::vector<std::int64_t>> exchange_offset_;  // [device][node] (or -1)
+  std::vector<bool> view_rows_;  // per node: input 0 is a replicated tensor read as local rows
+  std::size_t event_edges_ = 0;
+  bool planned_ = false;
+  std::unique_ptr<Impl> impl_;
+};
+
+}  // namespace mcke

@@ -1,0 +1,164 @@
+// capi_host.cpp -- extern "C" wrappers of the C++ host layer (include/mcke_host.h).
+#include "mcke_host.h"
+
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "mcke/graph/executor.hpp"
+
+struct mcke_graph {
+  mcke::Graph g;
+};
+struct mcke_executor {
+  std::unique_ptr<mcke::GraphExecutor> ex;
+};
+
+namespace {
+thread_local std::string g_err;
+
+int ret(const mcke::Status& s) {
+  if (s.ok()) return 0;
+  g_err = s.to_string();
+  return static_cast<int>(s.code());
+}
+
+template <typename T>
+int ret_ids(const mcke::StatusOr<std::vector<mcke::TensorId>>& r, uint32_t* out) {
+  if (!r.ok()) return ret(r.status());
+  if (out) *out = r.value().at(0);
+  return 0;
+}
+
+int add(mcke_graph* g, const char* name, mcke::OpPtr op, std::vector<mcke::TensorId> in, uint32_t* out) {
+  if (!g) {
+    g_err = "null graph";
+    return static_cast<int>(mcke::StatusCode::kInvalidArgument);
+  }
+  auto r = g->g.add_node(name ? name : "node", std::move(op), std::move(in));
+  return ret_ids<void>(r, out);
+}
+
+mcke::DType dtype_of(int v) { return static_cast<mcke::DType>(v); }
+}  // namespace
+
+extern "C" {
+
+const char* mcke_host_last_error_string(void) { return g_err.c_str(); }
+
+mcke_graph* mcke_graph_create(void) { return new mcke_graph(); }
+void mcke_graph_destroy(mcke_graph* g) { delete g; }
+
+int mcke_graph_add_input(mcke_graph* g, const char* name, const int64_t* dims, int rank, int dtype, int placement,
+                         uint32_t* id_out) {
+  if (!g || !dims || rank < 1 || placement < 0 || placement > 2 || (dtype != 0 && dtype != 2 && dtype != 4)) {
+    g_err = "mcke_graph_add_input: bad argument";
+    return static_cast<int>(mcke::StatusCode::kInvalidArgument);
+  }
+  mcke::TensorDesc d;
+  d.shape = mcke::Shape(std::vector<std::int64_t>(dims, dims + rank));
+  d.dtype = dtype_of(dtype);
+  d.name = name ? name : "input";
+  d.placement = static_cast<mcke::Placement>(placement);
+  const auto id = g->g.add_input(d);
+  if (id_out) *id_out = id;
+  return 0;
+}
+
+int mcke_graph_add_gemm(mcke_graph* g, const char* name, uint32_t a, uint32_t b, int64_t bias, float alpha, int act,
+                        int out_dtype, int variant, uint32_t* out) {
+  mcke::GemmParams p;
+  p.alpha = alpha;
+  p.act = static_cast<mcke::kernels::Activation>(act);
+  p.out_dtype = dtype_of(out_dtype);
+  p.variant = static_cast<mcke::kernels::GemmVariant>(variant);
+  std::vector<mcke::TensorId> in{a, b};
+  if (bias >= 0) in.push_back(static_cast<mcke::TensorId>(bias));
+  return add(g, name, std::make_unique<mcke::GemmOp>(p), in, out);
+}
+
+int mcke_graph_add_bias_act(mcke_graph* g, const char* name, uint32_t x, uint32_t bias, int act, int vector_width,
+                            uint32_t* out) {
+  mcke::BiasActParams p;
+  p.act = static_cast<mcke::BiasActParams::Act>(act);
+  p.vector_width = vector_width;
+  return add(g, name, std::make_unique<mcke::BiasActOp>(p), {x, bias}, out);
+}
+
+int mcke_graph_add_softmax(mcke_graph* g, const char* name, uint32_t x, int variant, uint32_t* out) {
+  mcke::SoftmaxParams p;
+  p.variant = static_cast<mcke::SoftmaxParams::Variant>(variant);
+  return add(g, name, std::make_unique<mcke::SoftmaxOp>(p), {x}, out);
+}
+
+int mcke_graph_add_reduce_row(mcke_graph* g, const char* name, uint32_t x, int kind, int variant, uint32_t* out) {
+  mcke::ReduceParams p;
+  p.kind = static_cast<mcke::ReduceParams::Kind>(kind);
+  p.variant = static_cast<mcke::ReduceParams::Variant>(variant);
+  return add(g, name, std::make_unique<mcke::ReduceOp>(p), {x}, out);
+}
+
+int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint32_t* out) {
+  return add(g, name, std::make_unique<mcke::FullReduceOp>(), {x}, out);
+}
+
+int mcke_graph_mark_output(mcke_graph* g, uint32_t t) { return g ? ret(g->g.mark_output(t)) : 2; }
+int mcke_graph_finalize(mcke_graph* g) { return g ? ret(g->g.finalize()) : 2; }
+
+mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device) {
+  if (!g || !devices || num_devices < 1) return nullptr;
+  mcke::ExecutorOptions o;
+  o.devices.assign(devices, devices + num_devices);
+  o.streams_per_device = streams_per_device > 0 ? streams_per_device : 4;
+  auto* e = new mcke_executor();
+  e->ex = std::make_unique<mcke::GraphExecutor>(g->g, o);
+  return e;
+}
+
+void mcke_executor_destroy(mcke_executor* e) { delete e; }
+
+#define EX_CHECK(e)                                        \
+  if (!(e) || !(e)->ex) {                                  \
+    g_err = "null executor";                               \
+    return static_cast<int>(mcke::StatusCode::kInvalidArgument); \
+  }
+
+int mcke_executor_plan_dry(mcke_executor* e) { EX_CHECK(e); return ret(e->ex->plan_dry()); }
+int mcke_executor_plan(mcke_executor* e) { EX_CHECK(e); return ret(e->ex->plan()); }
+int mcke_executor_set_input(mcke_executor* e, uint32_t t, const void* host, size_t bytes) {
+  EX_CHECK(e);
+  return ret(e->ex->set_input(t, host, bytes));
+}
+int mcke_executor_run_async(mcke_executor* e) { EX_CHECK(e); return ret(e->ex->run_async()); }
+int mcke_executor_synchronize(mcke_executor* e) { EX_CHECK(e); return ret(e->ex->synchronize()); }
+int mcke_executor_copy_output(mcke_executor* e, uint32_t t, void* host, size_t bytes) {
+  EX_CHECK(e);
+  return ret(e->ex->copy_output_to_host(t, host, bytes));
+}
+int mcke_executor_describe(mcke_executor* e, char* buf, size_t len) {
+  EX_CHECK(e);
+  const std::string s = e->ex->describe();
+  if (buf && len) {
+    const size_t n = s.size() < len - 1 ? s.size() : len - 1;
+    std::memcpy(buf, s.data(), n);
+    buf[n] = '\0';
+  }
+  return 0;
+}
+int mcke_executor_placement(mcke_executor* e, uint32_t t, int* placement_out) {
+  EX_CHECK(e);
+  if (placement_out) *placement_out = static_cast<int>(e->ex->tensor_plan(t).placement);
+  return 0;
+}
+int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_out) {
+  EX_CHECK(e);
+  if (bytes_out) *bytes_out = e->ex->arena_bytes(device_index);
+  return 0;
+}
+int mcke_executor_num_events(mcke_executor* e, size_t* out) {
+  EX_CHECK(e);
+  if (out) *out = e->ex->num_events();
+  return 0;
+}
+
+}  // extern "C"

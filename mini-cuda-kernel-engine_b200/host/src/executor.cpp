@@ -1,0 +1,557 @@
+// executor.cpp -- the sharding pass, stream assignment, memory plan and replay.
+#include "mcke/graph/executor.hpp"
+
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <sstream>
+
+namespace mcke {
+namespace {
+
+constexpr std::size_t kAlign = 256;
+std::size_t align_up(std::size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+const char* placement_name(Placement p) {
+  switch (p) {
+    case Placement::kReplicated: return "replicated";
+    case Placement::kRowSplit: return "row-split";
+    case Placement::kColSplit: return "col-split";
+  }
+  return "?";
+}
+
+// Split extent of a tensor under a placement: the flattened rows for rank >= 2,
+// the elements for rank 1, the columns for a column split.
+std::int64_t split_extent(const Shape& s, Placement p) {
+  if (p == Placement::kColSplit) return s.cols();
+  return s.rank() >= 2 ? s.rows() : s.numel();
+}
+
+Status nccl_status(ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return OkStatus();
+  return InternalError(std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+}  // namespace
+
+std::size_t TensorPlan::local_bytes(int d) const {
+  return static_cast<std::size_t>(local_shape.at(d).numel()) * dtype_size(dtype);
+}
+
+struct GraphExecutor::Impl {
+  struct Dev {
+    int device = 0;
+    void* arena = nullptr;
+    std::vector<rt::Stream> streams;
+    std::vector<rt::Event> node_events;  // indexed by NodeId (only where recorded)
+    std::vector<rt::Event> done;         // one per stream: end of the previous run
+    ncclComm_t comm = nullptr;
+  };
+  std::vector<Dev> devs;
+  bool ran_once = false;
+  ~Impl() {
+    for (Dev& d : devs) {
+      rt::DeviceGuard g(d.device);
+      if (d.comm) ncclCommDestroy(d.comm);
+      if (d.arena) cudaFree(d.arena);
+    }
+  }
+};
+
+GraphExecutor::GraphExecutor(Graph& g, ExecutorOptions opts) : g_(g), opts_(std::move(opts)) {}
+GraphExecutor::~GraphExecutor() = default;
+
+// ------------------------------------------------------------- placement
+
+Status GraphExecutor::place() {
+  const int D = num_devices();
+  if (D < 1) return InvalidArgumentError("ExecutorOptions.devices is empty");
+  const std::size_t T = g_.num_tensors();
+  tplan_.assign(T, TensorPlan{});
+  std::vector<bool> locked(T, false);      // a consumer has been planned against this placement
+  std::vector<bool> row_view(T, false);    // replicated intermediate read as local rows
+  view_rows_.assign(g_.num_nodes(), false);
+  for (TensorId t = 0; t < T; ++t) {
+    tplan_[t].dtype = g_.tensor(t).dtype;
+    tplan_[t].placement = (D > 1 && g_.is_input(t)) ? g_.tensor(t).placement : Placement::kReplicated;
+  }
+  auto P = [&](TensorId t) { return tplan_[t].placement; };
+  // Re-place a graph input that no planned consumer depends on yet.
+  auto require = [&](TensorId t, Placement want, const Node& n) -> Status {
+    if (P(t) == want) {
+      locked[t] = true;
+      return OkStatus();
+    }
+    if (!g_.is_input(t) || locked[t])
+      return FailedPreconditionError("node '" + n.name + "' needs tensor '" + g_.tensor(t).name + "' " +
+                                     placement_name(want) + " but it is already " + placement_name(P(t)) +
+                                     "; that would need a collective this executor does not insert");
+    if (want == Placement::kColSplit && g_.tensor(t).shape.rank() != 2 && g_.tensor(t).shape.rank() != 1)
+      return FailedPreconditionError("node '" + n.name + "': only rank-1/2 tensors can be column-split");
+    tplan_[t].placement = want;
+    locked[t] = true;
+    return OkStatus();
+  };
+
+  if (D > 1) {
+    for (NodeId nid : g_.topo_order()) {
+      const Node& n = g_.node(nid);
+      const std::string_view type = n.op->type_name();
+      Placement out = Placement::kReplicated;
+      if (type == "Gemm") {
+        const TensorId a = n.inputs[0], b = n.inputs[1];
+        if (P(a) == Placement::kRowSplit) {
+          MCKE_RETURN_IF_ERROR(require(b, Placement::kReplicated, n));
+          if (n.inputs.size() == 3) MCKE_RETURN_IF_ERROR(require(n.inputs[2], Placement::kReplicated, n));
+          out = Placement::kRowSplit;
+        } else if (P(a) == Placement::kReplicated) {
+          locked[a] = true;
+          MCKE_RETURN_IF_ERROR(require(b, Placement::kColSplit, n));
+          // a rank-1 bias column-splits element-wise, which is its row split
+          if (n.inputs.size() == 3) MCKE_RETURN_IF_ERROR(require(n.inputs[2], Placement::kColSplit, n));
+          out = Placement::kColSplit;
+        } else {
+          return FailedPreconditionError("node '" + n.name + "': a column-split A would need an all-gather");
+        }
+      } else if (type == "BiasAct") {
+        const TensorId x = n.inputs[0], bias = n.inputs[1];
+        if (P(x) == Placement::kColSplit) {
+          MCKE_RETURN_IF_ERROR(require(bias, Placement::kColSplit, n));
+          out = Placement::kColSplit;
+        } else {
+          if (P(x) == Placement::kReplicated) {
+            if (g_.is_input(x) && !locked[x]) MCKE_RETURN_IF_ERROR(require(x, Placement::kRowSplit, n));
+            else row_view[x] = locked[x] = view_rows_[nid] = true;
+          }
+          MCKE_RETURN_IF_ERROR(require(bias, Placement::kReplicated, n));
+          out = Placement::kRowSplit;
+        }
+      } else if (type == "Softmax" || type == "Reduce" || type == "FullReduce") {
+        const TensorId x = n.inputs[0];
+        if (P(x) == Placement::kColSplit)
+          return FailedPreconditionError("node '" + n.name + "' reduces rows of a column-split tensor; that needs "
+                                         "an all-gather this executor does not insert");
+        if (P(x) == Placement::kReplicated) {
+          if (g_.is_input(x) && !locked[x]) MCKE_RETURN_IF_ERROR(require(x, Placement::kRowSplit, n));
+          else row_view[x] = locked[x] = view_rows_[nid] = true;
+        }
+        locked[x] = true;
+        out = (type == "FullReduce") ? Placement::kReplicated : Placement::kRowSplit;
+      } else {
+        return UnimplementedError("node '" + n.name + "': no sharding rule for op " + std::string(type));
+      }
+      for (TensorId o : n.outputs) tplan_[o].placement = out;
+    }
+  }
+  // Local shapes.
+  for (TensorId t = 0; t < T; ++t) {
+    TensorPlan& tp = tplan_[t];
+    const Shape& s = g_.tensor(t).shape;
+    tp.local_shape.assign(D, s);
+    tp.row_begin.assign(D, 0);
+    tp.offset.assign(D, -1);
+    if (tp.placement == Placement::kReplicated) continue;
+    const std::int64_t E = split_extent(s, tp.placement);
+    if (E < D)
+      return FailedPreconditionError("tensor '" + g_.tensor(t).name + "' has " + std::to_string(E) +
+                                     " rows/columns to split over " + std::to_string(D) + " devices");
+    for (int d = 0; d < D; ++d) {
+      const std::int64_t b = E * d / D, e = E * (d + 1) / D;
+      tp.row_begin[d] = b;
+      if (tp.placement == Placement::kColSplit)
+        tp.local_shape[d] = s.rank() == 1 ? Shape{e - b} : Shape{s.rows(), e - b};
+      else
+        tp.local_shape[d] = s.rank() >= 2 ? Shape{e - b, s.cols()} : Shape{e - b};
+    }
+  }
+  // Row views of replicated intermediates use the row split of the consumer's
+  // other operands; record the boundaries so local_tensor can offset into them.
+  for (TensorId t = 0; t < T; ++t) {
+    if (!row_view[t]) continue;
+    const Shape& s = g_.tensor(t).shape;
+    const std::int64_t E = s.rank() >= 2 ? s.rows() : s.numel();
+    for (int d = 0; d < D; ++d) tplan_[t].row_begin[d] = E * d / D;
+  }
+  return OkStatus();
+}
+
+// ------------------------------------------------------------ streams
+
+Status GraphExecutor::assign_streams() {
+  const int S = std::max(1, opts_.streams_per_device);
+  const std::size_t N = g_.num_nodes();
+  node_stream_.assign(N, 0);
+  waits_.assign(N, {});
+  record_after_.assign(N, false);
+  std::vector<bool> donated(N, false);
+  std::vector<std::int64_t> last_use(S, -1);
+  std::int64_t tick = 0;
+  for (NodeId nid : g_.topo_order()) {
+    const Node& n = g_.node(nid);
+    int s = -1;
+    for (TensorId t : n.inputs) {
+      const NodeId p = g_.producer(t);
+      if (p != kInvalidNode && !donated[p]) {
+        donated[p] = true;
+        s = node_stream_[p];
+        break;
+      }
+    }
+    if (s < 0) s = static_cast<int>(std::min_element(last_use.begin(), last_use.end()) - last_use.begin());
+    node_stream_[nid] = s;
+    last_use[s] = tick++;
+  }
+  event_edges_ = 0;
+  for (NodeId nid : g_.topo_order()) {
+    const Node& n = g_.node(nid);
+    for (TensorId t : n.inputs) {
+      const NodeId p = g_.producer(t);
+      if (p == kInvalidNode || node_stream_[p] == node_stream_[nid]) continue;
+      if (std::find(waits_[nid].begin(), waits_[nid].end(), static_cast<int>(p)) != waits_[nid].end()) continue;
+      waits_[nid].push_back(static_cast<int>(p));
+      record_after_[p] = true;
+      ++event_edges_;
+    }
+  }
+  return OkStatus();
+}
+
+// ------------------------------------------------------------- memory
+
+Status GraphExecutor::plan_memory() {
+  const int D = num_devices();
+  const int S = std::max(1, opts_.streams_per_device);
+  const auto& order = g_.topo_order();
+  const std::size_t T = g_.num_tensors();
+  std::vector<std::int64_t> pos(g_.num_nodes(), 0);
+  for (std::size_t i = 0; i < order.size(); ++i) pos[order[i]] = static_cast<std::int64_t>(i);
+  // Last use and the set of streams touching each tensor.
+  std::vector<std::int64_t> last(T, -1);
+  std::vector<bool> single_stream(T, true);
+  std::vector<int> home(T, -1);
+  for (TensorId t = 0; t < T; ++t) {
+    const NodeId p = g_.producer(t);
+    if (p != kInvalidNode) {
+      home[t] = node_stream_[p];
+      last[t] = pos[p];
+    }
+    for (NodeId c : g_.consumers(t)) {
+      last[t] = std::max(last[t], pos[c]);
+      if (home[t] >= 0 && node_stream_[c] != home[t]) single_stream[t] = false;
+    }
+  }
+  arena_bytes_.assign(D, 0);
+  scratch_offset_.assign(D, std::vector<std::int64_t>(S, 0));
+  scratch_bytes_.assign(S, 0);
+  exchange_offset_.assign(D, std::vector<std::int64_t>(g_.num_nodes(), -1));
+  // Scratch per stream: the largest workspace any node on it needs (any device).
+  for (NodeId nid : order) {
+    const Node& n = g_.node(nid);
+    for (int d = 0; d < D; ++d) {
+      std::vector<TensorDesc> in;
+      for (TensorId t : n.inputs) {
+        TensorDesc desc = g_.tensor(t);
+        desc.shape = tplan_[t].local_shape[d];
+        in.push_back(desc);
+      }
+      scratch_bytes_[node_stream_[nid]] = std::max(scratch_bytes_[node_stream_[nid]], n.op->workspace_bytes(in));
+    }
+  }
+  for (int d = 0; d < D; ++d) {
+    std::size_t bump = 0;
+    struct Block {
+      std::size_t off, size;
+      int stream;
+      bool free;
+    };
+    std::vector<Block> blocks;
+    std::vector<int> block_of(T, -1);
+    auto fresh = [&](std::size_t bytes) {
+      const std::size_t off = bump;
+      bump += align_up(std::max<std::size_t>(bytes, 1));
+      return off;
+    };
+    for (TensorId t = 0; t < T; ++t)  // inputs and outputs own their bytes
+      if (g_.is_input(t) || g_.is_output(t)) tplan_[t].offset[d] = static_cast<std::int64_t>(fresh(tplan_[t].local_bytes(d)));
+    for (std::size_t i = 0; i < order.size(); ++i) {
+      const Node& n = g_.node(order[i]);
+      const int s = node_stream_[n.id];
+      for (TensorId o : n.outputs) {
+        if (tplan_[o].offset[d] >= 0) continue;
+        const std::size_t need = align_up(std::max<std::size_t>(tplan_[o].local_bytes(d), 1));
+        int best = -1;
+        if (single_stream[o])
+          for (std::size_t b = 0; b < blocks.size(); ++b)
+            if (blocks[b].free && blocks[b].stream == s && blocks[b].size >= need &&
+                (best < 0 || blocks[b].size < blocks[best].size))
+              best = static_cast<int>(b);
+        if (best < 0) {
+          blocks.push_back({fresh(need), need, single_stream[o] ? s : -1, false});
+          best = static_cast<int>(blocks.size()) - 1;
+        }
+        blocks[best].free = false;
+        block_of[o] = best;
+        tplan_[o].offset[d] = static_cast<std::int64_t>(blocks[best].off);
+      }
+      // Free intermediates whose last use was this node (same-stream blocks only).
+      for (TensorId t : n.inputs)
+        if (block_of[t] >= 0 && last[t] == static_cast<std::int64_t>(i) && blocks[block_of[t]].stream >= 0)
+          blocks[block_of[t]].free = true;
+      for (TensorId o : n.outputs)
+        if (block_of[o] >= 0 && last[o] == static_cast<std::int64_t>(i) && blocks[block_of[o]].stream >= 0)
+          blocks[block_of[o]].free = true;
+    }
+    // Exchange buffers: own partial + all devices' partials, per exchanging node.
+    for (NodeId nid : order) {
+      const std::size_t eb = g_.node(nid).op->exchange_bytes();
+      if (eb == 0) continue;
+      exchange_offset_[d][nid] = static_cast<std::int64_t>(fresh(eb * static_cast<std::size_t>(D + 1)));
+    }
+    for (int s = 0; s < S; ++s) scratch_offset_[d][s] = static_cast<std::int64_t>(fresh(scratch_bytes_[s]));
+    arena_bytes_[d] = bump;
+  }
+  return OkStatus();
+}
+
+Status GraphExecutor::plan_dry() {
+  if (!g_.finalized()) MCKE_RETURN_IF_ERROR(g_.finalize());
+  MCKE_RETURN_IF_ERROR(place());
+  MCKE_RETURN_IF_ERROR(assign_streams());
+  MCKE_RETURN_IF_ERROR(plan_memory());
+  return OkStatus();
+}
+
+Status GraphExecutor::plan() {
+  MCKE_RETURN_IF_ERROR(plan_dry());
+  impl_ = std::make_unique<Impl>();
+  const int D = num_devices();
+  const int S = std::max(1, opts_.streams_per_device);
+  impl_->devs.resize(D);
+  bool any_exchange = false;
+  for (NodeId nid : g_.topo_order()) any_exchange |= g_.node(nid).op->exchange_bytes() > 0;
+  for (int d = 0; d < D; ++d) {
+    auto& dv = impl_->devs[d];
+    dv.device = opts_.devices[d];
+    rt::DeviceGuard guard(dv.device);
+    const cudaError_t e = cudaMalloc(&dv.arena, std::max<std::size_t>(arena_bytes_[d], kAlign));
+    if (e != cudaSuccess)
+      return OutOfMemoryError("arena of " + std::to_string(arena_bytes_[d]) + " bytes on device " +
+                              std::to_string(dv.device) + ": " + cudaGetErrorString(e));
+    for (int s = 0; s < S; ++s) {
+      auto st = rt::Stream::create(dv.device);
+      MCKE_RETURN_IF_ERROR(st.status());
+      dv.streams.push_back(std::move(*st));
+      auto ev = rt::Event::create(dv.device);
+      MCKE_RETURN_IF_ERROR(ev.status());
+      dv.done.push_back(std::move(*ev));
+    }
+    dv.node_events.resize(g_.num_nodes());
+    for (NodeId nid = 0; nid < g_.num_nodes(); ++nid)
+      if (record_after_[nid]) {
+        auto ev = rt::Event::create(dv.device);
+        MCKE_RETURN_IF_ERROR(ev.status());
+        dv.node_events[nid] = std::move(*ev);
+      }
+  }
+  if (any_exchange && D > 1) {
+    std::vector<ncclComm_t> comms(D);
+    MCKE_RETURN_IF_ERROR(nccl_status(ncclCommInitAll(comms.data(), D, opts_.devices.data()), "ncclCommInitAll"));
+    for (int d = 0; d < D; ++d) impl_->devs[d].comm = comms[d];
+  }
+  planned_ = true;
+  return OkStatus();
+}
+
+Tensor GraphExecutor::local_tensor(TensorId t, int d) const {
+  const TensorPlan& tp = tplan_[t];
+  Tensor x;
+  x.dtype = tp.dtype;
+  x.device = opts_.devices[d];
+  x.shape = tp.local_shape[d];
+  x.data = impl_ ? static_cast<char*>(impl_->devs[d].arena) + tp.offset[d] : nullptr;
+  return x;
+}
+
+Status GraphExecutor::run_async() {
+  if (!planned_) return FailedPreconditionError("run_async: plan() has not succeeded");
+  const int D = num_devices();
+  const int S = std::max(1, opts_.streams_per_device);
+  // Each run starts after every stream of the previous run finished (join),
+  // so a reused block is never overwritten while a reader is still running.
+  for (auto& dv : impl_->devs) {
+    if (impl_->ran_once)
+      for (int s = 0; s < S; ++s)
+        for (int o = 0; o < S; ++o)
+          if (o != s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[o]));
+    if (opts_.poison_buffers) {
+      rt::DeviceGuard g(dv.device);
+      const int d = static_cast<int>(&dv - impl_->devs.data());
+      for (TensorId t = 0; t < g_.num_tensors(); ++t)
+        if (!g_.is_input(t))
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMemsetAsync(static_cast<char*>(dv.arena) + tplan_[t].offset[d], 0xFF,
+                                                    tplan_[t].local_bytes(d), dv.streams[0].native()));
+      MCKE_RETURN_IF_ERROR(dv.done[0].record(dv.streams[0]));
+      for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[0]));
+    }
+  }
+  for (NodeId nid : g_.topo_order()) {
+    Node& n = g_.node(nid);
+    const int s = node_stream_[nid];
+    std::vector<OpContext> ctx(D);
+    std::vector<std::vector<Tensor>> ins(D), outs(D);
+    for (int d = 0; d < D; ++d) {
+      auto& dv = impl_->devs[d];
+      for (int p : waits_[nid]) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.node_events[p]));
+      ctx[d].stream = dv.streams[s].native();
+      ctx[d].device = dv.device;
+      ctx[d].workspace = scratch_bytes_[s] ? static_cast<char*>(dv.arena) + scratch_offset_[d][s] : nullptr;
+      ctx[d].workspace_bytes = scratch_bytes_[s];
+      ctx[d].shard = d;
+      ctx[d].num_shards = D;
+      for (TensorId t : n.inputs) {
+        Tensor x = local_tensor(t, d);
+        // A replicated intermediate consumed row-wise: view this device's rows.
+        if (view_rows_[nid] && t == n.inputs[0]) {
+          const Shape& full = g_.tensor(t).shape;
+          const std::int64_t E = full.rank() >= 2 ? full.rows() : full.numel();
+          const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
+          const std::int64_t b = E * d / D, e = E * (d + 1) / D;
+          x.data = static_cast<char*>(x.data) + b * inner * static_cast<std::int64_t>(dtype_size(x.dtype));
+          x.shape = full.rank() >= 2 ? Shape{e - b, inner} : Shape{e - b};
+        }
+        ins[d].push_back(x);
+      }
+      for (TensorId t : n.outputs) outs[d].push_back(local_tensor(t, d));
+      // Range shards of a full reduce: global index of this device's first element.
+      if (!n.inputs.empty()) {
+        const TensorPlan& tp = tplan_[n.inputs[0]];
+        const Shape& full = g_.tensor(n.inputs[0]).shape;
+        const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
+        if (tp.placement == Placement::kRowSplit || view_rows_[nid])
+          ctx[d].index_base = (full.rank() >= 2 ? full.rows() : full.numel()) * d / D * inner;
+      }
+      if (exchange_offset_[d][nid] >= 0) ctx[d].exchange = static_cast<char*>(dv.arena) + exchange_offset_[d][nid];
+    }
+    for (int d = 0; d < D; ++d) {
+      rt::DeviceGuard g(impl_->devs[d].device);
+      const Status st = n.op->launch(ctx[d], ins[d], outs[d]);
+      if (!st.ok()) return Status(st.code(), "node '" + n.name + "' on device " + std::to_string(ctx[d].device) + ": " + st.message());
+    }
+    const std::size_t eb = n.op->exchange_bytes();
+    if (eb > 0) {
+      std::vector<void*> gathered(D);
+      for (int d = 0; d < D; ++d) gathered[d] = static_cast<char*>(ctx[d].exchange) + eb;
+      if (D > 1) {
+        MCKE_RETURN_IF_ERROR(nccl_status(ncclGroupStart(), "ncclGroupStart"));
+        for (int d = 0; d < D; ++d) {
+          rt::DeviceGuard g(impl_->devs[d].device);
+          MCKE_RETURN_IF_ERROR(nccl_status(ncclAllGather(ctx[d].exchange, gathered[d], eb, ncclUint8,
+                                                         impl_->devs[d].comm, ctx[d].stream),
+                                           "ncclAllGather"));
+        }
+        MCKE_RETURN_IF_ERROR(nccl_status(ncclGroupEnd(), "ncclGroupEnd"));
+      } else {
+        gathered[0] = ctx[0].exchange;
+      }
+      for (int d = 0; d < D; ++d) {
+        rt::DeviceGuard g(impl_->devs[d].device);
+        MCKE_RETURN_IF_ERROR(n.op->finish(ctx[d], gathered[d], outs[d]));
+      }
+    }
+    if (record_after_[nid])
+      for (auto& dv : impl_->devs) MCKE_RETURN_IF_ERROR(dv.node_events[nid].record(dv.streams[s]));
+  }
+  for (auto& dv : impl_->devs)
+    for (int s = 0; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.done[s].record(dv.streams[s]));
+  impl_->ran_once = true;
+  return OkStatus();
+}
+
+Status GraphExecutor::synchronize() {
+  if (!impl_) return FailedPreconditionError("synchronize: not planned");
+  for (auto& dv : impl_->devs)
+    for (auto& s : dv.streams) MCKE_RETURN_IF_ERROR(s.synchronize());
+  return OkStatus();
+}
+
+Status GraphExecutor::set_input(TensorId t, const void* host, std::size_t bytes) {
+  if (!planned_) return FailedPreconditionError("set_input: plan() has not succeeded");
+  if (!g_.is_input(t)) return InvalidArgumentError("set_input: tensor is not a graph input");
+  const TensorDesc& desc = g_.tensor(t);
+  const std::size_t es = dtype_size(desc.dtype);
+  if (bytes != static_cast<std::size_t>(desc.shape.numel()) * es)
+    return InvalidArgumentError("set_input: expected " + std::to_string(desc.shape.numel() * es) + " bytes");
+  const TensorPlan& tp = tplan_[t];
+  for (int d = 0; d < num_devices(); ++d) {
+    rt::DeviceGuard g(impl_->devs[d].device);
+    char* dst = static_cast<char*>(impl_->devs[d].arena) + tp.offset[d];
+    const char* src = static_cast<const char*>(host);
+    if (tp.placement == Placement::kReplicated) {
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+    } else if (tp.placement == Placement::kRowSplit) {
+      const std::int64_t inner = desc.shape.rank() >= 2 ? desc.shape.cols() : 1;
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy(dst, src + tp.row_begin[d] * inner * es, tp.local_bytes(d),
+                                           cudaMemcpyHostToDevice));
+    } else {
+      const std::int64_t R = desc.shape.rank() == 1 ? 1 : desc.shape.rows();
+      const std::int64_t C = desc.shape.cols();
+      const std::int64_t w = tp.local_shape[d].cols();
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy2D(dst, w * es, src + tp.row_begin[d] * es, C * es, w * es, R,
+                                             cudaMemcpyHostToDevice));
+    }
+  }
+  return OkStatus();
+}
+
+Status GraphExecutor::copy_output_to_host(TensorId t, void* host, std::size_t bytes) {
+  if (!planned_) return FailedPreconditionError("copy_output_to_host: plan() has not succeeded");
+  const TensorDesc& desc = g_.tensor(t);
+  const std::size_t es = dtype_size(desc.dtype);
+  if (bytes != static_cast<std::size_t>(desc.shape.numel()) * es)
+    return InvalidArgumentError("copy_output_to_host: expected " + std::to_string(desc.shape.numel() * es) + " bytes");
+  MCKE_RETURN_IF_ERROR(synchronize());
+  const TensorPlan& tp = tplan_[t];
+  char* dst = static_cast<char*>(host);
+  const int D = tp.placement == Placement::kReplicated ? 1 : num_devices();
+  for (int d = 0; d < D; ++d) {
+    rt::DeviceGuard g(impl_->devs[d].device);
+    const char* src = static_cast<const char*>(impl_->devs[d].arena) + tp.offset[d];
+    if (tp.placement == Placement::kReplicated) {
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost));
+    } else if (tp.placement == Placement::kRowSplit) {
+      const std::int64_t inner = desc.shape.rank() >= 2 ? desc.shape.cols() : 1;
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy(dst + tp.row_begin[d] * inner * es, src, tp.local_bytes(d),
+                                           cudaMemcpyDeviceToHost));
+    } else {
+      const std::int64_t R = desc.shape.rank() == 1 ? 1 : desc.shape.rows();
+      const std::int64_t C = desc.shape.cols();
+      const std::int64_t w = tp.local_shape[d].cols();
+      MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy2D(dst + tp.row_begin[d] * es, C * es, src, w * es, w * es, R,
+                                             cudaMemcpyDeviceToHost));
+    }
+  }
+  return OkStatus();
+}
+
+std::string GraphExecutor::describe() const {
+  std::ostringstream os;
+  os << "devices=" << num_devices() << " streams_per_device=" << opts_.streams_per_device
+     << " cross_stream_events=" << event_edges_ << "\n";
+  for (NodeId nid : g_.topo_order()) {
+    const Node& n = g_.node(nid);
+    os << "node " << n.name << " (" << n.op->type_name() << ") stream=" << node_stream_[nid] << " waits=[";
+    for (std::size_t i = 0; i < waits_[nid].size(); ++i) os << (i ? "," : "") << g_.node(waits_[nid][i]).name;
+    os << "]\n";
+  }
+  for (TensorId t = 0; t < g_.num_tensors(); ++t) {
+    os << "tensor " << g_.tensor(t).name << " " << g_.tensor(t).shape.to_string() << " "
+       << placement_name(tplan_[t].placement) << " local0=" << tplan_[t].local_shape[0].to_string()
+       << " offset0=" << tplan_[t].offset[0] << "\n";
+  }
+  for (int d = 0; d < num_devices(); ++d) os << "arena[" << d << "]=" << arena_bytes_[d] << "\n";
+  return os.str();
+}
+
+}  // namespace mcke

@@ -156,6 +156,22 @@ int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_
 /* Combines `count` partials (device memory, shard order) into one result. */
 int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count,
                               mcke_reduce_result* out, mcke_stream_t stream);
+/* No counterpart in the reference.  mcke_sm100_reduce_full_f32 for callers that
+ * cannot allocate device memory -- for example a host runtime whose memory
+ * manager owns every device allocation, or a foreign-language binding that
+ * holds only its own input and output buffers -- and so cannot pass a
+ * workspace.  Same result as mcke_sm100_reduce_full_f32; allocates nothing.
+ * Its scratch is a fixed 28,416-byte array (1184 partials of 24 bytes) inside
+ * the library, which every GPU that loads the library keeps until the process
+ * exits; a request needing more partials than that is rejected with
+ * MCKE_INVALID_ARGUMENT (the kernel's grid never needs more, so every n fits).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (other streams, other host threads) race and must be serialised by the
+ * caller.  Nothing in the array needs to start at zero. */
+int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mcke_reduce_result* out,
+                                       mcke_stream_t stream);
 
 /* ---- GEMM: C[M,N] = alpha * A[M,K] @ B[K,N] + beta * C, row-major -------- */
 

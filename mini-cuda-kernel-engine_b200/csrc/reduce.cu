@@ -16,6 +16,7 @@
 // index holding the maximum; each thread visits its elements in increasing
 // index order and the combine breaks value ties by index.
 #include <cfloat>
+#include <mutex>
 
 #include "mcke_common.cuh"
 
@@ -398,5 +399,85 @@ extern "C" int mcke_sm100_reduce_row_f32(const float* x, float* out, int64_t row
     if (vec) row_reduce_warp_kernel<false, true><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
     else row_reduce_warp_kernel<false, false><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
   }
+  return check_launch(who);
+}
+
+// ---- full reduce with no caller scratch -------------------------------------
+//
+// Some callers cannot allocate device memory at all: a host runtime whose
+// memory manager owns every device allocation and forbids side allocations, or
+// a foreign-language binding that only ever holds the caller's own input and
+// output buffers.  They cannot provide the workspace mcke_sm100_reduce_full_f32
+// needs, so this variant keeps its pass-1 partials in a fixed array in device
+// memory instead.  The array lives in this library's module: every GPU that
+// loads the library holds these bytes until the process exits.
+//
+// Capacity: one partial per pass-1 block, and the pass-1 grid never exceeds
+// kMaxBlocks (1184) blocks, so the array is 1184 x 24 = 28,416 bytes and every
+// n fits.  The capacity check below still rejects any request that would need
+// more, with a clear error, should the grid cap ever grow past the array.
+namespace mcke_sm100 {
+namespace {
+
+constexpr int64_t kStaticParts = kMaxBlocks;
+static __device__ __align__(256) Part g_static_parts[kStaticParts];
+
+// Device address of g_static_parts for each device, looked up once per device
+// with that device current (the host-side name is only a stand-in; a kernel
+// must be handed the device address).
+std::mutex g_static_mu;
+void* g_static_addr[64] = {};
+
+int static_parts_address(const char* who, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(MCKE_INVALID_ARGUMENT, "%s: device index %d beyond 63", who, dev);
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if (!g_static_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_parts);
+    if (e != cudaSuccess || !p)
+      return fail(MCKE_CUDA_ERROR, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+    g_static_addr[dev] = p;
+  }
+  *out = g_static_addr[dev];
+  return MCKE_OK;
+}
+
+}  // namespace
+}  // namespace mcke_sm100
+
+extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mcke_reduce_result* out,
+                                                  mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_full_f32_noalloc";
+  clear_error();
+  if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
+  if (n < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (n > 0 && !x) return fail(MCKE_INVALID_ARGUMENT, "%s: null input", who);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    reduce_full_combine_kernel<true><<<1, 32, 0, s>>>(nullptr, 0, out);
+    return check_launch(who);
+  }
+  if (!aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
+  const int64_t g = full_blocks(n);
+  if (g > kStaticParts)
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: n = %lld needs %lld partials but the built-in scratch holds %lld (%lld bytes)", who,
+                static_cast<long long>(n), static_cast<long long>(g), static_cast<long long>(kStaticParts),
+                static_cast<long long>(kStaticParts * static_cast<int64_t>(sizeof(Part))));
+  void* scratch = nullptr;
+  MCKE_RETURN_IF(static_parts_address(who, &scratch));
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+  int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
+  if (head > n) head = n;
+  // Pass 1 writes partials [0, g) before pass 2 reads exactly those, so the
+  // array's leftover contents from an earlier call are never read and nothing
+  // needs clearing.
+  Part* parts = static_cast<Part*>(scratch);
+  reduce_full_pass1_kernel<<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, 0, parts);
+  MCKE_RETURN_IF(check_launch(who));
+  reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   return check_launch(who);
 }

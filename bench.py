@@ -419,6 +419,65 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "peak": peaks["bf16_tflops"], "kernel_ms": round(kms, 4), "parallelism": f"columns of B and C over {g}"}
         del a, b, c
 
+    for fused in (True, False):
+        key = "dag_fused" if fused else "dag_unfused"
+        if key not in want:
+            continue
+        from mcke import host as mhost
+        rows_total, dm, fm, branches = 8192, 4096, 16384, 4
+        r0, r1 = shard(rows_total)
+        rows = r1 - r0
+        cpu = torch.Generator()
+        cpu.manual_seed(5)
+        bf = lambda t: t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        gr = mhost.Graph()
+        x = gr.input("X", (rows, dm), "bf16")
+        feeds = {x: bf(torch.randn(rows, dm, generator=cpu))}
+        for i in range(branches):
+            w1 = gr.input(f"W1_{i}", (dm, fm), "bf16")
+            b1 = gr.input(f"b1_{i}", (fm,), "f32")
+            w2 = gr.input(f"W2_{i}", (fm, dm), "bf16")
+            b2 = gr.input(f"b2_{i}", (dm,), "f32")
+            feeds[w1] = bf(torch.randn(dm, fm, generator=cpu) * 0.02)
+            feeds[w2] = bf(torch.randn(fm, dm, generator=cpu) * 0.02)
+            feeds[b1] = (torch.rand(fm, generator=cpu) * 2 - 1).numpy()
+            feeds[b2] = (torch.rand(dm, generator=cpu) * 2 - 1).numpy()
+            if fused:
+                h = gr.gemm(x, w1, bias=b1, act="gelu_tanh", out_dtype="bf16", name=f"gemm1_{i}")
+                y = gr.gemm(h, w2, bias=b2, name=f"gemm2_{i}")
+            else:
+                h = gr.bias_act(gr.gemm(x, w1, out_dtype="bf16", name=f"gemm1_{i}"), b1, "gelu_tanh",
+                               name=f"bias_gelu_{i}")
+                y = gr.bias_act(gr.gemm(h, w2, name=f"gemm2_{i}"), b2, "none", name=f"bias2_{i}")
+            gr.output(gr.softmax(y, name=f"softmax_{i}"))
+        gr.finalize()
+        ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4)
+        ex.plan()
+        for t, arr in feeds.items():
+            ex.set_input(t, arr)
+        del feeds
+        for _ in range(warm):
+            ex.run()
+        ex.synchronize()
+        dist.barrier(torch)
+        ds = max(3, min(args.steps, 10))
+        tot = 0.0
+        for _ in range(ds):
+            ex.run()
+            tot += ex.last_run_ms()
+        dist.barrier(torch)
+        tot = dist.max(torch, tot)
+        flops = branches * 2 * 2 * rows_total * dm * fm
+        out[key + "_config5"] = {
+            "value": round(flops * ds / (tot * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
+            "ms_per_run": round(tot / ds, 3), "branches": branches, "rows_per_gpu": rows,
+            "frac_of_bf16_peak": round(flops / g / (tot / ds * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+            "peak": peaks["bf16_tflops_sustained"], "peak_kind": "bf16_tflops_sustained (multi-kernel step)",
+            "note": ("GEMM1 with fused bias+GELU (bf16 out) -> GEMM2 with fused +b2 -> softmax" if fused else
+                     "GEMM1 -> bias+GELU -> GEMM2 -> +b2 -> softmax, one kernel each") +
+                    "; 4 branches on 4 streams of the C++ GraphExecutor, timed by its fork/join events"}
+        del ex, gr
+
     if "gemm_f32" in want:
         n0, n1 = shard(GEMM_N)
         gen = torch.Generator(device=dev)
@@ -492,7 +551,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mcke", "reference"], default="mcke")
-    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,gemm_f32",
+    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,dag_fused,dag_unfused,gemm_f32",
                     help="comma list of extra configs to report under 'ops' ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default="", help="run one small case per named kernel for ncu and exit")

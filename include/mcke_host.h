@@ -62,6 +62,8 @@ int mcke_executor_set_input(mcke_executor* e, uint32_t t, const void* host, size
 int mcke_executor_run_async(mcke_executor* e);
 int mcke_executor_synchronize(mcke_executor* e);
 int mcke_executor_copy_output(mcke_executor* e, uint32_t t, void* host, size_t bytes);
+/* Device time of the last run in ms (fork-to-join events, max over devices); synchronises. */
+int mcke_executor_last_run_ms(mcke_executor* e, float* ms_out);
 /* Writes a NUL-terminated plan description (placements, streams, waits, arena sizes). */
 int mcke_executor_describe(mcke_executor* e, char* buf, size_t len);
 /* Placement of tensor t after planning (MCKE_PLACE_*), its stream (node output), arena bytes. */

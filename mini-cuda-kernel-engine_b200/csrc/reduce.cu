@@ -90,7 +90,12 @@ int64_t full_blocks(int64_t n) {
 // Pass 1: each block writes one Part for its grid-strided share of x.
 // Elements before the first 16-byte boundary and after the last whole float4
 // go to global thread 0 (head first, tail last), keeping its visit order
-// increasing.
+// increasing.  In the vector body the running maximum is updated once per
+// float4 (its lane maximum against the running one) and only the float4's
+// index is remembered; the lane is resolved once, after the loop, by reloading
+// that float4 and taking its first element equal to the maximum.  A later
+// float4 with an equal maximum never replaces an earlier one, so the lowest
+// index survives, as in the element-wise rule.
 __global__ void __launch_bounds__(kThreads) reduce_full_pass1_kernel(const float* __restrict__ x,
                                                                      int64_t n, int64_t head,
                                                                      long long base,
@@ -103,24 +108,38 @@ __global__ void __launch_bounds__(kThreads) reduce_full_pass1_kernel(const float
     for (int64_t i = 0; i < head; ++i) part_add(p, x[i], base + i);
   const float* xa = x + head;
   const int64_t nv = (n - head) / 4;
-  for (int64_t v0 = tid; v0 < nv; v0 += nthreads * kUnroll) {
+  double s = p.s;
+  float m = p.m;
+  long long vbest = -1;  // float4 index holding the running maximum (pending lane)
+  const bool have_index = p.i >= 0;
+  auto take4 = [&](const float4& q, int64_t v) {
+    s += static_cast<double>(q.x);
+    s += static_cast<double>(q.y);
+    s += static_cast<double>(q.z);
+    s += static_cast<double>(q.w);
+    const float lm = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));  // NaN lanes never win
+    if (lm > m || (vbest < 0 && !have_index && lm == m)) {
+      m = lm;
+      vbest = v;
+    }
+  };
+  int64_t v0 = tid;
+  // Full strides: no bounds checks.
+  for (; v0 + (kUnroll - 1) * nthreads < nv; v0 += nthreads * kUnroll) {
     float4 q[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t v = v0 + u * nthreads;
-      if (v < nv) q[u] = ld_stream_f4(xa + 4 * v);
-    }
+    for (int u = 0; u < kUnroll; ++u) q[u] = ld_stream_f4(xa + 4 * (v0 + u * nthreads));
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t v = v0 + u * nthreads;
-      if (v < nv) {
-        const long long g = base + head + 4 * v;
-        part_add(p, q[u].x, g);
-        part_add(p, q[u].y, g + 1);
-        part_add(p, q[u].z, g + 2);
-        part_add(p, q[u].w, g + 3);
-      }
-    }
+    for (int u = 0; u < kUnroll; ++u) take4(q[u], v0 + u * nthreads);
+  }
+  for (int64_t v = v0; v < nv; v += nthreads) take4(ld_stream_f4(xa + 4 * v), v);
+  p.s = s;
+  if (vbest >= 0) {
+    const float4 q = ld_stream_f4(xa + 4 * vbest);
+    const int lane = (q.x == m) ? 0 : (q.y == m) ? 1 : (q.z == m) ? 2 : 3;
+    // the element's own bits: fmaxf may have returned +0 for a -0 that comes first
+    p.m = lane == 0 ? q.x : lane == 1 ? q.y : lane == 2 ? q.z : q.w;
+    p.i = base + head + 4 * vbest + lane;
   }
   if (tid == 0)
     for (int64_t i = head + 4 * nv; i < n; ++i) part_add(p, x[i], base + i);

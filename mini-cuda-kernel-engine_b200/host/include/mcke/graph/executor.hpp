@@ -70,6 +70,10 @@ class GraphExecutor {
   [[nodiscard]] Status set_input(TensorId t, const void* host, std::size_t bytes);
   [[nodiscard]] Status run_async();
   [[nodiscard]] Status synchronize();
+  // Device time of the last run_async, in ms: on each device, from an event
+  // recorded before the first node to one recorded after every stream joined;
+  // the maximum over devices.  Synchronises.
+  [[nodiscard]] StatusOr<float> last_run_ms();
   // Gathers a graph output's shards into host memory (whole tensor).
   [[nodiscard]] Status copy_output_to_host(TensorId t, void* host, std::size_t bytes);
 

@@ -135,6 +135,13 @@ int mcke_executor_copy_output(mcke_executor* e, uint32_t t, void* host, size_t b
   EX_CHECK(e);
   return ret(e->ex->copy_output_to_host(t, host, bytes));
 }
+int mcke_executor_last_run_ms(mcke_executor* e, float* ms_out) {
+  EX_CHECK(e);
+  auto r = e->ex->last_run_ms();
+  if (!r.ok()) return ret(r.status());
+  if (ms_out) *ms_out = *r;
+  return 0;
+}
 int mcke_executor_describe(mcke_executor* e, char* buf, size_t len) {
   EX_CHECK(e);
   const std::string s = e->ex->describe();

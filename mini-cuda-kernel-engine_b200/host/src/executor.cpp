@@ -5,7 +5,6 @@
 
 #include <algorithm>
 #include <cstring>
-#include <sstream>
 
 namespace mcke {
 namespace {
@@ -47,10 +46,14 @@ struct GraphExecutor::Impl {
     std::vector<rt::Stream> streams;
     std::vector<rt::Event> node_events;  // indexed by NodeId (only where recorded)
     std::vector<rt::Event> done;         // one per stream: end of the previous run
+    rt::Event t_start, t_end;            // timing events around one run (stream 0)
+    std::vector<rt::Event> exchange_ready;  // per exchanging node: this shard's partial is written
+    std::vector<rt::Event> exchange_done;   // per exchanging node: this device's copies are done
     ncclComm_t comm = nullptr;
   };
   std::vector<Dev> devs;
   bool ran_once = false;
+  bool peer_copy = false;
   ~Impl() {
     for (Dev& d : devs) {
       rt::DeviceGuard g(d.device);
@@ -347,6 +350,12 @@ Status GraphExecutor::plan() {
       MCKE_RETURN_IF_ERROR(ev.status());
       dv.done.push_back(std::move(*ev));
     }
+    auto t0 = rt::Event::create(dv.device, rt::Event::Kind::kTiming);
+    MCKE_RETURN_IF_ERROR(t0.status());
+    dv.t_start = std::move(*t0);
+    auto t1 = rt::Event::create(dv.device, rt::Event::Kind::kTiming);
+    MCKE_RETURN_IF_ERROR(t1.status());
+    dv.t_end = std::move(*t1);
     dv.node_events.resize(g_.num_nodes());
     for (NodeId nid = 0; nid < g_.num_nodes(); ++nid)
       if (record_after_[nid]) {
@@ -355,7 +364,28 @@ Status GraphExecutor::plan() {
         dv.node_events[nid] = std::move(*ev);
       }
   }
+  // NCCL needs distinct devices; a device list that repeats a GPU (several
+  // shards on one GPU) exchanges partials with device-to-device copies ordered
+  // by events instead.
+  std::vector<int> sorted = opts_.devices;
+  std::sort(sorted.begin(), sorted.end());
+  impl_->peer_copy = std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end();
   if (any_exchange && D > 1) {
+    for (auto& dv : impl_->devs) {
+      dv.exchange_ready.resize(g_.num_nodes());
+      dv.exchange_done.resize(g_.num_nodes());
+      for (NodeId nid = 0; nid < g_.num_nodes(); ++nid)
+        if (g_.node(nid).op->exchange_bytes() > 0) {
+          auto ev = rt::Event::create(dv.device);
+          MCKE_RETURN_IF_ERROR(ev.status());
+          dv.exchange_ready[nid] = std::move(*ev);
+          auto ev2 = rt::Event::create(dv.device);
+          MCKE_RETURN_IF_ERROR(ev2.status());
+          dv.exchange_done[nid] = std::move(*ev2);
+        }
+    }
+  }
+  if (any_exchange && D > 1 && !impl_->peer_copy) {
     std::vector<ncclComm_t> comms(D);
     MCKE_RETURN_IF_ERROR(nccl_status(ncclCommInitAll(comms.data(), D, opts_.devices.data()), "ncclCommInitAll"));
     for (int d = 0; d < D; ++d) impl_->devs[d].comm = comms[d];
@@ -385,6 +415,8 @@ Status GraphExecutor::run_async() {
       for (int s = 0; s < S; ++s)
         for (int o = 0; o < S; ++o)
           if (o != s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[o]));
+    MCKE_RETURN_IF_ERROR(dv.t_start.record(dv.streams[0]));
+    for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.t_start));
     if (opts_.poison_buffers) {
       rt::DeviceGuard g(dv.device);
       const int d = static_cast<int>(&dv - impl_->devs.data());
@@ -443,7 +475,29 @@ Status GraphExecutor::run_async() {
     if (eb > 0) {
       std::vector<void*> gathered(D);
       for (int d = 0; d < D; ++d) gathered[d] = static_cast<char*>(ctx[d].exchange) + eb;
-      if (D > 1) {
+      if (D > 1 && impl_->peer_copy) {
+        // Every shard's partial lands in every device's gathered buffer, in
+        // shard order; each copy waits on the event recorded after the partial.
+        for (int d = 0; d < D; ++d)
+          MCKE_RETURN_IF_ERROR(impl_->devs[d].exchange_ready[nid].record(impl_->devs[d].streams[s]));
+        for (int e = 0; e < D; ++e) {
+          auto& de = impl_->devs[e];
+          for (int d = 0; d < D; ++d) {
+            MCKE_RETURN_IF_ERROR(de.streams[s].wait(impl_->devs[d].exchange_ready[nid]));
+            rt::DeviceGuard g(de.device);
+            MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpyPeerAsync(static_cast<char*>(gathered[e]) + d * eb, de.device,
+                                                          ctx[d].exchange, impl_->devs[d].device, eb,
+                                                          de.streams[s].native()));
+          }
+        }
+        // No shard may overwrite its partial (next run) before every peer has
+        // copied it: each device's stream waits for all devices' copies.
+        for (int e = 0; e < D; ++e)
+          MCKE_RETURN_IF_ERROR(impl_->devs[e].exchange_done[nid].record(impl_->devs[e].streams[s]));
+        for (int d = 0; d < D; ++d)
+          for (int e = 0; e < D; ++e)
+            if (e != d) MCKE_RETURN_IF_ERROR(impl_->devs[d].streams[s].wait(impl_->devs[e].exchange_done[nid]));
+      } else if (D > 1) {
         MCKE_RETURN_IF_ERROR(nccl_status(ncclGroupStart(), "ncclGroupStart"));
         for (int d = 0; d < D; ++d) {
           rt::DeviceGuard g(impl_->devs[d].device);
@@ -463,10 +517,25 @@ Status GraphExecutor::run_async() {
     if (record_after_[nid])
       for (auto& dv : impl_->devs) MCKE_RETURN_IF_ERROR(dv.node_events[nid].record(dv.streams[s]));
   }
-  for (auto& dv : impl_->devs)
+  for (auto& dv : impl_->devs) {
     for (int s = 0; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.done[s].record(dv.streams[s]));
+    for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[0].wait(dv.done[s]));
+    MCKE_RETURN_IF_ERROR(dv.t_end.record(dv.streams[0]));
+  }
   impl_->ran_once = true;
   return OkStatus();
+}
+
+StatusOr<float> GraphExecutor::last_run_ms() {
+  if (!impl_ || !impl_->ran_once) return FailedPreconditionError("last_run_ms: nothing has run");
+  float worst = 0.f;
+  for (auto& dv : impl_->devs) {
+    MCKE_RETURN_IF_ERROR(dv.t_end.synchronize());
+    auto ms = rt::Event::elapsed_ms(dv.t_start, dv.t_end);
+    MCKE_RETURN_IF_ERROR(ms.status());
+    worst = std::max(worst, *ms);
+  }
+  return worst;
 }
 
 Status GraphExecutor::synchronize() {
@@ -536,22 +605,25 @@ Status GraphExecutor::copy_output_to_host(TensorId t, void* host, std::size_t by
 }
 
 std::string GraphExecutor::describe() const {
-  std::ostringstream os;
-  os << "devices=" << num_devices() << " streams_per_device=" << opts_.streams_per_device
-     << " cross_stream_events=" << event_edges_ << "\n";
+  // Plain string building (no iostreams): this library is loaded next to other
+  // C++ runtimes in one process, and the description must not depend on their
+  // stream machinery.
+  std::string s = "devices=" + std::to_string(num_devices()) +
+                  " streams_per_device=" + std::to_string(opts_.streams_per_device) +
+                  " cross_stream_events=" + std::to_string(event_edges_) + "\n";
   for (NodeId nid : g_.topo_order()) {
     const Node& n = g_.node(nid);
-    os << "node " << n.name << " (" << n.op->type_name() << ") stream=" << node_stream_[nid] << " waits=[";
-    for (std::size_t i = 0; i < waits_[nid].size(); ++i) os << (i ? "," : "") << g_.node(waits_[nid][i]).name;
-    os << "]\n";
+    s += "node " + n.name + " (" + std::string(n.op->type_name()) + ") stream=" + std::to_string(node_stream_[nid]) +
+         " waits=[";
+    for (std::size_t i = 0; i < waits_[nid].size(); ++i) s += (i ? "," : "") + g_.node(waits_[nid][i]).name;
+    s += "]\n";
   }
-  for (TensorId t = 0; t < g_.num_tensors(); ++t) {
-    os << "tensor " << g_.tensor(t).name << " " << g_.tensor(t).shape.to_string() << " "
-       << placement_name(tplan_[t].placement) << " local0=" << tplan_[t].local_shape[0].to_string()
-       << " offset0=" << tplan_[t].offset[0] << "\n";
-  }
-  for (int d = 0; d < num_devices(); ++d) os << "arena[" << d << "]=" << arena_bytes_[d] << "\n";
-  return os.str();
+  for (TensorId t = 0; t < g_.num_tensors(); ++t)
+    s += "tensor " + g_.tensor(t).name + " " + g_.tensor(t).shape.to_string() + " " +
+         placement_name(tplan_[t].placement) + " local0=" + tplan_[t].local_shape[0].to_string() +
+         " offset0=" + std::to_string(tplan_[t].offset[0]) + "\n";
+  for (int d = 0; d < num_devices(); ++d) s += "arena[" + std::to_string(d) + "]=" + std::to_string(arena_bytes_[d]) + "\n";
+  return s;
 }
 
 }  // namespace mcke

@@ -1,0 +1,131 @@
+"""GraphExecutor on the GPU: the config-5 DAG (fused and unfused), a sharded
+full reduce and a column-split GEMM, against the oracle composed op by op.
+
+A device list may repeat a GPU ([0, 0] = two shards on GPU 0): the sharding
+pass, per-shard arenas and streams, and the event-ordered peer-copy exchange
+of partials then all run on one B200.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover - CPU container
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from mcke import host  # noqa: E402
+
+
+def _dag_inputs(rows, d, f, seed):
+    x = oracle.to_bf16(oracle.fill_normal(rows * d, seed).reshape(rows, d))
+    w1 = oracle.to_bf16(oracle.fill_normal(d * f, seed + 1, 0.0, 0.05).reshape(d, f))
+    b1 = oracle.fill_random(f, seed + 2)
+    w2 = oracle.to_bf16(oracle.fill_normal(f * d, seed + 3, 0.0, 0.05).reshape(f, d))
+    b2 = oracle.fill_random(d, seed + 4)
+    return x, w1, b1, w2, b2
+
+
+def _dag_oracle(x, w1, b1, w2, b2, fused):
+    f32 = oracle.bf16_to_f32
+    lin1 = oracle.gemm(f32(x), f32(w1))
+    if fused:
+        hb = oracle.to_bf16(oracle.bias_act(lin1, b1, "gelu_tanh"))
+    else:
+        hb = oracle.to_bf16(oracle.bias_act(f32(oracle.to_bf16(lin1)), b1, "gelu_tanh"))
+    y = oracle.bias_act(oracle.gemm(f32(hb), f32(w2)), b2, "none")
+    return hb, oracle.row_softmax(y)
+
+
+@pytest.mark.parametrize("fused", [True, False])
+@pytest.mark.parametrize("devices", [[0], [0, 0]])
+def test_dag_matches_oracle(fused, devices):
+    rows, d, f, branches = 256, 128, 256, 2
+    g = host.Graph()
+    x = g.input("X", (rows, d), "bf16", "row_split")
+    data, outs, hs = {}, [], []
+    for i in range(branches):
+        xs = _dag_inputs(rows, d, f, 10 * i + 1)
+        w1 = g.input(f"W1_{i}", (d, f), "bf16")
+        b1 = g.input(f"b1_{i}", (f,), "f32")
+        w2 = g.input(f"W2_{i}", (f, d), "bf16")
+        b2 = g.input(f"b2_{i}", (d,), "f32")
+        data.update({w1: xs[1], b1: xs[2], w2: xs[3], b2: xs[4]})
+        data[x] = _dag_inputs(rows, d, f, 1)[0]
+        if fused:
+            hh = g.gemm(x, w1, bias=b1, act="gelu_tanh", out_dtype="bf16", name=f"gemm1_{i}")
+            y = g.gemm(hh, w2, bias=b2, name=f"gemm2_{i}")
+        else:
+            h0 = g.gemm(x, w1, out_dtype="bf16", name=f"gemm1_{i}")
+            hh = g.bias_act(h0, b1, "gelu_tanh", name=f"bias_gelu_{i}")
+            y = g.bias_act(g.gemm(hh, w2, name=f"gemm2_{i}"), b2, "none", name=f"bias2_{i}")
+        p = g.softmax(y, name=f"softmax_{i}")
+        g.output(p)
+        g.output(hh)
+        outs.append((p, hh, xs))
+    g.finalize()
+    ex = host.Executor(g, devices=devices, streams_per_device=4)
+    ex.plan()
+    for t, arr in data.items():
+        ex.set_input(t, arr)
+    first = None
+    for rep in range(2):
+        ex.run()
+        ex.synchronize()
+        got = [(ex.output(p), ex.output(hh)) for p, hh, _ in outs]
+        if first is None:
+            first = got
+        else:  # replay is bit-identical
+            for (p0, h0), (p1, h1) in zip(first, got):
+                assert np.array_equal(p0.view(np.uint32), p1.view(np.uint32))
+                assert np.array_equal(h0, h1)
+    for (p, hh, xs), (gp, gh) in zip(outs, first):
+        want_h, want_p = _dag_oracle(data[x], xs[1], xs[2], xs[3], xs[4], fused)
+        ulp = np.abs(gh.astype(np.int32) - want_h.astype(np.int32))
+        assert (ulp <= 1).mean() > 0.999 and (ulp == 0).mean() > 0.98
+        r = oracle.compare(gp, want_p, 1e-3, 1e-7)
+        assert r["mismatches"] == 0 and abs(gp.sum(axis=1) - 1).max() < 1e-4, r
+
+
+@pytest.mark.parametrize("devices", [[0], [0, 0, 0]])
+def test_sharded_full_reduce(devices):
+    n = 3_000_007
+    v = oracle.fill_random(n, 5)
+    v[2_999_999] = v[12] = np.float32(1.5)
+    g = host.Graph()
+    x = g.input("v", (n,))
+    r = g.reduce_full(x)
+    g.output(r)
+    g.finalize()
+    ex = host.Executor(g, devices=devices)
+    ex.plan()
+    ex.set_input(x, v)
+    ex.run()
+    import mcke
+    s, m, i = mcke.decode_result(ex.output(r).tobytes())
+    ws, wm, wi = oracle.full_reduce(v)
+    assert (m, i) == (wm, wi) == (1.5, 12)
+    assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))
+
+
+def test_column_split_gemm_f32():
+    m, k, n = 96, 64, 260
+    a = oracle.fill_random(m * k, 1).reshape(m, k)
+    b = oracle.fill_random(k * n, 2).reshape(k, n)
+    g = host.Graph()
+    ta, tb = g.input("A", (m, k)), g.input("B", (k, n))
+    c = g.gemm(ta, tb)
+    g.output(c)
+    g.finalize()
+    ex = host.Executor(g, devices=[0, 0])
+    ex.plan()
+    assert ex.placement(c) == "col_split"
+    ex.set_input(ta, a)
+    ex.set_input(tb, b)
+    ex.run()
+    r = oracle.compare(ex.output(c), oracle.gemm(a, b), oracle.tol_gemm(k), oracle.abs_tol_gemm(k))
+    assert r["mismatches"] == 0, r

@@ -258,6 +258,16 @@ def test_reduce_full_edge_cases(vals, expect):
     assert np.float32(m).view(np.uint32) == np.float32(em).view(np.uint32)
 
 
+def test_reduce_full_signed_zero_tie_in_the_vector_body():
+    # all-negative data with a -0 then a +0 inside one float4: the first (-0) wins
+    x = -np.abs(oracle.fill_random(1 << 16, 4)) - np.float32(1.0)
+    x[4096 + 1] = np.float32(-0.0)
+    x[4096 + 2] = np.float32(0.0)
+    s, m, i = mcke.decode_result(mcke.reduce_full(dev(x)))
+    ws, wm, wi = oracle.full_reduce(x)
+    assert (i, np.float32(m).view(np.uint32)) == (wi, np.float32(wm).view(np.uint32)) == (4097, np.uint32(0x80000000))
+
+
 def test_reduce_sharded_partials_combine_to_the_full_answer():
     n = 1 << 21
     x = oracle.fill_random(n, 3)

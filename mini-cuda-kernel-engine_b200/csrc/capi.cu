@@ -149,7 +149,7 @@ extern "C" int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm
   EpilogueParams ep{1.0f, 0.0f, nullptr, 0, 0, 1};
   if (bf16 && variant != MCKE_GEMM_SIMT) {
     launch_gemm_tcgen05(nullptr, nullptr, nullptr, 0, 0, 0, ep, nullptr, &kernel, &dyn);
-    threads = 192;
+    threads = 320;
   } else if (variant == MCKE_GEMM_TCGEN05) {
     return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands", who);
   } else {

@@ -10,8 +10,8 @@ Headline (``value``): BASELINE config 2, row softmax fp32 over logits
 [32768 x 1024] ~ N(0, 4^2) with every 64th row shifted by +80.  A step is one
 softmax pass over the whole batch, inputs already resident in HBM.  Bytes per
 step are algorithmic, 2 * 32768 * 1024 * 4 = 268,435,456 (one read of x, one
-write of y).  L2 is flushed (a 256 MiB write) between timed steps, outside the
-timed region; each step is timed with CUDA events on the launching stream.
+write of y).  L2 is flushed (a 256 MiB write, then a 256 MiB read, so no dirty lines
+are left to write back) between timed steps, outside the timed region; each step is timed with CUDA events on the launching stream.
 At N GPUs every rank processes its own full batch (weak scaling) and
 ``value`` = N * bytes / (max over ranks of the summed step time).
 
@@ -284,8 +284,15 @@ def run_mcke(args, dist) -> None:
     except Exception:
         pass
 
-    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    flush = lambda: flush_buf.fill_(1)  # noqa: E731
+    # L2 flush between timed steps: write a 256 MiB buffer (twice the 126 MB
+    # L2), then read a second one, so the next step starts with an L2 that
+    # holds none of its data and no dirty lines waiting to be written back.
+    flush_w = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+
+    def flush():
+        flush_w.fill_(1)
+        flush_r.sum()
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(2 + dist.rank)
@@ -318,7 +325,7 @@ def run_mcke(args, dist) -> None:
         ops = {}
         if args.ops:
             ops = run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic)
-    del flush_buf
+    del flush_w, flush_r
 
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": g, "steps": args.steps,
@@ -326,7 +333,7 @@ def run_mcke(args, dist) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (torch.randn * 4 on device, seed 2 + rank; every 64th row +80)",
         "config": {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows_per_gpu": ROWS,
-                   "cols": COLS, "l2": "flushed between timed steps (256 MiB write)",
+                   "cols": COLS, "l2": "flushed between timed steps (256 MiB write, then 256 MiB read)",
                    "parallelism": f"rows, weak scaling, {g} x full batch"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs"),
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),

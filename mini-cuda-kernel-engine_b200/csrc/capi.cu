@@ -43,6 +43,8 @@ int sm_count() {
 }
 
 int read_tc_watchdog(uint32_t* site);
+int read_reduce_watchdog(uint32_t* site);
+int read_softmax_watchdog(uint32_t* site);
 
 namespace {
 
@@ -111,6 +113,12 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site != 0)
     return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u); the kernel stopped early",
                 site);
+  MCKE_RETURN_IF(read_reduce_watchdog(&site));
+  if (site != 0)
+    return fail(MCKE_INTERNAL, "reduce (streamed): a bounded wait expired; the result is incomplete");
+  MCKE_RETURN_IF(read_softmax_watchdog(&site));
+  if (site != 0)
+    return fail(MCKE_INTERNAL, "softmax (streamed): a bounded wait expired; the result is incomplete");
   return MCKE_OK;
 }
 

@@ -80,71 +80,155 @@ __device__ __forceinline__ Part block_combine(Part p, Part* red) {
   return t;
 }
 
+// Pass-1 grid of the streamed kernel: one CTA per 16 KB chunk up to 3 per SM
+// of a B200 (a constant, so the combine tree is the same on any GPU).
+constexpr int64_t kFullCtaCap = 3 * 148;
 int64_t full_blocks(int64_t n) {
-  const int64_t per_block = static_cast<int64_t>(kThreads) * kUnroll * 4;
+  const int64_t per_block = 4096;  // floats per chunk
   int64_t g = (n + per_block - 1) / per_block;
-  if (g > kMaxBlocks) g = kMaxBlocks;
+  if (g > kFullCtaCap) g = kFullCtaCap;
   return g < 1 ? 1 : g;
 }
 
-// Pass 1: each block writes one Part for its grid-strided share of x.
-// Elements before the first 16-byte boundary and after the last whole float4
-// go to global thread 0 (head first, tail last), keeping its visit order
-// increasing.  In the vector body the running maximum is updated once per
-// float4 (its lane maximum against the running one) and only the float4's
-// index is remembered; the lane is resolved once, after the loop, by reloading
-// that float4 and taking its first element equal to the maximum.  A later
-// float4 with an equal maximum never replaces an earlier one, so the lowest
-// index survives, as in the element-wise rule.
-__global__ void __launch_bounds__(kThreads) reduce_full_pass1_kernel(const float* __restrict__ x,
-                                                                     int64_t n, int64_t head,
-                                                                     long long base,
-                                                                     Part* __restrict__ parts) {
+// Pass 1.  Each CTA walks its
+// chunks of 1024 float4 (16 KB; chunk c goes to CTA c mod G) through a 4-stage
+// ring in shared memory filled by bulk asynchronous copies (cp.async.bulk,
+// completion counted on an mbarrier per stage), so a CTA keeps 64 KB of reads
+// in flight with almost no registers and 3 CTAs per SM keep ~190 KB per SM in
+// flight -- enough to stream HBM at full rate.  Threads read their float4s
+// from shared memory in per-thread increasing index order (thread t takes
+// float4 t, t+256, ... of each chunk, chunks in increasing order).  The
+// running maximum is updated once per float4 and only that float4's index is
+// remembered; the lane is resolved after the loop by reloading the float4 and
+// taking its first element equal to the maximum (its own bits, so a -0 ahead
+// of a +0 wins).  A later float4 with an equal maximum never replaces an
+// earlier one, so the lowest index survives.  Head and tail elements (outside
+// whole 16-byte float4s) go to global thread 0: head first, tail last.  Waits on
+// the ring are bounded: on expiry the CTA records the site in a device word
+// (read by mcke_sm100_check_device_errors), waits for the copies it issued,
+// and stops.
+constexpr int kStreamStages = 4;
+constexpr int kChunkVec = 1024;                        // float4 per chunk (16 KB)
+constexpr int64_t kStreamCtas = 3 * 148;               // constant: same combine tree on any GPU
+constexpr std::size_t kStreamSmem = kStreamStages * kChunkVec * 16 + 64;
+constexpr unsigned long long kStreamWaitNs = 2000000000ull;
+
+__device__ uint32_t g_reduce_watchdog;
+
+__device__ __forceinline__ uint32_t s_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool stream_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (it == 0) t0 = t;
+    else if (t - t0 > kStreamWaitNs) return false;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
+                                                                      int64_t head, long long base,
+                                                                      Part* __restrict__ parts) {
+  extern __shared__ __align__(128) uint8_t smem[];
   __shared__ Part red[kWarps];
-  Part p = part_identity();
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * kThreads;
-  if (tid == 0)
-    for (int64_t i = 0; i < head; ++i) part_add(p, x[i], base + i);
+  const float4* ring = reinterpret_cast<const float4*>(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStreamStages * kChunkVec * 16);
+  const int tid = threadIdx.x;
   const float* xa = x + head;
   const int64_t nv = (n - head) / 4;
+  const int64_t nchunks = (nv + kChunkVec - 1) / kChunkVec;
+  const int64_t G = gridDim.x;
+  const int64_t mine = nchunks > static_cast<int64_t>(blockIdx.x) ? (nchunks - blockIdx.x + G - 1) / G : 0;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStreamStages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_addr(full + s)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+
+  auto issue = [&](int64_t i) {  // thread 0: my i-th chunk into stage i % kStreamStages
+    const int64_t v0 = (static_cast<int64_t>(blockIdx.x) + i * G) * kChunkVec;
+    const int64_t cnt = (nv - v0 < kChunkVec) ? nv - v0 : kChunkVec;
+    const uint32_t bytes = static_cast<uint32_t>(cnt * 16);
+    const uint32_t bar = s_addr(full + (i % kStreamStages));
+    const uint32_t dst = s_addr(ring + (i % kStreamStages) * kChunkVec);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(xa + 4 * v0), "r"(bytes), "r"(bar)
+                 : "memory");
+  };
+  if (tid == 0)
+    for (int64_t i = 0; i < mine && i < kStreamStages; ++i) issue(i);
+
+  Part p = part_identity();
+  if (blockIdx.x == 0 && tid == 0)
+    for (int64_t i = 0; i < head; ++i) part_add(p, x[i], base + i);
   double s = p.s;
   float m = p.m;
-  long long vbest = -1;  // float4 index holding the running maximum (pending lane)
+  long long vbest = -1;
   const bool have_index = p.i >= 0;
-  auto take4 = [&](const float4& q, int64_t v) {
-    s += static_cast<double>(q.x);
-    s += static_cast<double>(q.y);
-    s += static_cast<double>(q.z);
-    s += static_cast<double>(q.w);
-    const float lm = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));  // NaN lanes never win
-    if (lm > m || (vbest < 0 && !have_index && lm == m)) {
-      m = lm;
-      vbest = v;
+  bool failed = false;
+  int64_t i = 0;
+  for (; i < mine; ++i) {
+    const int stage = static_cast<int>(i % kStreamStages);
+    const bool ok = stream_wait(s_addr(full + stage), static_cast<uint32_t>((i / kStreamStages) & 1));
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
     }
-  };
-  int64_t v0 = tid;
-  // Full strides: no bounds checks.
-  for (; v0 + (kUnroll - 1) * nthreads < nv; v0 += nthreads * kUnroll) {
-    float4 q[kUnroll];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) q[u] = ld_stream_f4(xa + 4 * (v0 + u * nthreads));
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) take4(q[u], v0 + u * nthreads);
+    const int64_t v0 = (static_cast<int64_t>(blockIdx.x) + i * G) * kChunkVec;
+    const int cnt = static_cast<int>((nv - v0 < kChunkVec) ? nv - v0 : kChunkVec);
+    const float4* buf = ring + stage * kChunkVec;
+#pragma unroll 4
+    for (int j = tid; j < cnt; j += kThreads) {
+      const float4 q = buf[j];
+      s += static_cast<double>(q.x);
+      s += static_cast<double>(q.y);
+      s += static_cast<double>(q.z);
+      s += static_cast<double>(q.w);
+      const float lm = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
+      if (lm > m || (vbest < 0 && !have_index && lm == m)) {
+        m = lm;
+        vbest = v0 + j;
+      }
+    }
+    __syncthreads();  // every thread is done with this stage before it is refilled
+    if (tid == 0 && i + kStreamStages < mine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // reads before the async refill
+      issue(i + kStreamStages);
+    }
   }
-  for (int64_t v = v0; v < nv; v += nthreads) take4(ld_stream_f4(xa + 4 * v), v);
+  if (failed && tid == 0) {
+    atomicCAS(&g_reduce_watchdog, 0u, 1u);
+    // Let the copies already issued land before the CTA exits.
+    for (int64_t k = i; k < mine && k < i + kStreamStages; ++k)
+      stream_wait(s_addr(full + (k % kStreamStages)), static_cast<uint32_t>((k / kStreamStages) & 1));
+  }
   p.s = s;
   if (vbest >= 0) {
     const float4 q = ld_stream_f4(xa + 4 * vbest);
     const int lane = (q.x == m) ? 0 : (q.y == m) ? 1 : (q.z == m) ? 2 : 3;
-    // the element's own bits: fmaxf may have returned +0 for a -0 that comes first
     p.m = lane == 0 ? q.x : lane == 1 ? q.y : lane == 2 ? q.z : q.w;
     p.i = base + head + 4 * vbest + lane;
   }
-  if (tid == 0)
-    for (int64_t i = head + 4 * nv; i < n; ++i) part_add(p, x[i], base + i);
+  if (blockIdx.x == 0 && tid == 0)
+    for (int64_t e = head + 4 * nv; e < n; ++e) part_add(p, x[e], base + e);
   p = block_combine(p, red);
-  if (threadIdx.x == 0) parts[blockIdx.x] = p;
+  if (tid == 0) parts[blockIdx.x] = p;
 }
 
 // Pass 2 (and the cross-shard combine): one block folds `count` Parts in a
@@ -292,6 +376,41 @@ int64_t two_pass_split(int64_t rows, int64_t cols) {
 
 using namespace mcke_sm100;
 
+namespace mcke_sm100 {
+namespace {
+// The streamed pass 1 needs 64 KB of dynamic shared memory: opt in once per device.
+std::mutex g_stream_mu;
+bool g_stream_attr[64] = {};
+int ensure_stream_smem(const char* who) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(MCKE_CUDA_ERROR, "%s: no usable current device", who);
+  std::lock_guard<std::mutex> lk(g_stream_mu);
+  if (!g_stream_attr[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(reduce_full_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kStreamSmem));
+    if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
+    g_stream_attr[dev] = true;
+  }
+  return MCKE_OK;
+}
+}  // namespace
+
+// Reads and clears the streamed reduce's watchdog word on the current device.
+int read_reduce_watchdog(uint32_t* site) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_reduce_watchdog, sizeof(v));
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "reduce watchdog read: %s", cudaGetErrorString(e));
+  if (v != 0) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_reduce_watchdog, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "reduce watchdog clear: %s", cudaGetErrorString(e));
+  }
+  *site = v;
+  return MCKE_OK;
+}
+}  // namespace mcke_sm100
+
 extern "C" size_t mcke_sm100_reduce_full_workspace_bytes(int64_t n) {
   if (n <= 0) return 0;
   return static_cast<size_t>(full_blocks(n)) * sizeof(Part);
@@ -324,7 +443,8 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   Part* parts = static_cast<Part*>(workspace);
-  reduce_full_pass1_kernel<<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, index_base, parts);
+  MCKE_RETURN_IF(ensure_stream_smem(who));
+  reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts);
   MCKE_RETURN_IF(check_launch(who));
   if (final_result) reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   else reduce_full_combine_kernel<false><<<1, 1024, 0, s>>>(parts, g, out);
@@ -495,7 +615,8 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   // array's leftover contents from an earlier call are never read and nothing
   // needs clearing.
   Part* parts = static_cast<Part*>(scratch);
-  reduce_full_pass1_kernel<<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, 0, parts);
+  MCKE_RETURN_IF(ensure_stream_smem(who));
+  reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, 0, parts);
   MCKE_RETURN_IF(check_launch(who));
   reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   return check_launch(who);

@@ -64,7 +64,8 @@ def test_workspace_queries(mcke):
     l = mcke.lib()
     assert l.mcke_sm100_reduce_full_workspace_bytes(0) == 0
     assert l.mcke_sm100_reduce_full_workspace_bytes(1) == 24
-    # the combine grid is capped at 8 blocks x 148 SMs, whatever the device
-    assert l.mcke_sm100_reduce_full_workspace_bytes(1 << 28) == 8 * 148 * 24
+    # the combine grid is capped at 3 CTAs x 148 SMs, whatever the device
+    assert l.mcke_sm100_reduce_full_workspace_bytes(1 << 28) == 3 * 148 * 24
+    assert l.mcke_sm100_reduce_full_workspace_bytes(4096 * 5 + 1) == 6 * 24
     assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 1) == 0
     assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 2) == 64 * 19 * 8

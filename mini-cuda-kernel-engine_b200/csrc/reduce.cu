@@ -109,7 +109,6 @@ int64_t full_blocks(int64_t n) {
 // and stops.
 constexpr int kStreamStages = 4;
 constexpr int kChunkVec = 1024;                        // float4 per chunk (16 KB)
-constexpr int64_t kStreamCtas = 3 * 148;               // constant: same combine tree on any GPU
 constexpr std::size_t kStreamSmem = kStreamStages * kChunkVec * 16 + 64;
 constexpr unsigned long long kStreamWaitNs = 2000000000ull;
 

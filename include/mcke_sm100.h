@@ -102,6 +102,13 @@ const char* mcke_sm100_last_error_string(void);
  * since the last call, else MCKE_INTERNAL with the site in the message. */
 int mcke_sm100_check_device_errors(mcke_stream_t stream);
 
+/* ---- vector add (toolchain smoke test) ------------------------------------ */
+
+/* Replaces kernels.hpp:59 launch_vector_add_f32 (kernels/elementwise.cu:65):
+ * out[i] = a[i] + b[i], one IEEE add per element. */
+int mcke_sm100_vector_add_f32(const float* a, const float* b, float* out, size_t n,
+                              mcke_stream_t stream);
+
 /* ---- bias + activation: y[r][c] = act(x[r][c] + bias[c]) ---------------- */
 
 /* Replaces kernels.hpp:102 launch_bias_act_f32 (kernels/bias_act.cu:269).

@@ -283,3 +283,44 @@ extern "C" int mcke_sm100_bias_act_bf16(const uint16_t* x, const float* bias, ui
   }
   return check_launch(who);
 }
+
+// ---- vector add (toolchain smoke test) -------------------------------------
+// out[i] = a[i] + b[i].  Replaces mini-cuda-kernel-engine kernels/elementwise.cu
+// (launch_vector_add_f32 :65): the reference's first-light kernel, kept so a
+// new machine can be checked end to end with one exact IEEE add per element.
+namespace mcke_sm100 {
+namespace {
+__global__ void __launch_bounds__(kThreads) vector_add_f32_kernel(const float* __restrict__ a,
+                                                                  const float* __restrict__ b,
+                                                                  float* __restrict__ out, int64_t n,
+                                                                  bool vec) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (vec) {
+    for (int64_t i = t; i < n / 4; i += stride) {
+      const float4 x = ld_stream_f4(a + 4 * i), y = ld_stream_f4(b + 4 * i);
+      st_stream_f4(out + 4 * i, make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w));
+    }
+    for (int64_t i = (n / 4) * 4 + t; i < n; i += stride) out[i] = a[i] + b[i];
+  } else {
+    for (int64_t i = t; i < n; i += stride) out[i] = a[i] + b[i];
+  }
+}
+}  // namespace
+}  // namespace mcke_sm100
+
+extern "C" int mcke_sm100_vector_add_f32(const float* a, const float* b, float* out, size_t n,
+                                         mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_vector_add_f32";
+  clear_error();
+  if (n == 0) return MCKE_OK;
+  if (!a || !b || !out) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  const bool vec = aligned(a, 16) && aligned(b, 16) && aligned(out, 16);
+  int64_t blocks = (static_cast<int64_t>(n) / (vec ? 4 : 1) + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  vector_add_f32_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      a, b, out, static_cast<int64_t>(n), vec);
+  return check_launch(who);
+}

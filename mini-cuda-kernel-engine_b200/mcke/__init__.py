@@ -61,6 +61,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_version": (i32, []),
             "mcke_sm100_last_error_string": (ctypes.c_char_p, []),
             "mcke_sm100_check_device_errors": (i32, [vp]),
+            "mcke_sm100_vector_add_f32": (i32, [vp, vp, vp, sz, vp]),
             "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
             "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),
             "mcke_sm100_activation_f32": (i32, [vp, vp, i64, i32, i32, vp]),
@@ -113,6 +114,16 @@ def _need(t: torch.Tensor, dtype, name: str) -> None:
 
 def _act(a) -> int:
     return ACT[a] if isinstance(a, str) else int(a)
+
+
+# ---- vector add ------------------------------------------------------------------
+
+def vector_add(a, b, out=None, stream=None):
+    """out = a + b (float32), the toolchain smoke kernel."""
+    _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
+    out = torch.empty_like(a) if out is None else out
+    _check(lib().mcke_sm100_vector_add_f32(_ptr(a), _ptr(b), _ptr(out), a.numel(), _stream(a, stream)))
+    return out
 
 
 # ---- bias + activation -------------------------------------------------------

@@ -71,6 +71,18 @@ def fixtures():
     return dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "ref_fixtures.npz")))
 
 
+# ----------------------------------------------------------------- vector add
+
+@pytest.mark.parametrize("n", [1, 7, 4096, 1_000_003])
+def test_vector_add_is_one_exact_add(n):
+    a = oracle.fill_random(n + 1, 1, -9, 9)
+    b = oracle.fill_random(n + 1, 2, -9, 9)
+    for off in (0, 1):  # aligned and 4-byte-offset (scalar path) operands
+        ta, tb = dev(a)[off:off + n], dev(b)[off:off + n]
+        got = host(mcke.vector_add(ta, tb))
+        assert np.array_equal(got.view(np.uint32), (a[off:off + n] + b[off:off + n]).view(np.uint32))
+
+
 # ---------------------------------------------------------------- bias + act
 
 def test_bias_act_golden_vectors(vectors):

@@ -358,7 +358,7 @@ def run_mcke(args, dist) -> None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs"),
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs",
-                     "traffic": traffic.get("softmax_warp_row_kernel"),
+                     "traffic": traffic.get("softmax_stream_row_kernel"),
                      "algorithmic_bytes_per_launch": SOFTMAX_BYTES, "kernel_ms": round(kernel_ms, 5)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": SOFTMAX_BYTES // 2,
                 "d2h_bytes_per_step": SOFTMAX_BYTES // 2, "ms_per_step": round(e2e_ms / e2e_steps, 4),
@@ -425,7 +425,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "value": round(REDUCE_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
             "step_ms": round(kms, 5), "collective": "nccl all_gather of 24-byte partials" if g > 1 else None,
-            "traffic": traffic.get("reduce_full_pass1_kernel")}
+            "traffic": traffic.get("reduce_full_stream_kernel")}
         del xr
 
     if "gemm_bf16" in want:

@@ -101,6 +101,12 @@ const char* mcke_sm100_last_error_string(void);
  * the current device: 0 if no kernel of this library gave up on a bounded wait
  * since the last call, else MCKE_INTERNAL with the site in the message. */
 int mcke_sm100_check_device_errors(mcke_stream_t stream);
+/* Diagnostic with no counterpart in the reference: enqueues a one-thread kernel
+ * that waits on a barrier nothing arrives on, so its bounded wait (2 s) expires
+ * and records itself; the next mcke_sm100_check_device_errors() then returns
+ * MCKE_INTERNAL naming site 6, and the context stays usable.  For testing the
+ * failure path of the library's bounded waits without faulting a GPU. */
+int mcke_sm100_watchdog_selftest(mcke_stream_t stream);
 
 /* ---- vector add (toolchain smoke test) ------------------------------------ */
 

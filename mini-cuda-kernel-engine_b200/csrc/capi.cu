@@ -43,6 +43,7 @@ int sm_count() {
 }
 
 int read_tc_watchdog(uint32_t* site);
+int launch_watchdog_selftest(cudaStream_t s);
 int read_reduce_watchdog(uint32_t* site);
 int read_softmax_watchdog(uint32_t* site);
 
@@ -120,6 +121,12 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site != 0)
     return fail(MCKE_INTERNAL, "softmax (streamed): a bounded wait expired; the result is incomplete");
   return MCKE_OK;
+}
+
+extern "C" int mcke_sm100_watchdog_selftest(mcke_stream_t stream) {
+  clear_error();
+  MCKE_RETURN_IF(launch_watchdog_selftest(reinterpret_cast<cudaStream_t>(stream)));
+  return check_launch("mcke_sm100_watchdog_selftest");
 }
 
 extern "C" int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int64_t n,

@@ -697,6 +697,27 @@ int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m
   return MCKE_OK;
 }
 
+namespace {
+// Watchdog self-test: one thread waits on an mbarrier that nothing arrives on.
+// The bounded wait gives up after its limit, records kSiteSelfTest and the
+// kernel returns normally, so the context stays usable.
+constexpr uint32_t kSiteSelfTest = 6;
+__global__ void watchdog_selftest_kernel() {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t abort_word;
+  if (threadIdx.x != 0) return;
+  abort_word = 0u;
+  mbar_init(smem_u32(&bar), 1);
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  wait_bounded(smem_u32(&bar), 0u, &abort_word, kSiteSelfTest, false);
+}
+}  // namespace
+
+int launch_watchdog_selftest(cudaStream_t s) {
+  watchdog_selftest_kernel<<<1, 32, 0, s>>>();
+  return MCKE_OK;
+}
+
 int read_tc_watchdog(uint32_t* site) {
   uint32_t v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_watchdog, sizeof(v));

@@ -61,6 +61,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_version": (i32, []),
             "mcke_sm100_last_error_string": (ctypes.c_char_p, []),
             "mcke_sm100_check_device_errors": (i32, [vp]),
+            "mcke_sm100_watchdog_selftest": (i32, [vp]),
             "mcke_sm100_vector_add_f32": (i32, [vp, vp, vp, sz, vp]),
             "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
             "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),

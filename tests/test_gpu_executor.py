@@ -129,3 +129,54 @@ def test_column_split_gemm_f32():
     ex.run()
     r = oracle.compare(ex.output(c), oracle.gemm(a, b), oracle.tol_gemm(k), oracle.abs_tol_gemm(k))
     assert r["mismatches"] == 0, r
+
+
+two_gpus = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+
+
+@two_gpus
+def test_dag_on_two_gpus_matches_one():
+    rows, d, f = 256, 128, 256
+    outs = []
+    for devices in ([0], [0, 1]):
+        g = host.Graph()
+        x = g.input("X", (rows, d), "bf16", "row_split")
+        xs = _dag_inputs(rows, d, f, 3)
+        w1, b1 = g.input("W1", (d, f), "bf16"), g.input("b1", (f,), "f32")
+        w2, b2 = g.input("W2", (f, d), "bf16"), g.input("b2", (d,), "f32")
+        hh = g.gemm(x, w1, bias=b1, act="gelu_tanh", out_dtype="bf16")
+        p = g.softmax(g.gemm(hh, w2, bias=b2))
+        g.output(p)
+        g.finalize()
+        ex = host.Executor(g, devices=devices)
+        ex.plan()
+        for t, arr in zip((x, w1, b1, w2, b2), xs):
+            ex.set_input(t, arr)
+        ex.run()
+        outs.append(ex.output(p))
+    # one GPU runs the 256 rows as one 2-CTA tile, two GPUs as 128-row tiles:
+    # the same K-order accumulation, so agreement to a few fp32 ulp
+    r = oracle.compare(outs[1], outs[0], 1e-5, 1e-9)
+    assert r["mismatches"] == 0, r
+
+
+@two_gpus
+def test_nccl_sharded_full_reduce_on_two_gpus():
+    n = 2_000_003
+    v = oracle.fill_random(n, 8)
+    v[1_999_990] = v[40] = np.float32(1.75)
+    g = host.Graph()
+    x = g.input("v", (n,))
+    r = g.reduce_full(x)
+    g.output(r)
+    g.finalize()
+    ex = host.Executor(g, devices=[0, 1])
+    ex.plan()
+    ex.set_input(x, v)
+    for _ in range(2):
+        ex.run()
+        import mcke
+        s, m, i = mcke.decode_result(ex.output(r).tobytes())
+        assert (m, i) == (1.75, 40)
+        ws = oracle.full_reduce(v)[0]
+        assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))

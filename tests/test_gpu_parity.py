@@ -470,3 +470,19 @@ def test_gemm_kernel_attrs_report_no_spills():
         at = mcke.gemm_kernel_attrs(variant, dt)
         assert at["local_bytes"] == 0 and at["regs_per_thread"] > 0, (variant, at)
         assert at["max_blocks_per_sm_api"] >= 1
+
+
+# ------------------------------------------------------------ failure path
+
+def test_bounded_wait_expiry_is_reported_and_the_context_survives():
+    # A wait on a barrier nothing arrives on gives up after its 2 s limit; the
+    # host reads the status, and the next kernels run normally.
+    mcke.check_device_errors()  # start clean
+    s = torch.cuda.current_stream().cuda_stream
+    assert mcke.lib().mcke_sm100_watchdog_selftest(s) == mcke.OK
+    with pytest.raises(mcke.MckeError) as e:
+        mcke.check_device_errors()
+    assert e.value.code == mcke.INTERNAL and "site 6" in e.value.message
+    mcke.check_device_errors()  # the word was cleared
+    x = dev(oracle.fill_random(4096, 3))
+    assert mcke.decode_result(mcke.reduce_full(x))[2] == int(np.argmax(host(x)))

@@ -412,19 +412,33 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         ws = torch.empty(mcke.reduce_full_workspace_bytes(r1 - r0), dtype=torch.uint8, device=dev)
         res = torch.empty(16, dtype=torch.uint8, device=dev)
         part = torch.empty(24, dtype=torch.uint8, device=dev)
+        nccl_ms = None
+        p2p = None
         if g == 1:
             launch = lambda: mcke.reduce_full(xr, out=res, workspace=ws)  # noqa: E731
         else:
-            def launch():
+            # the NCCL all-gather of partials, timed for comparison; the
+            # reported number uses the peer-to-peer combine kernel
+            def launch_nccl():
                 mcke.reduce_full_partial(xr, r0, out=part, workspace=ws)
                 mcke.reduce_combine(mshard.exchange_partials(part, g), g, out=res)
+            ms_n, _ = timed_steps(torch, dist, launch_nccl, steps, warm, flush)
+            nccl_ms = ms_n / steps
+            p2p = mshard.P2PExchange(dev)
+            launch = lambda: p2p.reduce_full(xr, r0, out=res, workspace=ws)  # noqa: E731
         ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
         kms = statistics.mean(per)
         ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9
+        if p2p is not None:
+            torch.cuda.synchronize()
+            mcke.check_device_errors()
+            p2p.close()
         out["reduce_full_fp32_2^28"] = {
             "value": round(REDUCE_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "step_ms": round(kms, 5), "collective": "nccl all_gather of 24-byte partials" if g > 1 else None,
+            "step_ms": round(kms, 5),
+            "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
+            "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
             "traffic": traffic.get("reduce_full_stream_kernel")}
         del xr
 
@@ -506,6 +520,60 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                     "; 4 branches on 4 streams of the C++ GraphExecutor, timed by its fork/join events"}
         del ex, gr
 
+    if "dag_fanout" in want:
+        # The reference graph bench's fan-out (4 branches x 4 bias+GELU nodes,
+        # 2048x2048 fp32, per GPU): eager enqueue against CUDA-graph replay.
+        from mcke import host as mhost
+        fb, fd, fr, fc = 4, 4, 2048, 2048
+        cpu = torch.Generator()
+        cpu.manual_seed(7)
+        modes = {}
+        for mode in ("eager", "graph"):
+            gr = mhost.Graph()
+            x = gr.input("x", (fr, fc))
+            feeds = {x: torch.randn(fr, fc, generator=cpu).numpy()}
+            for b in range(fb):
+                h = x
+                for k in range(fd):
+                    bias = gr.input(f"b{b}_{k}", (fc,))
+                    feeds[bias] = (torch.rand(fc, generator=cpu) * 2 - 1).numpy()
+                    h = gr.bias_act(h, bias, "gelu_tanh", name=f"bias_gelu_{b}_{k}")
+                gr.output(h)
+            gr.finalize()
+            ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=(mode == "graph"))
+            ex.plan()
+            for t, arr in feeds.items():
+                ex.set_input(t, arr)
+            for _ in range(warm):
+                ex.run()
+            ex.synchronize()
+            dist.barrier(torch)
+            runs = 50
+            dev_ms, enq = 0.0, 0.0
+            for _ in range(runs):  # one run at a time: device time and host enqueue time
+                t0 = time.perf_counter()
+                ex.run()
+                enq += time.perf_counter() - t0
+                dev_ms += ex.last_run_ms()
+            ex.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(runs):  # back to back: does the host keep up?
+                ex.run()
+            ex.synchronize()
+            wall = (time.perf_counter() - t0) / runs * 1e3
+            dist.barrier(torch)
+            modes[mode] = {"device_ms_per_run": round(dist.max(torch, dev_ms / runs), 4),
+                           "host_enqueue_us_per_run": round(enq / runs * 1e6, 1),
+                           "back_to_back_ms_per_run": round(dist.max(torch, wall), 4)}
+            del ex, gr
+        moved = fb * fd * (2 * fr * fc + fc) * 4
+        gms = modes["graph"]["device_ms_per_run"]
+        out["dag_fanout_4x4_2048x2048_f32"] = {
+            "value": round(moved * g / (gms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "weak",
+            "algorithmic_bytes_per_gpu": moved, "eager": modes["eager"], "graph": modes["graph"],
+            "note": "16 bias+GELU nodes on 4 streams of the C++ GraphExecutor; value from the CUDA-graph replay's "
+                    "device time (events around each launch, max over ranks); back_to_back is host wall clock"}
+
     if "gemm_f32" in want:
         n0, n1 = shard(GEMM_N)
         gen = torch.Generator(device=dev)
@@ -579,7 +647,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mcke", "reference"], default="mcke")
-    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,dag_fused,dag_unfused,gemm_f32",
+    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,dag_fused,dag_unfused,dag_fanout,gemm_f32",
                     help="comma list of extra configs to report under 'ops' ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default="", help="run one small case per named kernel for ncu and exit")

@@ -54,6 +54,14 @@ int mcke_graph_finalize(mcke_graph* g);
 
 /* GraphExecutor (executor.hpp:283) over `num_devices` GPUs. */
 mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device);
+/* As mcke_executor_create, with option flags:
+ *   MCKE_EXECUTOR_CUDA_GRAPH  capture the first run into one CUDA graph per GPU
+ *                             and replay it (devices all distinct or one GPU repeated);
+ *   MCKE_EXECUTOR_POISON      fill intermediates with 0xFF before each run (tests). */
+#define MCKE_EXECUTOR_CUDA_GRAPH 1u
+#define MCKE_EXECUTOR_POISON 2u
+mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
+                                       unsigned flags);
 void mcke_executor_destroy(mcke_executor* e);
 /* Planning only (placement, streams, memory): touches no GPU. */
 int mcke_executor_plan_dry(mcke_executor* e);

@@ -1,6 +1,6 @@
 /*
  * mcke_sm100.h -- C-ABI of libmcke_sm100a.so, the B200 (sm_100a) kernel library
- * that replaces mini-cuda-kernel-engine's kernel layer (its kernels/*.cu).
+ * that replaces mini-cuda-kernel-engine's kernel layer (the .cu files of its kernels/ directory).
  *
  * Every entry point is a plain C function over caller-owned device pointers,
  * int64 extents and enum ints, enqueued on an explicit CUDA stream.  None
@@ -169,6 +169,28 @@ int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_
 /* Combines `count` partials (device memory, shard order) into one result. */
 int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count,
                               mcke_reduce_result* out, mcke_stream_t stream);
+/* New (sharded full reduce, one process per GPU): this rank reduces its shard
+ * x[0..n) (global index of x[0] = index_base), stores its 24-byte partial into
+ * slot `rank` of every rank's exchange buffer over peer memory, waits (bounded,
+ * 1 s) for all ranks' slots in its own buffer and writes the combined result,
+ * folded in rank order.  peer_buffers: DEVICE array of `world` pointers to the
+ * ranks' exchange buffers as mapped in this process (this rank's own at index
+ * `rank`), each mcke_sm100_reduce_p2p_buffer_bytes(world) bytes, zeroed before
+ * first use.  epoch: 1, 2, 3, ... one per call, the same on every rank.  Every
+ * rank must make the call for each epoch; a rank that does not arrive makes the
+ * others give up after 1 s with argmax -1 and MCKE_INTERNAL from
+ * mcke_sm100_check_device_errors().  Workspace as for mcke_sm100_reduce_full_f32. */
+size_t mcke_sm100_reduce_p2p_buffer_bytes(int world);
+int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
+                                   void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                   mcke_reduce_result* out, void* workspace, size_t workspace_bytes,
+                                   mcke_stream_t stream);
+/* Set-up helpers for exchange buffers shared between processes (CUDA IPC).
+ * create: cudaMalloc + zero + IPC handle (64 bytes written to handle_out);
+ * open: map a peer's handle in this process; close: unmap (opened = 1) or free. */
+int mcke_sm100_ipc_buffer_create(size_t bytes, void** dev_ptr, void* handle_out);
+int mcke_sm100_ipc_buffer_open(const void* handle, void** dev_ptr);
+int mcke_sm100_ipc_buffer_close(void* dev_ptr, int opened);
 /* No counterpart in the reference.  mcke_sm100_reduce_full_f32 for callers that
  * cannot allocate device memory -- for example a host runtime whose memory
  * manager owns every device allocation, or a foreign-language binding that

@@ -115,6 +115,8 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
     return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u); the kernel stopped early",
                 site);
   MCKE_RETURN_IF(read_reduce_watchdog(&site));
+  if (site == 2)
+    return fail(MCKE_INTERNAL, "reduce (p2p exchange): a peer's partial did not arrive within 1 s; the result is incomplete");
   if (site != 0)
     return fail(MCKE_INTERNAL, "reduce (streamed): a bounded wait expired; the result is incomplete");
   MCKE_RETURN_IF(read_softmax_watchdog(&site));

@@ -16,6 +16,7 @@
 // index holding the maximum; each thread visits its elements in increasing
 // index order and the combine breaks value ties by index.
 #include <cfloat>
+#include <cstring>
 #include <mutex>
 
 #include "mcke_common.cuh"
@@ -619,4 +620,172 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   MCKE_RETURN_IF(check_launch(who));
   reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   return check_launch(who);
+}
+
+// ---- sharded full reduce with a peer-to-peer one-shot combine ----------------
+//
+// For one process per GPU: instead of an all-gather through a collective
+// library, each rank's combine kernel folds its own pass-1 partials into the
+// shard partial, stores it into slot `rank` of every rank's exchange buffer
+// (peer memory over NVLink, plain stores), publishes it with an epoch flag,
+// waits (bounded) until every rank's slot in its own buffer carries the same
+// epoch, and folds the slots in rank order.  Slots are double-buffered by
+// epoch parity: a rank can run at most one epoch ahead of any peer that is
+// still reading, so the two halves never collide.  Exchange buffers are
+// created and shared across processes with the CUDA IPC helpers below
+// (set-up time; the entry point itself allocates nothing).
+namespace mcke_sm100 {
+namespace {
+
+struct Slot {
+  Part p;
+  unsigned long long epoch;
+};
+static_assert(sizeof(Slot) == 32, "slot layout");
+constexpr unsigned long long kP2pWaitNs = 1000000000ull;
+
+__global__ void __launch_bounds__(1024) reduce_exchange_p2p_kernel(const Part* __restrict__ parts, int64_t count,
+                                                                   Slot* const* __restrict__ peers, int world,
+                                                                   int rank, unsigned long long epoch,
+                                                                   mcke_reduce_result* __restrict__ out) {
+  __shared__ Part red[32];
+  __shared__ Part mine;
+  __shared__ int all_ok;
+  Part p = part_identity();
+  for (int64_t j = threadIdx.x; j < count; j += blockDim.x) p = part_combine(p, parts[j]);
+  p = block_combine(p, red);
+  if (threadIdx.x == 0) {
+    mine = p;
+    all_ok = 1;
+  }
+  __syncthreads();
+  const int half = static_cast<int>(epoch & 1ull) * world;
+  if (static_cast<int>(threadIdx.x) < world) {
+    Slot* dst = peers[threadIdx.x] + half + rank;
+    volatile Part* vp = &dst->p;
+    vp->s = mine.s;
+    vp->m = mine.m;
+    vp->reserved = 0;
+    vp->i = mine.i;
+    __threadfence_system();  // the partial is visible before its flag
+    *reinterpret_cast<volatile unsigned long long*>(&dst->epoch) = epoch;
+  }
+  // Wait for every rank's slot in this rank's own buffer.
+  if (static_cast<int>(threadIdx.x) < world) {
+    volatile unsigned long long* flag = &(peers[rank] + half + threadIdx.x)->epoch;
+    unsigned long long t0 = 0;
+    bool ok = false;
+    for (uint32_t it = 0;; ++it) {
+      if (*flag == epoch) {
+        ok = true;
+        break;
+      }
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > kP2pWaitNs) break;
+    }
+    if (!ok) {
+      all_ok = 0;
+      atomicCAS(&g_reduce_watchdog, 0u, 2u);
+    }
+    __threadfence_system();  // slot contents after the flag
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Part t = part_identity();
+    if (all_ok) {
+      for (int r = 0; r < world; ++r) {
+        const volatile Part* sp = &(peers[rank] + half + r)->p;
+        Part q;
+        q.s = sp->s;
+        q.m = sp->m;
+        q.reserved = 0;
+        q.i = sp->i;
+        t = part_combine(t, q);
+      }
+    }
+    mcke_reduce_result res;
+    res.sum = static_cast<float>(t.s);
+    res.max = t.m;
+    res.argmax = all_ok ? t.i : -1;
+    *out = res;
+  }
+}
+
+}  // namespace
+}  // namespace mcke_sm100
+
+extern "C" size_t mcke_sm100_reduce_p2p_buffer_bytes(int world) {
+  return world > 0 ? static_cast<size_t>(2 * world) * sizeof(Slot) : 0;
+}
+
+extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
+                                              void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                              mcke_reduce_result* out, void* workspace, size_t workspace_bytes,
+                                              mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_full_p2p_f32";
+  clear_error();
+  if (!out || !peer_buffers) return fail(MCKE_INVALID_ARGUMENT, "%s: null output or peer table", who);
+  if (world < 1 || world > 1024 || rank < 0 || rank >= world)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: bad world/rank %d/%d", who, world, rank);
+  if (epoch == 0) return fail(MCKE_INVALID_ARGUMENT, "%s: epoch must start at 1 (0 marks an empty slot)", who);
+  if (n < 0 || (n > 0 && !x)) return fail(MCKE_INVALID_ARGUMENT, "%s: bad input", who);
+  if (index_base < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative index_base", who);
+  if (n > 0 && !aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
+  const size_t need = n > 0 ? mcke_sm100_reduce_full_workspace_bytes(n) : 0;
+  if (n > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 16)))
+    return fail(MCKE_INVALID_ARGUMENT, "%s: needs %zu bytes of 16-byte aligned workspace", who, need);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int64_t g = 0;
+  Part* parts = static_cast<Part*>(workspace);
+  if (n > 0) {
+    g = full_blocks(n);
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+    int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
+    if (head > n) head = n;
+    MCKE_RETURN_IF(ensure_stream_smem(who));
+    reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts);
+    MCKE_RETURN_IF(check_launch(who));
+  }
+  reduce_exchange_p2p_kernel<<<1, 1024, 0, s>>>(parts, g, reinterpret_cast<Slot* const*>(peer_buffers), world, rank,
+                                                 static_cast<unsigned long long>(epoch), out);
+  return check_launch(who);
+}
+
+// ---- CUDA IPC set-up helpers for the exchange buffers ---------------------------
+
+extern "C" int mcke_sm100_ipc_buffer_create(size_t bytes, void** dev_ptr, void* handle_out) {
+  static const char* who = "mcke_sm100_ipc_buffer_create";
+  clear_error();
+  if (!dev_ptr || !handle_out || bytes == 0) return fail(MCKE_INVALID_ARGUMENT, "%s: bad argument", who);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(MCKE_OUT_OF_MEMORY, "%s: cudaMalloc: %s", who, cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
+  }
+  *dev_ptr = p;
+  return MCKE_OK;
+}
+
+extern "C" int mcke_sm100_ipc_buffer_open(const void* handle, void** dev_ptr) {
+  static const char* who = "mcke_sm100_ipc_buffer_open";
+  clear_error();
+  if (!handle || !dev_ptr) return fail(MCKE_INVALID_ARGUMENT, "%s: bad argument", who);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
+  return MCKE_OK;
+}
+
+extern "C" int mcke_sm100_ipc_buffer_close(void* dev_ptr, int opened) {
+  clear_error();
+  const cudaError_t e = opened ? cudaIpcCloseMemHandle(dev_ptr) : cudaFree(dev_ptr);
+  if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "mcke_sm100_ipc_buffer_close: %s", cudaGetErrorString(e));
+  return MCKE_OK;
 }

@@ -27,6 +27,13 @@
 //           4. allocation (one cudaMalloc per device), NCCL communicators
 //              (only if some node exchanges), streams and events.
 //   run_async()  enqueues every node on every device; never synchronises.
+//              With ExecutorOptions::use_graph the first call captures that
+//              enqueue into one CUDA graph per GPU (stream capture from each
+//              device's stream 0, forked to its other streams by events; the
+//              NCCL exchange is captured with it) and launches it; later calls
+//              only launch the instantiated graphs: one host call per GPU
+//              instead of one per node and event.  Pointers are fixed at plan
+//              time (arena offsets), so a replay reads the current inputs.
 //
 // plan_dry() runs steps 1-3 without touching CUDA, for tests on a host with
 // no GPU.
@@ -45,6 +52,9 @@ struct ExecutorOptions {
   std::vector<int> devices{0};
   int streams_per_device = 4;
   bool poison_buffers = false;  // fill intermediates with 0xFF before each run
+  // Capture the first run_async into CUDA graphs and replay them.  Needs a
+  // device list that is all distinct GPUs or one GPU repeated.
+  bool use_graph = false;
 };
 
 struct TensorPlan {
@@ -90,6 +100,8 @@ class GraphExecutor {
   [[nodiscard]] Status assign_streams();
   [[nodiscard]] Status plan_memory();
   [[nodiscard]] Tensor local_tensor(TensorId t, int d) const;
+  [[nodiscard]] Status enqueue(bool capturing);
+  [[nodiscard]] Status capture();
 
   Graph& g_;
   ExecutorOptions opts_;

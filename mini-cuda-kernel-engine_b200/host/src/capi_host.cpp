@@ -105,14 +105,21 @@ int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint
 int mcke_graph_mark_output(mcke_graph* g, uint32_t t) { return g ? ret(g->g.mark_output(t)) : 2; }
 int mcke_graph_finalize(mcke_graph* g) { return g ? ret(g->g.finalize()) : 2; }
 
-mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device) {
+mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
+                                       unsigned flags) {
   if (!g || !devices || num_devices < 1) return nullptr;
   mcke::ExecutorOptions o;
   o.devices.assign(devices, devices + num_devices);
   o.streams_per_device = streams_per_device > 0 ? streams_per_device : 4;
+  o.use_graph = (flags & MCKE_EXECUTOR_CUDA_GRAPH) != 0;
+  o.poison_buffers = (flags & MCKE_EXECUTOR_POISON) != 0;
   auto* e = new mcke_executor();
   e->ex = std::make_unique<mcke::GraphExecutor>(g->g, o);
   return e;
+}
+
+mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device) {
+  return mcke_executor_create_ex(g, devices, num_devices, streams_per_device, 0);
 }
 
 void mcke_executor_destroy(mcke_executor* e) { delete e; }

@@ -49,12 +49,21 @@ struct GraphExecutor::Impl {
     rt::Event t_start, t_end;            // timing events around one run (stream 0)
     std::vector<rt::Event> exchange_ready;  // per exchanging node: this shard's partial is written
     std::vector<rt::Event> exchange_done;   // per exchanging node: this device's copies are done
+    rt::Event fork, join;                // graph capture: fan-out from / back to the origin stream
     ncclComm_t comm = nullptr;
   };
   std::vector<Dev> devs;
   bool ran_once = false;
   bool peer_copy = false;
+  // Graph mode: one instantiated graph per capture group (a GPU); origin[i] is
+  // the device entry whose stream 0 launches execs[i] and carries its timing.
+  std::vector<cudaGraphExec_t> execs;
+  std::vector<int> origins;
   ~Impl() {
+    for (std::size_t i = 0; i < execs.size(); ++i) {
+      rt::DeviceGuard g(devs[origins[i]].device);
+      cudaGraphExecDestroy(execs[i]);
+    }
     for (Dev& d : devs) {
       rt::DeviceGuard g(d.device);
       if (d.comm) ncclCommDestroy(d.comm);
@@ -350,6 +359,14 @@ Status GraphExecutor::plan() {
       MCKE_RETURN_IF_ERROR(ev.status());
       dv.done.push_back(std::move(*ev));
     }
+    if (opts_.use_graph) {
+      auto f = rt::Event::create(dv.device);
+      MCKE_RETURN_IF_ERROR(f.status());
+      dv.fork = std::move(*f);
+      auto j = rt::Event::create(dv.device);
+      MCKE_RETURN_IF_ERROR(j.status());
+      dv.join = std::move(*j);
+    }
     auto t0 = rt::Event::create(dv.device, rt::Event::Kind::kTiming);
     MCKE_RETURN_IF_ERROR(t0.status());
     dv.t_start = std::move(*t0);
@@ -406,12 +423,126 @@ Tensor GraphExecutor::local_tensor(TensorId t, int d) const {
 
 Status GraphExecutor::run_async() {
   if (!planned_) return FailedPreconditionError("run_async: plan() has not succeeded");
+  if (!opts_.use_graph) {
+    MCKE_RETURN_IF_ERROR(enqueue(false));
+    impl_->ran_once = true;
+    return OkStatus();
+  }
+  if (impl_->execs.empty()) MCKE_RETURN_IF_ERROR(capture());
+  // Stream order on each origin stream serialises replays, so a replay never
+  // overwrites a block that the previous one is still reading.
+  for (std::size_t i = 0; i < impl_->execs.size(); ++i) {
+    auto& dv = impl_->devs[impl_->origins[i]];
+    rt::DeviceGuard g(dv.device);
+    MCKE_RETURN_IF_ERROR(dv.t_start.record(dv.streams[0]));
+    MCKE_CUDA_RETURN_IF_ERROR(cudaGraphLaunch(impl_->execs[i], dv.streams[0].native()));
+    MCKE_RETURN_IF_ERROR(dv.t_end.record(dv.streams[0]));
+  }
+  return OkStatus();
+}
+
+Status GraphExecutor::capture() {
+  const int D = num_devices();
+  const int S = std::max(1, opts_.streams_per_device);
+  std::vector<std::vector<int>> groups;
+  if (D > 1 && impl_->peer_copy) {
+    // Repeated GPUs exchange with event-ordered copies between the entries:
+    // that only captures when every entry is on one GPU (one capture).
+    for (int d = 1; d < D; ++d)
+      if (impl_->devs[d].device != impl_->devs[0].device)
+        return InvalidArgumentError("use_graph: the device list must be distinct GPUs or one GPU repeated");
+    groups.emplace_back();
+    for (int d = 0; d < D; ++d) groups[0].push_back(d);
+  } else {
+    for (int d = 0; d < D; ++d) groups.push_back({d});
+  }
+  // Every group's capture is open before any node is enqueued: the NCCL
+  // exchange of a sharded reduce is one group call over all GPUs.
+  std::vector<int> begun;
+  auto abort_captures = [&](Status st) {
+    for (int gi : begun) {
+      auto& o = impl_->devs[groups[gi][0]];
+      rt::DeviceGuard g(o.device);
+      cudaGraph_t partial = nullptr;
+      cudaStreamEndCapture(o.streams[0].native(), &partial);
+      if (partial) cudaGraphDestroy(partial);
+    }
+    cudaGetLastError();
+    return st;
+  };
+  for (std::size_t gi = 0; gi < groups.size(); ++gi) {
+    auto& o = impl_->devs[groups[gi][0]];
+    rt::DeviceGuard g(o.device);
+    cudaError_t e = cudaStreamBeginCapture(o.streams[0].native(), cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) return abort_captures(InternalError(std::string("cudaStreamBeginCapture: ") + cudaGetErrorString(e)));
+    begun.push_back(static_cast<int>(gi));
+    Status st = o.fork.record(o.streams[0]);
+    for (int d : groups[gi])
+      for (int s = 0; s < S && st.ok(); ++s)
+        if (d != groups[gi][0] || s != 0) st = impl_->devs[d].streams[s].wait(o.fork);
+    if (!st.ok()) return abort_captures(st);
+  }
+  Status st = enqueue(true);
+  if (!st.ok()) return abort_captures(st);
+  for (auto& grp : groups) {
+    auto& o = impl_->devs[grp[0]];
+    for (std::size_t k = 1; k < grp.size() && st.ok(); ++k) {
+      auto& dv = impl_->devs[grp[k]];
+      st = dv.join.record(dv.streams[0]);
+      if (st.ok()) st = o.streams[0].wait(dv.join);
+    }
+    if (!st.ok()) return abort_captures(st);
+  }
+  std::vector<cudaGraph_t> graphs;
+  for (int gi : begun) {
+    auto& o = impl_->devs[groups[gi][0]];
+    rt::DeviceGuard g(o.device);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(o.streams[0].native(), &graph);
+    if (e != cudaSuccess || !graph) {
+      st = InternalError(std::string("cudaStreamEndCapture: ") + cudaGetErrorString(e));
+      break;
+    }
+    graphs.push_back(graph);
+  }
+  if (st.ok()) {
+    for (std::size_t gi = 0; gi < graphs.size(); ++gi) {
+      rt::DeviceGuard g(impl_->devs[groups[gi][0]].device);
+      cudaGraphExec_t exec = nullptr;
+      const cudaError_t e = cudaGraphInstantiate(&exec, graphs[gi], 0);
+      if (e != cudaSuccess) {
+        st = InternalError(std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
+        break;
+      }
+      impl_->execs.push_back(exec);
+      impl_->origins.push_back(groups[gi][0]);
+    }
+  }
+  for (std::size_t gi = 0; gi < graphs.size(); ++gi) {
+    rt::DeviceGuard g(impl_->devs[groups[gi][0]].device);
+    cudaGraphDestroy(graphs[gi]);
+  }
+  if (!st.ok()) {
+    for (std::size_t i = 0; i < impl_->execs.size(); ++i) {
+      rt::DeviceGuard g(impl_->devs[impl_->origins[i]].device);
+      cudaGraphExecDestroy(impl_->execs[i]);
+    }
+    impl_->execs.clear();
+    impl_->origins.clear();
+    cudaGetLastError();
+  }
+  return st;
+}
+
+Status GraphExecutor::enqueue(bool capturing) {
   const int D = num_devices();
   const int S = std::max(1, opts_.streams_per_device);
   // Each run starts after every stream of the previous run finished (join),
   // so a reused block is never overwritten while a reader is still running.
+  // (A captured run needs no such wait: graph launches on one stream are
+  // ordered.)
   for (auto& dv : impl_->devs) {
-    if (impl_->ran_once)
+    if (impl_->ran_once && !capturing)
       for (int s = 0; s < S; ++s)
         for (int o = 0; o < S; ++o)
           if (o != s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[o]));
@@ -522,14 +653,18 @@ Status GraphExecutor::run_async() {
     for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[0].wait(dv.done[s]));
     MCKE_RETURN_IF_ERROR(dv.t_end.record(dv.streams[0]));
   }
-  impl_->ran_once = true;
   return OkStatus();
 }
 
 StatusOr<float> GraphExecutor::last_run_ms() {
   if (!impl_ || !impl_->ran_once) return FailedPreconditionError("last_run_ms: nothing has run");
   float worst = 0.f;
-  for (auto& dv : impl_->devs) {
+  for (std::size_t d = 0; d < impl_->devs.size(); ++d) {
+    // In graph mode only the origins record timing events outside a capture.
+    if (opts_.use_graph &&
+        std::find(impl_->origins.begin(), impl_->origins.end(), static_cast<int>(d)) == impl_->origins.end())
+      continue;
+    auto& dv = impl_->devs[d];
     MCKE_RETURN_IF_ERROR(dv.t_end.synchronize());
     auto ms = rt::Event::elapsed_ms(dv.t_start, dv.t_end);
     MCKE_RETURN_IF_ERROR(ms.status());

@@ -74,6 +74,11 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_reduce_full_f32": (i32, [vp, i64, vp, vp, sz, vp]),
             "mcke_sm100_reduce_full_partial_f32": (i32, [vp, i64, i64, vp, vp, sz, vp]),
             "mcke_sm100_reduce_combine": (i32, [vp, i64, vp, vp]),
+            "mcke_sm100_reduce_p2p_buffer_bytes": (sz, [i32]),
+            "mcke_sm100_reduce_full_p2p_f32": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp, sz, vp]),
+            "mcke_sm100_ipc_buffer_create": (i32, [sz, ctypes.POINTER(vp), vp]),
+            "mcke_sm100_ipc_buffer_open": (i32, [vp, ctypes.POINTER(vp)]),
+            "mcke_sm100_ipc_buffer_close": (i32, [vp, i32]),
             "mcke_sm100_gemm_f32": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
             "mcke_sm100_gemm_bf16": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
             "mcke_sm100_gemm_bf16_ex": (i32, [vp, vp, vp, i32, i64, i64, i64, f32, f32, vp, i32, i32, vp]),
@@ -214,6 +219,43 @@ def reduce_combine(partials, count: int, out=None, stream=None):
         out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=partials.device)
     _check(lib().mcke_sm100_reduce_combine(_ptr(partials), count, _ptr(out), _stream(partials, stream)))
     return out
+
+
+def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch: int, out=None,
+                    workspace=None, stream=None):
+    """One rank's step of a sharded full reduce with the peer-to-peer combine
+    (mcke_sm100_reduce_full_p2p_f32).  ``peer_table``: int64 CUDA tensor of the
+    ranks' exchange-buffer addresses as mapped in this process; see
+    :class:`mcke.shard.P2PExchange`, which owns the buffers and the epochs."""
+    _need(x, torch.float32, "x")
+    n = x.numel()
+    if out is None:
+        out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=x.device)
+    need = reduce_full_workspace_bytes(n)
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+    _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), n, index_base, _ptr(peer_table), world, rank, epoch,
+                                                _ptr(out), _ptr(workspace), workspace.numel(),
+                                                _stream(x, stream)))
+    return out
+
+
+def ipc_buffer_create(nbytes: int) -> tuple[int, bytes]:
+    """cudaMalloc + zero + CUDA IPC handle on the current device: (address, 64-byte handle)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _check(lib().mcke_sm100_ipc_buffer_create(nbytes, ctypes.byref(ptr), handle))
+    return ptr.value, handle.raw
+
+
+def ipc_buffer_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    _check(lib().mcke_sm100_ipc_buffer_open(ctypes.create_string_buffer(bytes(handle), 64), ctypes.byref(ptr)))
+    return ptr.value
+
+
+def ipc_buffer_close(ptr: int, opened: bool) -> None:
+    _check(lib().mcke_sm100_ipc_buffer_close(ptr, 1 if opened else 0))
 
 
 def decode_result(buf) -> tuple[float, float, int]:

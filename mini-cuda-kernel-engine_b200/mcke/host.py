@@ -45,6 +45,7 @@ def lib() -> ctypes.CDLL:
             "mcke_graph_mark_output": (i32, [vp, u32]),
             "mcke_graph_finalize": (i32, [vp]),
             "mcke_executor_create": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32]),
+            "mcke_executor_create_ex": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32, ctypes.c_uint]),
             "mcke_executor_destroy": (None, [vp]),
             "mcke_executor_plan_dry": (i32, [vp]),
             "mcke_executor_plan": (i32, [vp]),
@@ -136,10 +137,12 @@ class Graph:
 class Executor:
     """mcke::GraphExecutor over the given CUDA device ordinals."""
 
-    def __init__(self, graph: Graph, devices=(0,), streams_per_device: int = 4):
+    def __init__(self, graph: Graph, devices=(0,), streams_per_device: int = 4, cuda_graph: bool = False,
+                 poison: bool = False):
         self.graph = graph
         devs = (ctypes.c_int * len(devices))(*devices)
-        self._h = lib().mcke_executor_create(graph._h, devs, len(devices), streams_per_device)
+        flags = (1 if cuda_graph else 0) | (2 if poison else 0)
+        self._h = lib().mcke_executor_create_ex(graph._h, devs, len(devices), streams_per_device, flags)
         if not self._h:
             raise MckeError(2, "mcke_executor_create failed")
 

@@ -180,3 +180,133 @@ def test_nccl_sharded_full_reduce_on_two_gpus():
         assert (m, i) == (1.75, 40)
         ws = oracle.full_reduce(v)[0]
         assert abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws)))
+
+
+# ---- CUDA-graph replay (ExecutorOptions::use_graph) --------------------------------
+
+def _fanout_graph(branches, depth, rows, cols, seed):
+    """The reference graph bench's fan-out shape: a shared input, `branches`
+    chains of `depth` bias+GELU nodes each."""
+    g = host.Graph()
+    x = g.input("x", (rows, cols), "f32", "row_split")
+    data = {x: oracle.fill_normal(rows * cols, seed).reshape(rows, cols)}
+    outs = []
+    for b in range(branches):
+        h = x
+        for k in range(depth):
+            bias = g.input(f"b{b}_{k}", (cols,), "f32")
+            data[bias] = oracle.fill_random(cols, seed + 10 * b + k + 1)
+            h = g.bias_act(h, bias, "gelu_tanh", name=f"bias_gelu_{b}_{k}")
+        g.output(h)
+        outs.append(h)
+    g.finalize()
+    return g, x, data, outs
+
+
+def _run(g, data, outs, devices, cuda_graph, reps=1, poison=False):
+    ex = host.Executor(g, devices=devices, streams_per_device=4, cuda_graph=cuda_graph, poison=poison)
+    ex.plan()
+    for t, arr in data.items():
+        ex.set_input(t, arr)
+    for _ in range(reps):
+        ex.run()
+    ex.synchronize()
+    return ex, [ex.output(o) for o in outs]
+
+
+@pytest.mark.parametrize("devices", [[0], [0, 0]])
+def test_graph_replay_matches_eager_bitwise(devices):
+    g, x, data, outs = _fanout_graph(4, 4, 256, 384, 3)
+    _, want = _run(g, data, outs, devices, cuda_graph=False)
+    ex, got = _run(g, data, outs, devices, cuda_graph=True, reps=3, poison=True)
+    for a, b in zip(got, want):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert ex.last_run_ms() > 0
+    # a replay reads the current inputs: new data in, new (matching) results out
+    data2 = dict(data)
+    data2[x] = oracle.fill_normal(256 * 384, 99).reshape(256, 384)
+    ex.set_input(x, data2[x])
+    ex.run()
+    got2 = [ex.output(o) for o in outs]
+    _, want2 = _run(g, data2, outs, devices, cuda_graph=False)
+    for a, b, c in zip(got2, want2, got):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        assert not np.array_equal(a, c)
+    # and against the oracle, op by op
+    h = data2[x]
+    for bias in list(data2)[1:5]:  # creation order: x, then b0_0 .. b0_3
+        h = oracle.bias_act(h, data2[bias], "gelu_tanh")
+    r = oracle.compare(got2[0], h, 1e-5, 1e-6)
+    assert r["mismatches"] == 0, r
+
+
+def test_graph_replay_of_dag_with_tcgen05_gemms():
+    rows, d, f = 256, 128, 256
+    gr = host.Graph()
+    x = gr.input("X", (rows, d), "bf16", "row_split")
+    xs = _dag_inputs(rows, d, f, 5)
+    w1, b1 = gr.input("W1", (d, f), "bf16"), gr.input("b1", (f,), "f32")
+    w2, b2 = gr.input("W2", (f, d), "bf16"), gr.input("b2", (d,), "f32")
+    hh = gr.gemm(x, w1, bias=b1, act="gelu_tanh", out_dtype="bf16")
+    p = gr.softmax(gr.gemm(hh, w2, bias=b2))
+    gr.output(p)
+    gr.finalize()
+    data = dict(zip((x, w1, b1, w2, b2), xs))
+    _, want = _run(gr, data, [p], [0], cuda_graph=False)
+    _, got = _run(gr, data, [p], [0], cuda_graph=True, reps=2)
+    assert np.array_equal(got[0].view(np.uint32), want[0].view(np.uint32))
+    import mcke
+    mcke.check_device_errors()
+
+
+def test_graph_replay_of_sharded_reduce_on_one_gpu():
+    n = 1_000_003
+    v = oracle.fill_random(n, 6)
+    v[999_000] = np.float32(1.5)
+    g = host.Graph()
+    x = g.input("v", (n,))
+    r = g.reduce_full(x)
+    g.output(r)
+    g.finalize()
+    import mcke
+    _, want = _run(g, {x: v}, [r], [0, 0, 0], cuda_graph=False)
+    _, got = _run(g, {x: v}, [r], [0, 0, 0], cuda_graph=True, reps=3)
+    assert got[0].tobytes() == want[0].tobytes()
+    assert mcke.decode_result(got[0].tobytes())[1:] == (1.5, 999_000)
+
+
+@two_gpus
+def test_graph_replay_with_nccl_exchange_on_two_gpus():
+    n = 2_000_003
+    v = oracle.fill_random(n, 9)
+    v[1_500_000] = np.float32(1.5)
+    g = host.Graph()
+    x = g.input("v", (n,))
+    r = g.reduce_full(x)
+    g.output(r)
+    g.finalize()
+    import mcke
+    _, want = _run(g, {x: v}, [r], [0, 1], cuda_graph=False)
+    _, got = _run(g, {x: v}, [r], [0, 1], cuda_graph=True, reps=3)
+    assert got[0].tobytes() == want[0].tobytes()
+    assert mcke.decode_result(got[0].tobytes())[1:] == (1.5, 1_500_000)
+    gf, xf, data, outs = _fanout_graph(2, 3, 512, 256, 4)
+    _, want = _run(gf, data, outs, [0, 1], cuda_graph=False)
+    _, got = _run(gf, data, outs, [0, 1], cuda_graph=True, reps=2)
+    for a, b in zip(got, want):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@two_gpus
+def test_graph_mode_rejects_a_mixed_device_list():
+    gr = host.Graph()
+    xx = gr.input("v", (1000,))
+    rr = gr.reduce_full(xx)
+    gr.output(rr)
+    gr.finalize()
+    ex = host.Executor(gr, devices=[0, 0, 1], cuda_graph=True)
+    ex.plan()
+    ex.set_input(xx, oracle.fill_random(1000, 1))
+    import mcke
+    with pytest.raises(mcke.MckeError, match="distinct GPUs or one GPU repeated"):
+        ex.run()

@@ -438,6 +438,7 @@ Status GraphExecutor::run_async() {
     MCKE_CUDA_RETURN_IF_ERROR(cudaGraphLaunch(impl_->execs[i], dv.streams[0].native()));
     MCKE_RETURN_IF_ERROR(dv.t_end.record(dv.streams[0]));
   }
+  impl_->ran_once = true;
   return OkStatus();
 }
 
@@ -616,9 +617,13 @@ Status GraphExecutor::enqueue(bool capturing) {
           for (int d = 0; d < D; ++d) {
             MCKE_RETURN_IF_ERROR(de.streams[s].wait(impl_->devs[d].exchange_ready[nid]));
             rt::DeviceGuard g(de.device);
-            MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpyPeerAsync(static_cast<char*>(gathered[e]) + d * eb, de.device,
-                                                          ctx[d].exchange, impl_->devs[d].device, eb,
-                                                          de.streams[s].native()));
+            char* dst = static_cast<char*>(gathered[e]) + d * eb;
+            if (de.device == impl_->devs[d].device)  // (the form a stream capture accepts)
+              MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpyAsync(dst, ctx[d].exchange, eb, cudaMemcpyDeviceToDevice,
+                                                        de.streams[s].native()));
+            else
+              MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpyPeerAsync(dst, de.device, ctx[d].exchange, impl_->devs[d].device,
+                                                            eb, de.streams[s].native()));
           }
         }
         // No shard may overwrite its partial (next run) before every peer has

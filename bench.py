@@ -425,7 +425,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             ms_n, _ = timed_steps(torch, dist, launch_nccl, steps, warm, flush)
             nccl_ms = ms_n / steps
             p2p = mshard.P2PExchange(dev)
-            launch = lambda: p2p.reduce_full(xr, r0, out=res, workspace=ws)  # noqa: E731
+            launch = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
         ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
         kms = statistics.mean(per)
         ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9

@@ -173,18 +173,22 @@ int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count
  * x[0..n) (global index of x[0] = index_base), stores its 24-byte partial into
  * slot `rank` of every rank's exchange buffer over peer memory, waits (bounded,
  * 1 s) for all ranks' slots in its own buffer and writes the combined result,
- * folded in rank order.  peer_buffers: DEVICE array of `world` pointers to the
- * ranks' exchange buffers as mapped in this process (this rank's own at index
- * `rank`), each mcke_sm100_reduce_p2p_buffer_bytes(world) bytes, zeroed before
- * first use.  epoch: 1, 2, 3, ... one per call, the same on every rank.  Every
- * rank must make the call for each epoch; a rank that does not arrive makes the
- * others give up after 1 s with argmax -1 and MCKE_INTERNAL from
- * mcke_sm100_check_device_errors().  Workspace as for mcke_sm100_reduce_full_f32. */
+ * folded in rank order.  One kernel per call and no workspace: the pass-1
+ * partials go to this rank's own buffer, whose CTA 0 folds them.
+ * peer_buffers: DEVICE array of `world` pointers to the ranks' exchange
+ * buffers as mapped in this process (this rank's own at index `rank`), each
+ * mcke_sm100_reduce_p2p_buffer_bytes(world) bytes (2 * world 64-byte exchange
+ * slots, then 444 slots for this rank's pass-1 partials; every 8-byte word
+ * carries 4 data bytes and the epoch, so no fence orders data and flag),
+ * zeroed before first use.  epoch: 1, 2, 3, ... < 2^32, one per call, the same
+ * on every rank; calls of one rank are ordered on one stream.  Every rank must
+ * make the call for each epoch; a rank that does not arrive makes the others
+ * give up after 1 s with argmax -1 and MCKE_INTERNAL from
+ * mcke_sm100_check_device_errors(). */
 size_t mcke_sm100_reduce_p2p_buffer_bytes(int world);
 int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
                                    void* const* peer_buffers, int world, int rank, uint64_t epoch,
-                                   mcke_reduce_result* out, void* workspace, size_t workspace_bytes,
-                                   mcke_stream_t stream);
+                                   mcke_reduce_result* out, mcke_stream_t stream);
 /* Set-up helpers for exchange buffers shared between processes (CUDA IPC).
  * create: cudaMalloc + zero + IPC handle (64 bytes written to handle_out);
  * open: map a peer's handle in this process; close: unmap (opened = 1) or free. */

@@ -69,21 +69,36 @@ __device__ __forceinline__ Part part_shfl_xor(const Part& p, int o) {
   return q;
 }
 
-// Fixed-shape block combine: xor butterfly in each warp (every lane ends with
-// the same bits), then warp 0 folds the kWarps warp results in warp order.
-__device__ __forceinline__ Part block_combine(Part p, Part* red) {
+// Called by all 32 lanes of a warp.  It reconverges them first: lanes that
+// left a loop or a branch at different times would otherwise run the FP64
+// steps one divergent group at a time.
+__device__ __forceinline__ Part warp_butterfly(Part p) {
+  __syncwarp();
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) p = part_combine(p, part_shfl_xor(p, o));
+  return p;
+}
+
+// Fixed-shape block combine: xor butterfly in each warp (every lane ends with
+// the same bits: the combine is commutative), then warp 0 runs the same
+// butterfly over the warp results (lane w takes warp w's, lanes past the last
+// warp the identity).  The result is valid in thread 0 only.
+__device__ __forceinline__ Part block_combine(Part p, Part* red) {
+  p = warp_butterfly(p);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = p;
   __syncthreads();
-  Part t = red[0];
-  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) t = part_combine(t, red[w]);
-  return t;
+  if (threadIdx.x < 32) {
+    p = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : part_identity();
+    p = warp_butterfly(p);
+  }
+  return p;
 }
 
 // Pass-1 grid of the streamed kernel: one CTA per 16 KB chunk up to 3 per SM
 // of a B200 (a constant, so the combine tree is the same on any GPU).
 constexpr int64_t kFullCtaCap = 3 * 148;
+static_assert(kFullCtaCap < 2 * kThreads && 2 * kThreads / 32 <= 16,
+              "the P2P collector polls at most two part slots per thread");
 int64_t full_blocks(int64_t n) {
   const int64_t per_block = 4096;  // floats per chunk
   int64_t g = (n + per_block - 1) / per_block;
@@ -99,10 +114,9 @@ int64_t full_blocks(int64_t n) {
 // flight -- enough to stream HBM at full rate.  Threads read their float4s
 // from shared memory in per-thread increasing index order (thread t takes
 // float4 t, t+256, ... of each chunk, chunks in increasing order).  The
-// running maximum is updated once per float4 and only that float4's index is
-// remembered; the lane is resolved after the loop by reloading the float4 and
-// taking its first element equal to the maximum (its own bits, so a -0 ahead
-// of a +0 wins).  A later float4 with an equal maximum never replaces an
+// running maximum is updated once per float4; on an update the float4's index
+// and its first element equal to the maximum (its own bits, so a -0 ahead of
+// a +0 wins) are remembered.  A later float4 with an equal maximum never replaces an
 // earlier one, so the lowest index survives.  Head and tail elements (outside
 // whole 16-byte float4s) go to global thread 0: head first, tail last.  Waits on
 // the ring are bounded: on expiry the CTA records the site in a device word
@@ -138,9 +152,118 @@ __device__ __forceinline__ bool stream_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
+// ---- peer-to-peer combine of a sharded full reduce ----------------------------
+//
+// For one process per GPU: rank r's result slot lives in every rank's exchange
+// buffer; a call stores this rank's shard partial into slot `rank` of every
+// rank's buffer (peer memory over NVLink), waits (bounded) until each slot of
+// its own buffer carries the call's tag and folds the slots in rank order.
+// Slots use a low-latency format: each 8-byte word holds 4 bytes of the
+// partial and the 4-byte tag (the epoch), and an aligned 8-byte store is
+// single-copy atomic, so a reader that sees the tag in all six words has the
+// whole partial -- no fence on either side.  Slots are double-buffered by
+// epoch parity: a rank can run at most one epoch ahead of a peer that is still
+// reading, so the halves never collide.  After the 2 * world exchange slots
+// each buffer holds kFullCtaCap slots of the same format for the pass-1
+// partials of this rank's own call (only this GPU touches them).
+struct LLSlot {
+  unsigned long long w[8];  // words 0..5: data | tag << 32; 6, 7 unused
+};
+static_assert(sizeof(LLSlot) == 64, "slot layout");
+constexpr unsigned long long kP2pWaitNs = 1000000000ull;
+
+struct P2pArgs {
+  LLSlot* const* peers;  // device table: every rank's buffer as mapped here
+  mcke_reduce_result* out;
+  uint32_t tag;
+  uint32_t parity;
+  int world;
+  int rank;
+};
+
+__device__ __forceinline__ void ll_store(LLSlot* slot, const Part& p, uint32_t tag) {
+  const unsigned long long t = static_cast<unsigned long long>(tag) << 32;
+  const unsigned long long ib = static_cast<unsigned long long>(p.i);
+  volatile unsigned long long* w = slot->w;
+  w[0] = t | static_cast<uint32_t>(__double2loint(p.s));
+  w[1] = t | static_cast<uint32_t>(__double2hiint(p.s));
+  w[2] = t | __float_as_uint(p.m);
+  w[3] = t;
+  w[4] = t | (ib & 0xffffffffull);
+  w[5] = t | (ib >> 32);
+}
+
+__device__ __forceinline__ bool ll_try_load(const LLSlot* slot, uint32_t tag, Part& p) {
+  const volatile unsigned long long* w = slot->w;
+  unsigned long long v[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) v[k] = w[k];
+  bool ok = true;
+#pragma unroll
+  for (int k = 0; k < 6; ++k) ok = ok && static_cast<uint32_t>(v[k] >> 32) == tag;
+  if (!ok) return false;
+  p.s = __hiloint2double(static_cast<int>(static_cast<uint32_t>(v[1])), static_cast<int>(static_cast<uint32_t>(v[0])));
+  p.m = __uint_as_float(static_cast<uint32_t>(v[2]));
+  p.reserved = 0;
+  p.i = static_cast<long long>((v[5] << 32) | (v[4] & 0xffffffffull));
+  return true;
+}
+
+// Bounded wait (kP2pWaitNs) until the non-null slots carry `tag`.  The waiter
+// sleeps between polls so that it takes no issue slots from the CTAs still
+// streaming on its SM.
+__device__ __forceinline__ bool ll_wait(const LLSlot* s0, const LLSlot* s1, uint32_t tag, Part& p0, Part& p1) {
+  bool d0 = s0 == nullptr, d1 = s1 == nullptr;
+  unsigned long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (!d0) d0 = ll_try_load(s0, tag, p0);
+    if (!d1) d1 = ll_try_load(s1, tag, p1);
+    if (d0 && d1) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (it == 0) t0 = t;
+    else if (t - t0 > kP2pWaitNs) return false;
+    __nanosleep(32);
+  }
+}
+
+// Block-wide; `mine` is the same in every thread; `scratch` is shared memory
+// for `world` Parts.  Thread r publishes to rank r and then collects rank r's
+// slot of this rank's buffer, so the latencies of the ranks overlap; thread 0
+// folds the collected slots in rank order.
+__device__ void p2p_publish_and_combine(const Part& mine, const P2pArgs& a, Part* scratch) {
+  __shared__ int all_ok;
+  if (threadIdx.x == 0) all_ok = 1;
+  __syncthreads();
+  const int half = static_cast<int>(a.parity) * a.world;
+  for (int r = threadIdx.x; r < a.world; r += blockDim.x) ll_store(a.peers[r] + half + a.rank, mine, a.tag);
+  bool ok = true;
+  for (int r = threadIdx.x; r < a.world; r += blockDim.x) {
+    Part q, unused;
+    if (ll_wait(a.peers[a.rank] + half + r, nullptr, a.tag, q, unused)) scratch[r] = q;
+    else ok = false;
+  }
+  if (!ok) {
+    all_ok = 0;
+    atomicCAS(&g_reduce_watchdog, 0u, 2u);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    Part t = part_identity();
+    if (all_ok)
+      for (int r = 0; r < a.world; ++r) t = part_combine(t, scratch[r]);
+    mcke_reduce_result res;
+    res.sum = static_cast<float>(t.s);
+    res.max = t.m;
+    res.argmax = all_ok ? t.i : -1;
+    *a.out = res;
+  }
+}
+
+template <bool kP2p>
 __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
-                                                                      Part* __restrict__ parts) {
+                                                                      Part* __restrict__ parts, P2pArgs p2p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ Part red[kWarps];
   const float4* ring = reinterpret_cast<const float4*>(smem);
@@ -180,6 +303,8 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
   double s = p.s;
   float m = p.m;
   long long vbest = -1;
+  int lbest = 0;
+  float mbest = 0.f;
   const bool have_index = p.i >= 0;
   bool failed = false;
   int64_t i = 0;
@@ -204,6 +329,10 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
       if (lm > m || (vbest < 0 && !have_index && lm == m)) {
         m = lm;
         vbest = v0 + j;
+        // the float4's first element equal to its maximum, with its own bits
+        // (so a -0 ahead of a +0 wins)
+        lbest = (q.x == lm) ? 0 : (q.y == lm) ? 1 : (q.z == lm) ? 2 : 3;
+        mbest = lbest == 0 ? q.x : lbest == 1 ? q.y : lbest == 2 ? q.z : q.w;
       }
     }
     __syncthreads();  // every thread is done with this stage before it is refilled
@@ -220,15 +349,59 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
   }
   p.s = s;
   if (vbest >= 0) {
-    const float4 q = ld_stream_f4(xa + 4 * vbest);
-    const int lane = (q.x == m) ? 0 : (q.y == m) ? 1 : (q.z == m) ? 2 : 3;
-    p.m = lane == 0 ? q.x : lane == 1 ? q.y : lane == 2 ? q.z : q.w;
-    p.i = base + head + 4 * vbest + lane;
+    p.m = mbest;
+    p.i = base + head + 4 * vbest + lbest;
   }
   if (blockIdx.x == 0 && tid == 0)
     for (int64_t e = head + 4 * nv; e < n; ++e) part_add(p, x[e], base + e);
   p = block_combine(p, red);
-  if (tid == 0) parts[blockIdx.x] = p;
+  if (!kP2p && tid == 0) parts[blockIdx.x] = p;
+  if constexpr (kP2p) {
+    // Hand-off without an atomic or a fence: every CTA stores its partial in
+    // its slot of this rank's part area (low-latency format); CTA 0 collects
+    // them as they arrive -- thread t the virtual lanes t and t+256 of
+    // reduce_full_combine_kernel's 1024-thread fold (G <= kFullCtaCap < 512,
+    // so the rest are the identity) -- which makes the shard partial
+    // bit-identical to the two-launch path, and runs the exchange.  Only CTA 0
+    // waits, on CTAs that never wait, so the grid cannot deadlock.
+    LLSlot* local = p2p.peers[p2p.rank] + 2 * p2p.world;
+    if (tid == 0) ll_store(local + blockIdx.x, p, p2p.tag);
+    if (blockIdx.x != 0) return;
+    __shared__ Part red32[16];
+    __shared__ Part shard;
+    __shared__ int parts_ok;
+    if (tid == 0) parts_ok = 1;
+    __syncthreads();
+    const int G = static_cast<int>(gridDim.x);
+    Part v0 = part_identity(), v1 = part_identity(), q0, q1;
+    const bool got = ll_wait(tid < G ? local + tid : nullptr, tid + kThreads < G ? local + tid + kThreads : nullptr,
+                             p2p.tag, q0, q1);
+    if (!got) parts_ok = 0;
+    if (got && tid < G) v0 = part_combine(v0, q0);
+    if (got && tid + kThreads < G) v1 = part_combine(v1, q1);
+    v0 = warp_butterfly(v0);
+    v1 = warp_butterfly(v1);
+    if ((tid & 31) == 0) {
+      red32[tid >> 5] = v0;
+      red32[(tid >> 5) + kWarps] = v1;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      Part r = tid < 2 * kWarps ? red32[tid] : part_identity();
+      r = warp_butterfly(r);
+      if (tid == 0) {
+        if (!parts_ok) {
+          atomicCAS(&g_reduce_watchdog, 0u, 1u);
+          r.i = -1;
+        }
+        shard = r;
+      }
+    }
+    __syncthreads();
+    // the ring is idle now (every bulk copy has landed): its shared memory
+    // holds the collected slots
+    p2p_publish_and_combine(shard, p2p, reinterpret_cast<Part*>(smem));
+  }
 }
 
 // Pass 2 (and the cross-shard combine): one block folds `count` Parts in a
@@ -387,8 +560,11 @@ int ensure_stream_smem(const char* who) {
     return fail(MCKE_CUDA_ERROR, "%s: no usable current device", who);
   std::lock_guard<std::mutex> lk(g_stream_mu);
   if (!g_stream_attr[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(reduce_full_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(kStreamSmem));
+    cudaError_t e = cudaFuncSetAttribute(reduce_full_stream_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kStreamSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(reduce_full_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kStreamSmem));
     if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
     g_stream_attr[dev] = true;
   }
@@ -444,7 +620,7 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   if (head > n) head = n;
   Part* parts = static_cast<Part*>(workspace);
   MCKE_RETURN_IF(ensure_stream_smem(who));
-  reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts);
+  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
   if (final_result) reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   else reduce_full_combine_kernel<false><<<1, 1024, 0, s>>>(parts, g, out);
@@ -616,140 +792,59 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   // needs clearing.
   Part* parts = static_cast<Part*>(scratch);
   MCKE_RETURN_IF(ensure_stream_smem(who));
-  reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, 0, parts);
+  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, 0, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
   reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   return check_launch(who);
 }
 
 // ---- sharded full reduce with a peer-to-peer one-shot combine ----------------
-//
-// For one process per GPU: instead of an all-gather through a collective
-// library, each rank's combine kernel folds its own pass-1 partials into the
-// shard partial, stores it into slot `rank` of every rank's exchange buffer
-// (peer memory over NVLink, plain stores), publishes it with an epoch flag,
-// waits (bounded) until every rank's slot in its own buffer carries the same
-// epoch, and folds the slots in rank order.  Slots are double-buffered by
-// epoch parity: a rank can run at most one epoch ahead of any peer that is
-// still reading, so the two halves never collide.  Exchange buffers are
-// created and shared across processes with the CUDA IPC helpers below
-// (set-up time; the entry point itself allocates nothing).
 namespace mcke_sm100 {
 namespace {
-
-struct Slot {
-  Part p;
-  unsigned long long epoch;
-};
-static_assert(sizeof(Slot) == 32, "slot layout");
-constexpr unsigned long long kP2pWaitNs = 1000000000ull;
-
-__global__ void __launch_bounds__(1024) reduce_exchange_p2p_kernel(const Part* __restrict__ parts, int64_t count,
-                                                                   Slot* const* __restrict__ peers, int world,
-                                                                   int rank, unsigned long long epoch,
-                                                                   mcke_reduce_result* __restrict__ out) {
-  __shared__ Part red[32];
-  __shared__ Part mine;
-  __shared__ int all_ok;
-  Part p = part_identity();
-  for (int64_t j = threadIdx.x; j < count; j += blockDim.x) p = part_combine(p, parts[j]);
-  p = block_combine(p, red);
-  if (threadIdx.x == 0) {
-    mine = p;
-    all_ok = 1;
-  }
-  __syncthreads();
-  const int half = static_cast<int>(epoch & 1ull) * world;
-  if (static_cast<int>(threadIdx.x) < world) {
-    Slot* dst = peers[threadIdx.x] + half + rank;
-    volatile Part* vp = &dst->p;
-    vp->s = mine.s;
-    vp->m = mine.m;
-    vp->reserved = 0;
-    vp->i = mine.i;
-    __threadfence_system();  // the partial is visible before its flag
-    *reinterpret_cast<volatile unsigned long long*>(&dst->epoch) = epoch;
-  }
-  // Wait for every rank's slot in this rank's own buffer.
-  if (static_cast<int>(threadIdx.x) < world) {
-    volatile unsigned long long* flag = &(peers[rank] + half + threadIdx.x)->epoch;
-    unsigned long long t0 = 0;
-    bool ok = false;
-    for (uint32_t it = 0;; ++it) {
-      if (*flag == epoch) {
-        ok = true;
-        break;
-      }
-      unsigned long long t;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (it == 0) t0 = t;
-      else if (t - t0 > kP2pWaitNs) break;
-    }
-    if (!ok) {
-      all_ok = 0;
-      atomicCAS(&g_reduce_watchdog, 0u, 2u);
-    }
-    __threadfence_system();  // slot contents after the flag
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    Part t = part_identity();
-    if (all_ok) {
-      for (int r = 0; r < world; ++r) {
-        const volatile Part* sp = &(peers[rank] + half + r)->p;
-        Part q;
-        q.s = sp->s;
-        q.m = sp->m;
-        q.reserved = 0;
-        q.i = sp->i;
-        t = part_combine(t, q);
-      }
-    }
-    mcke_reduce_result res;
-    res.sum = static_cast<float>(t.s);
-    res.max = t.m;
-    res.argmax = all_ok ? t.i : -1;
-    *out = res;
-  }
+// Only for an empty shard (no pass-1 CTA to run the exchange).
+__global__ void __launch_bounds__(kThreads) reduce_p2p_empty_kernel(P2pArgs a) {
+  extern __shared__ __align__(16) uint8_t scratch[];
+  p2p_publish_and_combine(part_identity(), a, reinterpret_cast<Part*>(scratch));
 }
-
 }  // namespace
 }  // namespace mcke_sm100
 
 extern "C" size_t mcke_sm100_reduce_p2p_buffer_bytes(int world) {
-  return world > 0 ? static_cast<size_t>(2 * world) * sizeof(Slot) : 0;
+  return world > 0 ? static_cast<size_t>(2 * world + kFullCtaCap) * sizeof(LLSlot) : 0;
 }
 
 extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
                                               void* const* peer_buffers, int world, int rank, uint64_t epoch,
-                                              mcke_reduce_result* out, void* workspace, size_t workspace_bytes,
-                                              mcke_stream_t stream) {
+                                              mcke_reduce_result* out, mcke_stream_t stream) {
   static const char* who = "mcke_sm100_reduce_full_p2p_f32";
   clear_error();
   if (!out || !peer_buffers) return fail(MCKE_INVALID_ARGUMENT, "%s: null output or peer table", who);
   if (world < 1 || world > 1024 || rank < 0 || rank >= world)
     return fail(MCKE_INVALID_ARGUMENT, "%s: bad world/rank %d/%d", who, world, rank);
-  if (epoch == 0) return fail(MCKE_INVALID_ARGUMENT, "%s: epoch must start at 1 (0 marks an empty slot)", who);
+  if (epoch == 0 || epoch > 0xffffffffull)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: epoch must be in [1, 2^32) (0 marks an empty slot)", who);
   if (n < 0 || (n > 0 && !x)) return fail(MCKE_INVALID_ARGUMENT, "%s: bad input", who);
   if (index_base < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative index_base", who);
   if (n > 0 && !aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
-  const size_t need = n > 0 ? mcke_sm100_reduce_full_workspace_bytes(n) : 0;
-  if (n > 0 && (!workspace || workspace_bytes < need || !aligned(workspace, 16)))
-    return fail(MCKE_INVALID_ARGUMENT, "%s: needs %zu bytes of 16-byte aligned workspace", who, need);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  int64_t g = 0;
-  Part* parts = static_cast<Part*>(workspace);
-  if (n > 0) {
-    g = full_blocks(n);
-    const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
-    int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
-    if (head > n) head = n;
-    MCKE_RETURN_IF(ensure_stream_smem(who));
-    reduce_full_stream_kernel<<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts);
-    MCKE_RETURN_IF(check_launch(who));
+  P2pArgs a;
+  a.peers = reinterpret_cast<LLSlot* const*>(peer_buffers);
+  a.out = out;
+  a.tag = static_cast<uint32_t>(epoch);
+  a.parity = static_cast<uint32_t>(epoch & 1);
+  a.world = world;
+  a.rank = rank;
+  if (n == 0) {
+    reduce_p2p_empty_kernel<<<1, kThreads, static_cast<size_t>(world) * sizeof(Part), s>>>(a);
+    return check_launch(who);
   }
-  reduce_exchange_p2p_kernel<<<1, 1024, 0, s>>>(parts, g, reinterpret_cast<Slot* const*>(peer_buffers), world, rank,
-                                                 static_cast<unsigned long long>(epoch), out);
+  const int64_t g = full_blocks(n);
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
+  int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
+  if (head > n) head = n;
+  MCKE_RETURN_IF(ensure_stream_smem(who));
+  reduce_full_stream_kernel<true><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(
+      x, n, head, index_base, nullptr, a);
   return check_launch(who);
 }
 

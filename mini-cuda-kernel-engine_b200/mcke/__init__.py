@@ -75,7 +75,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_reduce_full_partial_f32": (i32, [vp, i64, i64, vp, vp, sz, vp]),
             "mcke_sm100_reduce_combine": (i32, [vp, i64, vp, vp]),
             "mcke_sm100_reduce_p2p_buffer_bytes": (sz, [i32]),
-            "mcke_sm100_reduce_full_p2p_f32": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp, sz, vp]),
+            "mcke_sm100_reduce_full_p2p_f32": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp]),
             "mcke_sm100_ipc_buffer_create": (i32, [sz, ctypes.POINTER(vp), vp]),
             "mcke_sm100_ipc_buffer_open": (i32, [vp, ctypes.POINTER(vp)]),
             "mcke_sm100_ipc_buffer_close": (i32, [vp, i32]),
@@ -221,22 +221,16 @@ def reduce_combine(partials, count: int, out=None, stream=None):
     return out
 
 
-def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch: int, out=None,
-                    workspace=None, stream=None):
+def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch: int, out=None, stream=None):
     """One rank's step of a sharded full reduce with the peer-to-peer combine
     (mcke_sm100_reduce_full_p2p_f32).  ``peer_table``: int64 CUDA tensor of the
     ranks' exchange-buffer addresses as mapped in this process; see
     :class:`mcke.shard.P2PExchange`, which owns the buffers and the epochs."""
     _need(x, torch.float32, "x")
-    n = x.numel()
     if out is None:
         out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=x.device)
-    need = reduce_full_workspace_bytes(n)
-    if workspace is None:
-        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
-    _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), n, index_base, _ptr(peer_table), world, rank, epoch,
-                                                _ptr(out), _ptr(workspace), workspace.numel(),
-                                                _stream(x, stream)))
+    _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), x.numel(), index_base, _ptr(peer_table), world, rank,
+                                                epoch, _ptr(out), _stream(x, stream)))
     return out
 
 

@@ -24,6 +24,15 @@ import mcke  # noqa: E402
 from mcke import shard as mshard  # noqa: E402
 
 
+def _ll_slot(s, m, i, tag):
+    """A 64-byte exchange slot: six 8-byte words, each 4 data bytes of the
+    24-byte partial plus the 4-byte tag."""
+    data = np.frombuffer(mshard.pack_partial(s, m, i), dtype=np.uint32).astype(np.uint64)
+    words = np.zeros(8, dtype=np.uint64)
+    words[:6] = data | (np.uint64(tag) << np.uint64(32))
+    return words.view(np.uint8).copy()
+
+
 def _table(*bufs):
     return torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
 
@@ -55,20 +64,20 @@ def test_index_base_and_rank_slot():
     b1 = torch.zeros(nb, dtype=torch.uint8, device="cuda")
     table = _table(b0, b1)
     # Rank 0 has already published epoch 1 into rank 1's buffer: epoch 1 uses
-    # the odd half (slots 2..3), rank 0's slot is 2.  Rank 1's call stores its
-    # own slot 3 in both buffers and folds slots 2, 3 of b1.
+    # the odd half (slots 2..3 of 64 bytes), rank 0's slot is 2.  Rank 1's call
+    # stores its own slot 3 in both buffers and folds slots 2, 3 of b1.
     s0, m0, i0 = mcke.decode_partial(mcke.reduce_full_partial(x0, 0))
-    slot = np.frombuffer(mshard.pack_partial(s0, m0, i0) + np.uint64(1).tobytes(), dtype=np.uint8)
-    b1[2 * 32:3 * 32].copy_(torch.from_numpy(slot.copy()))
+    b1[2 * 64:3 * 64].copy_(torch.from_numpy(_ll_slot(s0, m0, i0, 1)))
     got = mcke.decode_result(mcke.reduce_full_p2p(x1, 100_000, table, 2, 1, 1))
     want = oracle.full_reduce(v)
     assert got[1:] == (1.5, 150_000)
     assert abs(got[0] - np.float32(want[0])) <= np.spacing(np.float32(abs(want[0])))
     mcke.check_device_errors()
-    # rank 1's partial reached rank 0's buffer too, with its flag
-    raw = b0[3 * 32:4 * 32].cpu().numpy().tobytes()
-    assert np.frombuffer(raw[24:], dtype=np.uint64)[0] == 1
-    assert mshard.unpack_partial(raw)[1:] == (1.5, 150_000)
+    # rank 1's partial reached rank 0's buffer too, every word tagged
+    words = b0[3 * 64:4 * 64].cpu().numpy().view(np.uint64)
+    assert all(int(w) >> 32 == 1 for w in words[:6])
+    data = (words[:6] & np.uint64(0xFFFFFFFF)).astype(np.uint32).tobytes()
+    assert mshard.unpack_partial(data)[1:] == (1.5, 150_000)
 
 
 def test_missing_peer_expires_and_is_reported():
@@ -91,7 +100,7 @@ def test_argument_checks():
     x = torch.ones(16, device="cuda")
     buf = torch.zeros(64, dtype=torch.uint8, device="cuda")
     t = _table(buf)
-    for world, rank, epoch in ((0, 0, 1), (1, 1, 1), (1, 0, 0)):
+    for world, rank, epoch in ((0, 0, 1), (1, 1, 1), (1, 0, 0), (1, 0, 1 << 32)):
         with pytest.raises(mcke.MckeError):
             mcke.reduce_full_p2p(x, 0, t, world, rank, epoch)
     with pytest.raises(mcke.MckeError):

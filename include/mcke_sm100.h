@@ -218,6 +218,20 @@ int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mcke_reduce_re
  * never reads C; k == 0 writes beta * C.  variant: AUTO or SIMT. */
 int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int64_t n,
                         int64_t k, float alpha, float beta, int variant, mcke_stream_t stream);
+/* New: float32 GEMM on the tensor cores (3xTF32): A and B are each split into
+ * hi (low 13 mantissa bits cleared) and lo = x - hi parts in `workspace`, and
+ * the tcgen05 kernel accumulates A_hi*B_lo + A_lo*B_hi + A_hi*B_hi in fp32 --
+ * fp32-level accuracy (relative error ~1e-6, not bit-identical to an FFMA loop)
+ * at tensor-core speed.  c = act(alpha * A@B + beta * C + bias[col]), float32;
+ * bias may be NULL.  Needs K % 4 == 0, N % 4 == 0, 16-byte aligned A and B and
+ * mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k) bytes of 256-byte aligned
+ * workspace (8 * (M*K + K*N) bytes, rounded); other shapes are rejected (use
+ * mcke_sm100_gemm_f32).  Same contract as launch_gemm_f32 (kernels.hpp:265)
+ * otherwise: beta == 0 never reads C, k == 0 writes act(beta * C + bias). */
+size_t mcke_sm100_gemm_f32_tc_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int mcke_sm100_gemm_f32_tc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                           float alpha, float beta, const float* bias, int act, void* workspace,
+                           size_t workspace_bytes, mcke_stream_t stream);
 /* New: bf16 inputs (raw 16-bit patterns), float32 accumulation and output. */
 int mcke_sm100_gemm_bf16(const uint16_t* a, const uint16_t* b, float* c, int64_t m, int64_t n,
                          int64_t k, float alpha, float beta, int variant, mcke_stream_t stream);

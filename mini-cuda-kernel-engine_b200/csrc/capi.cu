@@ -138,6 +138,50 @@ extern "C" int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int
                     nullptr, MCKE_ACT_NONE, variant, stream);
 }
 
+extern "C" size_t mcke_sm100_gemm_f32_tc_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  return gemm_tf32x3_workspace_bytes(m, n, k);
+}
+
+extern "C" int mcke_sm100_gemm_f32_tc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                                      float alpha, float beta, const float* bias, int act, void* workspace,
+                                      size_t workspace_bytes, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_gemm_f32_tc";
+  clear_error();
+  if (m < 0 || n < 0 || k < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (m == 0 || n == 0) return MCKE_OK;
+  if (!a || !b || !c) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
+  if (a == c || b == c)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: output aliases an input, which violates the __restrict__ contract", who);
+  if (m > 2147483647LL || n > 2147483647LL || k > 2147483647LL)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: extent exceeds INT32_MAX", who);
+  if (act < MCKE_ACT_NONE || act > MCKE_ACT_GELU_TANH)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  EpilogueParams ep;
+  ep.alpha = alpha;
+  ep.beta = beta;
+  ep.bias = bias;
+  ep.act = act;
+  ep.out_bf16 = 0;
+  ep.vec_ok = (n % 4 == 0) && aligned(c, 16) ? 1 : 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (k == 0) {  // C = act(beta * C + bias): no products to split
+    MCKE_RETURN_IF(launch_gemm_simt(a, b, c, m, n, k, false, ep, s, nullptr));
+    return check_launch(who);
+  }
+  if (k % 4 != 0 || n % 4 != 0 || !aligned(a, 16) || !aligned(b, 16))
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: needs K %% 4 == 0, N %% 4 == 0 and 16-byte aligned A and B (TMA rows); no fallback is applied",
+                who);
+  const size_t need = gemm_tf32x3_workspace_bytes(m, n, k);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(MCKE_INVALID_ARGUMENT,
+                "%s: needs %zu bytes of 256-byte aligned workspace (got %zu); query "
+                "mcke_sm100_gemm_f32_tc_workspace_bytes() first",
+                who, need, workspace_bytes);
+  MCKE_RETURN_IF(launch_gemm_tf32x3(a, b, c, m, n, k, ep, workspace, s, nullptr, nullptr));
+  return check_launch(who);
+}
+
 extern "C" int mcke_sm100_gemm_bf16(const uint16_t* a, const uint16_t* b, float* c, int64_t m,
                                     int64_t n, int64_t k, float alpha, float beta, int variant,
                                     mcke_stream_t stream) {

@@ -71,5 +71,11 @@ int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m
                         const void** kernel_out, std::size_t* smem_out);
 bool tcgen05_shape_ok(const void* a, const void* b, const void* c, int64_t m, int64_t n, int64_t k,
                       bool out_bf16);
+// fp32 GEMM on the tensor cores in the 3xTF32 form (split kernels, then the
+// tcgen05 kernel); workspace holds the hi/lo parts of A and B.
+std::size_t gemm_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
+int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                       const EpilogueParams& ep, void* workspace, cudaStream_t s, const void** kernel_out,
+                       std::size_t* smem_out);
 
 }  // namespace mcke_sm100

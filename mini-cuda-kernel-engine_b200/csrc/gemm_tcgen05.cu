@@ -35,9 +35,21 @@
 // its own TMA loads and MMAs in flight, frees its TMEM and exits; both CTAs of
 // a pair always meet at the final cluster barrier.
 //
+// fp32 operands (kTf32 = true) take the same template through .kind::tf32 in
+// the 3xTF32 form: each operand is split beforehand into hi = its value with
+// the low 13 mantissa bits cleared (exact in tf32) and lo = value - hi, and
+// every k-step issues A_hi*B_lo + A_lo*B_hi + A_hi*B_hi into the fp32
+// accumulator, which recovers fp32-level accuracy (the dropped lo*lo term and
+// the tf32 rounding of lo are ~2^-22 relative).  Rows of 128 bytes hold 32
+// fp32 values, so a k-block is 32 deep and an MMA step 8 deep; a stage holds
+// A, B, A_lo and B_lo (64 KB per CTA in the pair shape, 3 stages).  B is fed
+// K-major (the split pass writes B^T): on this part an N-major B operand of
+// .kind::tf32 accumulated nothing (measured with all-ones operands, where the
+// same descriptors with .kind::f16 give the right sum), so only K-major is used.
+//
 // Tensor-memory and descriptor encodings follow the PTX ISA for tcgen05
-// (instruction descriptor for .kind::f16, shared-memory matrix descriptor with
-// version 1 and SWIZZLE_128B), written out by hand below.
+// (instruction descriptor for .kind::f16 / .kind::tf32, shared-memory matrix
+// descriptor with version 1 and SWIZZLE_128B), written out by hand below.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -48,37 +60,49 @@
 namespace mcke_sm100 {
 namespace {
 
-constexpr int BK = 64;
-constexpr int UMMA_K = 16;
-constexpr int B_BOX_BYTES = 64 * BK * 2;  // one 64(N) x 64(K) box, 8 KB
 constexpr int TMEM_COLS = 512;            // two accumulators of 256 fp32 columns
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;  // 320
 constexpr int kGroupM = 16;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
-template <bool kPair>
+template <bool kPair, bool kTf32 = false>
 struct Cfg {
+  static constexpr int ELEM = kTf32 ? 4 : 2;          // operand bytes
+  static constexpr int BK = 128 / ELEM;               // k-block: one 128-byte swizzle row
+  static constexpr int UMMA_K = 32 / ELEM;            // k per MMA: 32 bytes of a row
+  static constexpr int BOX_COLS = 128 / ELEM;         // B box: one swizzle row of N
+  static constexpr int B_BOX_BYTES = BOX_COLS * BK * ELEM;
+  static_assert(B_BOX_BYTES == 128 * BK, "a B box is BK rows of 128 bytes");
+  static constexpr int OPS = kTf32 ? 2 : 1;           // hi (+ lo) copies of each operand
   static constexpr int BM = 128;                      // rows of A per CTA
   static constexpr int BN = 256;                      // output columns per tile
   static constexpr int TILE_M = kPair ? 2 * BM : BM;  // output rows per tile
   static constexpr int B_COLS = kPair ? BN / 2 : BN;  // columns of B per CTA
-  static constexpr int STAGES = kPair ? 6 : 4;
-  static constexpr int A_STAGE = BM * BK * 2;
-  static constexpr int B_STAGE = B_COLS * BK * 2;
-  static constexpr int STAGE = A_STAGE + B_STAGE;
+  static constexpr int A_STAGE = BM * BK * ELEM;
+  static constexpr int B_STAGE = B_COLS * BK * ELEM;
+  static constexpr int STAGE = OPS * (A_STAGE + B_STAGE);  // A, B, then A_lo, B_lo
+  static constexpr int STAGES = kTf32 ? (kPair ? 3 : 2) : (kPair ? 6 : 4);
+  // k-blocks per tensor-memory accumulation unit: tf32 partial sums are moved
+  // to registers every PROMOTE k-blocks (128 k); bf16 accumulates a whole tile.
+  static constexpr int PROMOTE = kTf32 ? 4 : 0;
   static constexpr int TX = kPair ? 2 * STAGE : STAGE;  // bytes landing on the leader's full barrier
   static constexpr int EPI_ARRIVALS = kPair ? 2 * kEpiWarps : kEpiWarps;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
   static constexpr std::size_t SMEM = static_cast<std::size_t>(STAGES) * STAGE + 1024 + 256;
-  // Instruction descriptor, .kind::f16: D f32 (bits 4-5 = 1), A bf16 (7-9 = 1),
-  // B bf16 (10-12 = 1), A K-major (bit 15 = 0), B N-major (bit 16 = 1),
-  // N >> 3 at bits 17-22, M >> 4 at bits 24-28.
-  static constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | (0u << 15) | (1u << 16) |
+  // Instruction descriptor, .kind::f16 / .kind::tf32: D f32 (bits 4-5 = 1),
+  // A and B bf16 (1) or tf32 (2) at bits 7-9 and 10-12, A K-major (bit 15 = 0),
+  // B N-major (bit 16 = 1; bf16) or K-major (0; tf32), N >> 3 at bits 17-22,
+  // M >> 4 at bits 24-28.
+  static constexpr uint32_t FMT = kTf32 ? 2u : 1u;
+  static constexpr uint32_t B_MN_MAJOR = kTf32 ? 0u : 1u;  // tf32: B^T, K-major
+  static constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | (0u << 15) | (B_MN_MAJOR << 16) |
                                     (static_cast<uint32_t>(BN >> 3) << 17) |
                                     (static_cast<uint32_t>(TILE_M >> 4) << 24);
 };
 static_assert(Cfg<false>::SMEM <= 232448 && Cfg<true>::SMEM <= 232448, "shared memory budget");
+static_assert(Cfg<false, true>::SMEM <= 232448 && Cfg<true, true>::SMEM <= 232448, "shared memory budget");
+static_assert(Cfg<true, true>::B_STAGE % 1024 == 0 && Cfg<false, true>::A_STAGE % 1024 == 0, "stage alignment");
 
 // Sites reported through the watchdog word (1-based).
 enum : uint32_t { kSiteProducer = 1, kSiteMmaFull = 2, kSiteMmaEmpty = 3, kSiteEpilogue = 4, kSiteDrain = 5 };
@@ -188,21 +212,36 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-template <bool kPair>
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  if constexpr (kPair) {
+template <bool kPair, bool kTf32>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  constexpr uint32_t idesc = Cfg<kPair, kTf32>::IDESC;
+  if constexpr (kPair && kTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else if constexpr (kTf32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else if constexpr (kPair) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(Cfg<true>::IDESC), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
   } else {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(Cfg<false>::IDESC), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
   }
 }
@@ -291,12 +330,12 @@ __device__ __forceinline__ float epi_act(float v) {
 
 // 32 accumulator values of row gm, columns gn0 .. gn0+31.
 // `fast`: C 16-byte aligned, N % 8 == 0 and bias (if any) 16-byte aligned.
+// v: the 32 accumulator values of columns gn0.. of row gm (scaled in place).
 template <bool kBf16Out, bool kBias, int kAct>
-__device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int N, int64_t gm, int gn0,
-                                          const uint32_t (&r)[32], bool fast) {
-  float v[32];
+__device__ __forceinline__ void epi_vals(const EpilogueParams& ep, void* c, int N, int64_t gm, int gn0, float (&v)[32],
+                                         bool fast) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = ep.alpha * __uint_as_float(r[j]);
+  for (int j = 0; j < 32; ++j) v[j] = ep.alpha * v[j];
   const int64_t base = gm * N + gn0;
   if (fast && gn0 + 32 <= N) {
     if constexpr (!kBf16Out) {
@@ -354,19 +393,34 @@ __device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int
   }
 }
 
+template <bool kBf16Out, bool kBias, int kAct>
+__device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int N, int64_t gm, int gn0,
+                                          const uint32_t (&r)[32], bool fast) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  epi_vals<kBf16Out, kBias, kAct>(ep, c, N, gm, gn0, v, fast);
+}
+
 // ---- the kernel -------------------------------------------------------------------
 
-template <bool kPair, bool kBf16Out, bool kBias, int kAct>
+template <bool kPair, bool kTf32, bool kBf16Out, bool kBias, int kAct>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
                         void* __restrict__ c, int M, int N, int K, EpilogueParams ep, int fast) {
-  using C = Cfg<kPair>;
+  using C = Cfg<kPair, kTf32>;
+  constexpr int BK = C::BK;
+  constexpr int UMMA_K = C::UMMA_K;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + C::STAGES * C::A_STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_STAGE);
+  // Stage s: A, B (and A_lo, B_lo) back to back, each a multiple of 1024 bytes.
+  auto sA = [&](int st) { return smem + st * C::STAGE; };
+  auto sB = [&](int st) { return smem + st * C::STAGE + C::A_STAGE; };
+  auto sAlo = [&](int st) { return smem + st * C::STAGE + C::A_STAGE + C::B_STAGE; };
+  auto sBlo = [&](int st) { return smem + st * C::STAGE + 2 * C::A_STAGE + C::B_STAGE; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -397,6 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_b)) : "memory");
+    if constexpr (kTf32) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_alo)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_blo)) : "memory");
+    }
   }
   if (warp == 1) tmem_alloc<kPair>(smem_u32(tmem_slot));
   tc_fence_before();
@@ -432,11 +490,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t fb = full_bar(stage);
           if (leader) mbar_expect_tx(fb, C::TX);
           if constexpr (kPair) fb = map_to_rank(fb, 0);
-          tma_load_2d<kPair>(smem_u32(sA + stage * C::A_STAGE), &tmap_a, fb, kb * BK, row0);
+          tma_load_2d<kPair>(smem_u32(sA(stage)), &tmap_a, fb, kb * BK, row0);
+          if constexpr (kTf32) {
+            // B^T rows col0.. (K-major): one box of B_COLS rows x 32 k
+            tma_load_2d<kPair>(smem_u32(sB(stage)), &tmap_b, fb, kb * BK, col0);
+            tma_load_2d<kPair>(smem_u32(sAlo(stage)), &tmap_alo, fb, kb * BK, row0);
+            tma_load_2d<kPair>(smem_u32(sBlo(stage)), &tmap_blo, fb, kb * BK, col0);
+          } else {
 #pragma unroll
-          for (int j = 0; j < C::B_COLS / 64; ++j)
-            tma_load_2d<kPair>(smem_u32(sB + stage * C::B_STAGE + j * B_BOX_BYTES), &tmap_b, fb, col0 + 64 * j,
-                               kb * BK);
+            for (int j = 0; j < C::B_COLS / C::BOX_COLS; ++j)
+              tma_load_2d<kPair>(smem_u32(sB(stage) + j * C::B_BOX_BYTES), &tmap_b, fb, col0 + C::BOX_COLS * j,
+                                 kb * BK);
+          }
           issued_mask |= 1u << stage;
           parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -456,45 +521,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
+    // Accumulation units alternate between the two TMEM accumulators: one unit
+    // per tile (bf16), or one per PROMOTE k-blocks (tf32).
     if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int lt = 0;
-      for (int t = unit; t < num_tiles && ok; t += units, ++lt) {
-        const int acc = lt & 1;
-        const uint32_t aphase = static_cast<uint32_t>(lt >> 1) & 1u;
-        if (!wait_bounded(tempty_bar(acc), aphase ^ 1u, abort_flag, kSiteMmaEmpty, true)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
-          if (!wait_bounded(full_bar(stage), phase, abort_flag, kSiteMmaFull, true)) {
+      int lc = 0;
+      const int unit_kb = kTf32 ? C::PROMOTE : kblocks;
+      for (int t = unit; t < num_tiles && ok; t += units) {
+        for (int kb0 = 0; kb0 < kblocks && ok; kb0 += unit_kb, ++lc) {
+          const int acc = lc & 1;
+          const uint32_t aphase = static_cast<uint32_t>(lc >> 1) & 1u;
+          if (!wait_bounded(tempty_bar(acc), aphase ^ 1u, abort_flag, kSiteMmaEmpty, true)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * C::A_STAGE);
-          const uint32_t b_base = smem_u32(sB + stage * C::B_STAGE);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
+          const int kb1 = min(kb0 + unit_kb, kblocks);
+          for (int kb = kb0; kb < kb1; ++kb) {
+            if (!wait_bounded(full_bar(stage), phase, abort_flag, kSiteMmaFull, true)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sA(stage));
+            const uint32_t b_base = smem_u32(sB(stage));
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // A: K-major SW128, +32 bytes per 16-deep step; SBO = 8 rows x 128 B.
-            const uint64_t adesc = smem_desc(a_base + k * (UMMA_K * 2), 16, 1024);
-            // B: N-major SW128, +16 rows x 128 B per step; LBO = one 64-wide
-            // N box (8 KB), SBO = 8 k-rows x 128 B.
-            const uint64_t bdesc = smem_desc(b_base + k * (UMMA_K * 128), B_BOX_BYTES, 1024);
-            umma_bf16<kPair>(d_tmem, adesc, bdesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
+              // A: K-major SW128, +32 bytes per step; SBO = 8 rows x 128 B.
+              const uint64_t adesc = smem_desc(a_base + k * 32, 16, 1024);
+              if constexpr (kTf32) {
+                // B^T: K-major like A.  Small terms first: A_hi*B_lo, A_lo*B_hi,
+                // then A_hi*B_hi.
+                const uint64_t bdesc = smem_desc(b_base + k * 32, 16, 1024);
+                const uint64_t aldesc = smem_desc(smem_u32(sAlo(stage)) + k * 32, 16, 1024);
+                const uint64_t bldesc = smem_desc(smem_u32(sBlo(stage)) + k * 32, 16, 1024);
+                umma<kPair, true>(d_tmem, adesc, bldesc, accum);
+                umma<kPair, true>(d_tmem, aldesc, bdesc, 1u);
+                umma<kPair, true>(d_tmem, adesc, bdesc, 1u);
+              } else {
+                // B: N-major SW128, +UMMA_K rows x 128 B per step; LBO = one
+                // BOX_COLS-wide N box, SBO = 8 k-rows x 128 B.
+                const uint64_t bdesc = smem_desc(b_base + k * (UMMA_K * 128), C::B_BOX_BYTES, 1024);
+                umma<kPair, false>(d_tmem, adesc, bdesc, accum);
+              }
+            }
+            umma_commit_all<kPair>(empty_bar(stage));
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          umma_commit_all<kPair>(empty_bar(stage));
-          if (++stage == C::STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (!ok) break;
+          umma_commit_all<kPair>(tfull_bar(acc));
         }
-        if (!ok) break;
-        umma_commit_all<kPair>(tfull_bar(acc));
       }
       // Every MMA this thread issued has completed once drain_bar flips.
       umma_commit_self<kPair>(drain_bar);
@@ -507,30 +590,72 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;      // which alternate 32-column chunks
     uint32_t tempty_leader0 = tempty_bar(0);
     if constexpr (kPair) tempty_leader0 = map_to_rank(tempty_leader0, 0);
-    int lt = 0;
-    for (int t = unit; t < num_tiles; t += units, ++lt) {
-      const int acc = lt & 1;
-      const uint32_t aphase = static_cast<uint32_t>(lt >> 1) & 1u;
+    // Wait for accumulation unit lc; false on abort.
+    auto wait_unit = [&](int lc) {
       int ok = 1;
-      if (lane == 0) ok = wait_bounded(tfull_bar(acc), aphase, abort_flag, kSiteEpilogue, true) ? 1 : 0;
+      if (lane == 0)
+        ok = wait_bounded(tfull_bar(lc & 1), static_cast<uint32_t>(lc >> 1) & 1u, abort_flag, kSiteEpilogue, true)
+                 ? 1
+                 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
-      const int64_t gm = static_cast<int64_t>(mb) * C::TILE_M + static_cast<int>(rank) * C::BM + quad * 32 + lane;
-      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * C::BN);
-#pragma unroll 1
-      for (int chunk = half; chunk < C::BN / 32; chunk += 2) {
-        uint32_t r[32];
-        tmem_ld32(trow + static_cast<uint32_t>(chunk * 32), r);
-        if (gm < M) epi_chunk<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + chunk * 32, r, fast != 0);
-      }
+      if (ok) tc_fence_after();
+      return ok != 0;
+    };
+    auto release_unit = [&](int lc) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if constexpr (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * acc);
-        else mbar_arrive(tempty_bar(acc));
+        if constexpr (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * (lc & 1));
+        else mbar_arrive(tempty_bar(lc & 1));
+      }
+    };
+    int lc = 0;
+    for (int t = unit; t < num_tiles; t += units) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int64_t gm = static_cast<int64_t>(mb) * C::TILE_M + static_cast<int>(rank) * C::BM + quad * 32 + lane;
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+      if constexpr (!kTf32) {
+        if (!wait_unit(lc)) break;
+        const uint32_t tacc = trow + static_cast<uint32_t>((lc & 1) * C::BN);
+#pragma unroll 1
+        for (int chunk = half; chunk < C::BN / 32; chunk += 2) {
+          uint32_t r[32];
+          tmem_ld32(tacc + static_cast<uint32_t>(chunk * 32), r);
+          if (gm < M) epi_chunk<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + chunk * 32, r, fast != 0);
+        }
+        release_unit(lc);
+        ++lc;
+      } else {
+        // Partial sums of PROMOTE k-blocks each, added in fp32 (round to
+        // nearest) in registers: 4 chunks x 32 columns per thread.
+        float sum[4][32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[q][j] = 0.f;
+        bool ok = true;
+        for (int kb0 = 0; kb0 < kblocks; kb0 += C::PROMOTE, ++lc) {
+          if (!wait_unit(lc)) {
+            ok = false;
+            break;
+          }
+          const uint32_t tacc = trow + static_cast<uint32_t>((lc & 1) * C::BN);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t r[32];
+            tmem_ld32(tacc + static_cast<uint32_t>((half + 2 * q) * 32), r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[q][j] += __uint_as_float(r[j]);
+          }
+          release_unit(lc);
+        }
+        if (!ok) break;
+        if (gm < M) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            epi_vals<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + (half + 2 * q) * 32, sum[q], fast != 0);
+        }
       }
     }
   }
@@ -558,38 +683,46 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Row-major [rows, cols] bf16 matrix, box {box_cols (inner), box_rows}.
+// Row-major [rows, cols] bf16 or fp32 matrix, box {box_cols (inner), box_rows}.
 int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
-             uint32_t box_rows) {
+             uint32_t box_rows, bool fp32 = false) {
   auto fn = encode_fn();
   if (!fn) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint64_t strides[1] = {cols * (fp32 ? 4 : 2)};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+  const CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return MCKE_OK;
 }
 
-using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, void*, int, int, int, EpilogueParams, int);
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, void*, int,
+                          int, int, EpilogueParams, int);
 
-template <bool kPair, bool kBf16, bool kBias>
+template <bool kPair, bool kTf32, bool kBf16, bool kBias>
 KernelFn pick_act(int act) {
   switch (act) {
-    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kBf16, kBias, MCKE_ACT_RELU>;
-    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kBf16, kBias, MCKE_ACT_GELU_ERF>;
-    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kBf16, kBias, MCKE_ACT_GELU_TANH>;
-    default: return gemm_tcgen05_kernel<kPair, kBf16, kBias, MCKE_ACT_NONE>;
+    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_RELU>;
+    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_GELU_ERF>;
+    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_GELU_TANH>;
+    default: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_NONE>;
   }
 }
 
-template <bool kPair>
+// bf16 operands: every output type; fp32 operands (3xTF32): fp32 output.
+template <bool kPair, bool kTf32>
 KernelFn pick(bool bf16, bool bias, int act) {
-  if (bf16) return bias ? pick_act<kPair, true, true>(act) : pick_act<kPair, true, false>(act);
-  return bias ? pick_act<kPair, false, true>(act) : pick_act<kPair, false, false>(act);
+  if constexpr (kTf32) {
+    (void)bf16;
+    return bias ? pick_act<kPair, true, false, true>(act) : pick_act<kPair, true, false, false>(act);
+  } else {
+    if (bf16) return bias ? pick_act<kPair, false, true, true>(act) : pick_act<kPair, false, true, false>(act);
+    return bias ? pick_act<kPair, false, false, true>(act) : pick_act<kPair, false, false, false>(act);
+  }
 }
 
 // Clusters of two that can be resident at once on this device (cached).
@@ -652,30 +785,46 @@ bool tcgen05_shape_ok(const void* a, const void* b, const void* c, int64_t m, in
          k < (1LL << 31) && aligned(a, 16) && aligned(b, 16);
 }
 
-int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m, int64_t n,
-                        int64_t k, const EpilogueParams& ep, cudaStream_t s,
-                        const void** kernel_out, std::size_t* smem_out) {
+namespace {
+
+// Common launcher of both operand types: bf16 (a, b) or 3xTF32 (a, b = the hi
+// parts, alo, blo = the lo parts).
+template <bool kTf32>
+int launch_tc(const void* a, const void* b, const void* alo, const void* blo, void* c, int64_t m, int64_t n,
+              int64_t k, const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out) {
   // A pair tile is 256 rows; below that the single-CTA shape wastes less.
-  const bool pair = m > Cfg<false>::BM;
+  const bool pair = m > Cfg<false, kTf32>::BM;
   const bool has_bias = ep.bias != nullptr;
-  KernelFn kfn = pair ? pick<true>(ep.out_bf16 != 0, has_bias, ep.act) : pick<false>(ep.out_bf16 != 0, has_bias, ep.act);
-  const std::size_t smem = pair ? Cfg<true>::SMEM : Cfg<false>::SMEM;
+  KernelFn kfn = pair ? pick<true, kTf32>(ep.out_bf16 != 0, has_bias, ep.act)
+                      : pick<false, kTf32>(ep.out_bf16 != 0, has_bias, ep.act);
+  const std::size_t smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
   if (kernel_out) *kernel_out = reinterpret_cast<const void*>(kfn);
   if (smem_out) *smem_out = smem;
   if (m == 0 || n == 0) return MCKE_OK;
   if (!ensure_smem_attr(kfn, smem)) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cannot set shared memory size");
-  CUtensorMap ta, tb;
-  MCKE_RETURN_IF(make_map(&ta, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), 64, Cfg<false>::BM));
-  MCKE_RETURN_IF(make_map(&tb, b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), 64, BK));
+  using C1 = Cfg<false, kTf32>;
+  CUtensorMap ta, tb, talo, tblo;
+  MCKE_RETURN_IF(make_map(&ta, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), C1::BK, C1::BM, kTf32));
+  if constexpr (kTf32) {
+    // b, blo are B^T [n, k]: boxes of B_COLS rows (pair: 128, single: 256) x 32 k
+    const uint32_t bcols = pair ? Cfg<true, true>::B_COLS : Cfg<false, true>::B_COLS;
+    MCKE_RETURN_IF(make_map(&tb, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k), C1::BK, bcols, true));
+    MCKE_RETURN_IF(make_map(&talo, alo, static_cast<uint64_t>(m), static_cast<uint64_t>(k), C1::BK, C1::BM, true));
+    MCKE_RETURN_IF(make_map(&tblo, blo, static_cast<uint64_t>(n), static_cast<uint64_t>(k), C1::BK, bcols, true));
+  } else {
+    MCKE_RETURN_IF(make_map(&tb, b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), C1::BOX_COLS, C1::BK));
+    talo = ta;
+    tblo = tb;
+  }
   const int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
-  const int tile_m = pair ? Cfg<true>::TILE_M : Cfg<false>::TILE_M;
+  const int tile_m = pair ? Cfg<true, kTf32>::TILE_M : Cfg<false, kTf32>::TILE_M;
   const int64_t tiles = ((m + tile_m - 1) / tile_m) * ((n + 255) / 256);
   if (tiles > 2147483647LL) return fail(MCKE_INVALID_ARGUMENT, "gemm (tcgen05): too many tiles");
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
   if (!pair) {
     int grid = sm_count();
     if (tiles < grid) grid = static_cast<int>(tiles);
-    kfn<<<grid, kThreads, smem, s>>>(ta, tb, c, mi, ni, ki, ep, fast);
+    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, c, mi, ni, ki, ep, fast);
     return MCKE_OK;
   }
   int pairs = max_pairs(kfn);
@@ -692,15 +841,104 @@ int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, c, mi, ni, ki, ep, fast);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, c, mi, ni, ki, ep, fast);
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
   return MCKE_OK;
 }
 
-namespace {
+// hi = x with the low 13 mantissa bits cleared (exact in tf32), lo = x - hi.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                                         float* __restrict__ lo, int64_t n) {
+  const int64_t n4 = n / 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = ld_stream_f4(x + 4 * i);
+    float4 h, l;
+    h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);
+    h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);
+    h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u);
+    h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);
+    l.x = v.x - h.x;
+    l.y = v.y - h.y;
+    l.z = v.z - h.z;
+    l.w = v.w - h.w;
+    reinterpret_cast<float4*>(hi)[i] = h;
+    reinterpret_cast<float4*>(lo)[i] = l;
+  }
+  for (int64_t i = 4 * n4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float h = __uint_as_float(__float_as_uint(x[i]) & 0xffffe000u);
+    hi[i] = h;
+    lo[i] = x[i] - h;
+  }
+}
+
+// B [k, n] -> B^T hi and lo [n, k]: 32 x 32 tiles through shared memory
+// (reads coalesced along n, writes along k).
+__global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* __restrict__ b,
+                                                                   float* __restrict__ hi_t,
+                                                                   float* __restrict__ lo_t, int64_t k,
+                                                                   int64_t n) {
+  __shared__ float tile[32][33];
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32, k0 = static_cast<int64_t>(blockIdx.y) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+#pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t kk = k0 + r, nn = n0 + tx;
+    tile[r][tx] = (kk < k && nn < n) ? __ldg(b + kk * n + nn) : 0.f;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t nn = n0 + r, kk = k0 + tx;
+    if (nn < n && kk < k) {
+      const float v = tile[tx][r];
+      const float h = __uint_as_float(__float_as_uint(v) & 0xffffe000u);
+      hi_t[nn * k + kk] = h;
+      lo_t[nn * k + kk] = v - h;
+    }
+  }
+}
+
+constexpr std::size_t kSplitAlign = 1024;
+std::size_t split_bytes(int64_t elems) {
+  return (static_cast<std::size_t>(elems) * 4 + kSplitAlign - 1) / kSplitAlign * kSplitAlign;
+}
+
+}  // namespace
+
+int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m, int64_t n,
+                        int64_t k, const EpilogueParams& ep, cudaStream_t s,
+                        const void** kernel_out, std::size_t* smem_out) {
+  return launch_tc<false>(a, b, nullptr, nullptr, c, m, n, k, ep, s, kernel_out, smem_out);
+}
+
+std::size_t gemm_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  return 2 * split_bytes(m * k) + 2 * split_bytes(k * n);
+}
+
+int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                       const EpilogueParams& ep, void* workspace, cudaStream_t s, const void** kernel_out,
+                       std::size_t* smem_out) {
+  if (m == 0 || n == 0 || k == 0)
+    return launch_tc<true>(nullptr, nullptr, nullptr, nullptr, c, 0, 0, 0, ep, s, kernel_out, smem_out);
+  char* w = static_cast<char*>(workspace);
+  float* ahi = reinterpret_cast<float*>(w);
+  float* alo = reinterpret_cast<float*>(w + split_bytes(m * k));
+  float* bhi = reinterpret_cast<float*>(w + 2 * split_bytes(m * k));
+  float* blo = reinterpret_cast<float*>(w + 2 * split_bytes(m * k) + split_bytes(k * n));
+  const int grid = 4 * sm_count();
+  split_tf32_kernel<<<grid, 256, 0, s>>>(a, ahi, alo, m * k);
+  const dim3 tgrid(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((k + 31) / 32));
+  if (tgrid.y > 65535u) return fail(MCKE_INVALID_ARGUMENT, "gemm (3xTF32): K too large for the transpose grid");
+  split_tf32_transpose_kernel<<<tgrid, 256, 0, s>>>(b, bhi, blo, k, n);
+  return launch_tc<true>(ahi, bhi, alo, blo, c, m, n, k, ep, s, kernel_out, smem_out);
+}
+
 // Watchdog self-test: one thread waits on an mbarrier that nothing arrives on.
 // The bounded wait gives up after its limit, records kSiteSelfTest and the
 // kernel returns normally, so the context stays usable.
+namespace {
 constexpr uint32_t kSiteSelfTest = 6;
 __global__ void watchdog_selftest_kernel() {
   __shared__ uint64_t bar;

@@ -80,6 +80,8 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_ipc_buffer_open": (i32, [vp, ctypes.POINTER(vp)]),
             "mcke_sm100_ipc_buffer_close": (i32, [vp, i32]),
             "mcke_sm100_gemm_f32": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
+            "mcke_sm100_gemm_f32_tc_workspace_bytes": (sz, [i64, i64, i64]),
+            "mcke_sm100_gemm_f32_tc": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, vp, i32, vp, sz, vp]),
             "mcke_sm100_gemm_bf16": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
             "mcke_sm100_gemm_bf16_ex": (i32, [vp, vp, vp, i32, i64, i64, i64, f32, f32, vp, i32, i32, vp]),
             "mcke_sm100_gemm_kernel_attrs": (i32, [i32, i32, vp]),
@@ -318,6 +320,33 @@ def gemm(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, variant="auto", bi
         _check(lib().mcke_sm100_gemm_bf16_ex(_ptr(a), _ptr(b), _ptr(c),
                                              DTYPE["bf16" if odt == torch.bfloat16 else "f32"],
                                              m, n, k, alpha, beta, _ptr(bias), _act(act), v, s))
+    return c
+
+
+def gemm_f32_tc_workspace_bytes(m: int, n: int, k: int) -> int:
+    return lib().mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k)
+
+
+def gemm_f32_tc(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, bias=None, act="none", workspace=None,
+                stream=None):
+    """float32 C = act(alpha * A @ B + beta * C + bias) on the tensor cores
+    (3xTF32, mcke_sm100_gemm_f32_tc); ``workspace`` holds the hi/lo split of A
+    and B (allocated here when not given)."""
+    _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
+    m, k = a.shape
+    k2, n = b.shape
+    if k != k2:
+        raise ValueError("inner dimensions differ")
+    if c is None:
+        c = torch.zeros((m, n), dtype=torch.float32, device=a.device)
+    _need(c, torch.float32, "c")
+    if bias is not None:
+        _need(bias, torch.float32, "bias")
+    need = gemm_f32_tc_workspace_bytes(m, n, k)
+    if workspace is None:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.device)
+    _check(lib().mcke_sm100_gemm_f32_tc(_ptr(a), _ptr(b), _ptr(c), m, n, k, alpha, beta, _ptr(bias), _act(act),
+                                        _ptr(workspace), workspace.numel(), _stream(a, stream)))
     return c
 
 

@@ -93,7 +93,9 @@ struct GemmParams {
   float alpha = 1.f;
   float beta = 0.f;  // must be 0 in a graph (C is not a graph input), as in the reference
   using Variant = kernels::GemmVariant;
-  Variant variant = Variant::kTiledRegBlock;  // f32 inputs; bf16 inputs always use kTcgen05Bf16
+  // f32 inputs: the reference's ladder (FFMA kernel) or kTcgen05Tf32x3 (tensor
+  // cores, which also takes bias/act); bf16 inputs always use kTcgen05Bf16.
+  Variant variant = Variant::kTiledRegBlock;
   kernels::GemmTile tile{};
   // Epilogue fusion (new): inputs are [A, B] or [A, B, bias]; act applied last.
   kernels::Activation act = kernels::Activation::kNone;
@@ -107,6 +109,8 @@ class GemmOp final : public Op {
   [[nodiscard]] Status launch(const OpContext&, const std::vector<Tensor>&, const std::vector<Tensor>&) override;
   [[nodiscard]] StatusOr<std::vector<TensorDesc>> infer(const std::vector<TensorDesc>&) const override;
   [[nodiscard]] OpCost cost(const std::vector<TensorDesc>&) const override;
+  // kTcgen05Tf32x3: the hi/lo split of A and B; 0 otherwise.
+  [[nodiscard]] std::size_t workspace_bytes(const std::vector<TensorDesc>&) const override;
   [[nodiscard]] const GemmParams& params() const { return p_; }
 
  private:

@@ -33,6 +33,7 @@ enum class GemmVariant : std::uint8_t {
   kNaive, kTiledSmem, kTiledRegBlock, kWarpTile, kCublasRef,
   kWarpTileNoDbuf, kWarpTileVec4, kNaiveUncoalesced,
   kTcgen05Bf16,
+  kTcgen05Tf32x3,  // new: f32 operands on the tensor cores (3xTF32), needs workspace
 };
 
 // The reference's tile descriptor; validated exactly as the reference does
@@ -91,6 +92,12 @@ struct GemmTile {
                                     GemmTile tile, rt::StreamHandle stream);
 // bf16 A[M,K] @ B[K,N] with a fused epilogue c = act(alpha*acc + beta*C + bias[col]),
 // C float32 or bfloat16 (beta must be 0 for bf16).
+// New: f32 GEMM on the tensor cores (3xTF32), c = act(alpha * A@B + beta * C +
+// bias); the workspace holds the hi/lo split of A and B.
+[[nodiscard]] std::size_t gemm_f32_tc_workspace_bytes(std::int64_t m, std::int64_t n, std::int64_t k) noexcept;
+[[nodiscard]] Status launch_gemm_f32_tc(const float* a, const float* b, float* c, std::int64_t m, std::int64_t n,
+                                        std::int64_t k, float alpha, float beta, const float* bias, Activation act,
+                                        void* workspace, std::size_t workspace_bytes, rt::StreamHandle stream);
 [[nodiscard]] Status launch_gemm_bf16(const std::uint16_t* a, const std::uint16_t* b, void* c, DType c_dtype,
                                      std::int64_t m, std::int64_t n, std::int64_t k, float alpha, float beta,
                                      const float* bias, Activation act, rt::StreamHandle stream);

@@ -23,6 +23,7 @@ bool gemm_tile_is_supported(GemmVariant v, const GemmTile& t) {
     case GemmVariant::kNaiveUncoalesced:
     case GemmVariant::kCublasRef:
     case GemmVariant::kTcgen05Bf16:
+    case GemmVariant::kTcgen05Tf32x3:
       return true;  // these own no GemmTile
     case GemmVariant::kTiledSmem:
       return t.bm == 32 && t.bn == 32 && t.bk == 32 && t.tm == 1 && t.tn == 1;
@@ -98,9 +99,22 @@ Status launch_gemm_f32(const float* a, const float* b, float* c, std::int64_t m,
     return UnimplementedError("launch_gemm_f32: the cuBLAS comparison row is not part of this library");
   if (variant == GemmVariant::kTcgen05Bf16)
     return InvalidArgumentError("launch_gemm_f32: kTcgen05Bf16 takes bf16 operands (launch_gemm_bf16)");
+  if (variant == GemmVariant::kTcgen05Tf32x3)
+    return InvalidArgumentError("launch_gemm_f32: kTcgen05Tf32x3 needs a workspace (launch_gemm_f32_tc)");
   if (!gemm_tile_is_supported(variant, tile))
     return InvalidArgumentError("launch_gemm_f32: tile is not one the variant is defined for; no fallback is applied");
   return from_capi(mcke_sm100_gemm_f32(a, b, c, m, n, k, alpha, beta, MCKE_GEMM_AUTO, st(stream)));
+}
+
+std::size_t gemm_f32_tc_workspace_bytes(std::int64_t m, std::int64_t n, std::int64_t k) noexcept {
+  return mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k);
+}
+
+Status launch_gemm_f32_tc(const float* a, const float* b, float* c, std::int64_t m, std::int64_t n, std::int64_t k,
+                          float alpha, float beta, const float* bias, Activation act, void* workspace,
+                          std::size_t workspace_bytes, rt::StreamHandle stream) {
+  return from_capi(mcke_sm100_gemm_f32_tc(a, b, c, m, n, k, alpha, beta, bias, static_cast<int>(act), workspace,
+                                          workspace_bytes, st(stream)));
 }
 
 Status launch_gemm_bf16(const std::uint16_t* a, const std::uint16_t* b, void* c, DType c_dtype, std::int64_t m,

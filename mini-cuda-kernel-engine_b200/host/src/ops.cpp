@@ -58,8 +58,10 @@ StatusOr<std::vector<TensorDesc>> GemmOp::infer(const std::vector<TensorDesc>& i
     return InvalidArgumentError("GemmOp: bias must be f32 of shape [N]");
   const bool bf16 = in[0].dtype == DType::kBF16;
   if (!bf16) {
-    if (in.size() == 3 || p_.act != kernels::Activation::kNone || p_.out_dtype != DType::kF32)
-      return InvalidArgumentError("GemmOp: epilogue fusion and bf16 output need bf16 operands");
+    const bool tc = p_.variant == kernels::GemmVariant::kTcgen05Tf32x3;
+    if (p_.out_dtype != DType::kF32) return InvalidArgumentError("GemmOp: f32 operands give an f32 output");
+    if (!tc && (in.size() == 3 || p_.act != kernels::Activation::kNone))
+      return InvalidArgumentError("GemmOp: epilogue fusion with f32 operands needs kTcgen05Tf32x3");
     if (p_.variant == kernels::GemmVariant::kTcgen05Bf16)
       return InvalidArgumentError("GemmOp: kTcgen05Bf16 needs bf16 operands");
     if (p_.variant == kernels::GemmVariant::kCublasRef)
@@ -87,6 +89,11 @@ OpCost GemmOp::cost(const std::vector<TensorDesc>& in) const {
   return c;
 }
 
+std::size_t GemmOp::workspace_bytes(const std::vector<TensorDesc>& in) const {
+  if (in.size() < 2 || in[0].dtype != DType::kF32 || p_.variant != kernels::GemmVariant::kTcgen05Tf32x3) return 0;
+  return kernels::gemm_f32_tc_workspace_bytes(in[0].shape[0], in[1].shape[1], in[0].shape[1]);
+}
+
 Status GemmOp::launch(const OpContext& ctx, const std::vector<Tensor>& in, const std::vector<Tensor>& out) {
   if ((in.size() != 2 && in.size() != 3) || out.size() != 1)
     return InvalidArgumentError("GemmOp::launch: expects 2 or 3 inputs and 1 output");
@@ -96,6 +103,12 @@ Status GemmOp::launch(const OpContext& ctx, const std::vector<Tensor>& in, const
     const float* b = in[1].data_as<float>();
     float* c = out[0].data_as<float>();
     if (!a || !b || !c) return InvalidArgumentError("GemmOp::launch: a tensor is undefined or not f32");
+    if (p_.variant == kernels::GemmVariant::kTcgen05Tf32x3) {
+      const float* bias = in.size() == 3 ? in[2].data_as<float>() : nullptr;
+      if (in.size() == 3 && !bias) return InvalidArgumentError("GemmOp::launch: bias is not f32");
+      return kernels::launch_gemm_f32_tc(a, b, c, m, n, k, p_.alpha, p_.beta, bias, p_.act, ctx.workspace,
+                                         ctx.workspace_bytes, ctx.stream);
+    }
     return kernels::launch_gemm_f32(a, b, c, m, n, k, p_.alpha, p_.beta, p_.variant, p_.tile, ctx.stream);
   }
   const bf16* a = in[0].data_as<bf16>();

@@ -20,6 +20,7 @@ PLACE = {"replicated": 0, "row_split": 1, "col_split": 2}
 PLACE_NAME = {v: k for k, v in PLACE.items()}
 ACT = {"none": 0, "relu": 1, "gelu_erf": 2, "gelu_tanh": 3}
 GEMM_VARIANT_TILED_REGBLOCK = 2  # the reference's GemmParams default
+GEMM_VARIANT_TCGEN05_TF32X3 = 9  # f32 operands on the tensor cores (3xTF32)
 _lib = None
 
 

@@ -137,6 +137,23 @@ def test_column_split_gemm_and_range_split_reduce(host):
     assert ex.placement(r) == "replicated"
 
 
+def test_tensor_core_f32_gemm_sizes_its_split_workspace(host):
+    # kTcgen05Tf32x3 asks for the hi/lo split of A and of its B column block
+    # (8 bytes per element of each), which the per-stream scratch must hold
+    m, k, n, d = 512, 256, 1024, 2
+    arenas = []
+    for variant in (host.GEMM_VARIANT_TILED_REGBLOCK, host.GEMM_VARIANT_TCGEN05_TF32X3):
+        g = host.Graph()
+        a, b = g.input("A", (m, k)), g.input("B", (k, n))
+        g.output(g.gemm(a, b, variant=variant))
+        g.finalize()
+        ex = host.Executor(g, devices=list(range(d)))
+        ex.plan_dry()
+        arenas.append(ex.arena_bytes(0))
+    split = 8 * (m * k + k * n // d)
+    assert arenas[1] - arenas[0] >= split - 4096  # (alignment slack)
+
+
 def test_sharding_refuses_what_needs_a_collective(host):
     g = host.Graph()
     a = g.input("A", (64, 64))

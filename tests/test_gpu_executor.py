@@ -310,3 +310,26 @@ def test_graph_mode_rejects_a_mixed_device_list():
     import mcke
     with pytest.raises(mcke.MckeError, match="distinct GPUs or one GPU repeated"):
         ex.run()
+
+
+def test_graph_gemm_f32_on_the_tensor_cores_with_bias_and_gelu():
+    # GemmOp with kTcgen05Tf32x3: the executor sizes the split workspace from
+    # workspace_bytes(); column-split over two shards of one GPU as well
+    m, k, n = 200, 96, 264
+    a = oracle.fill_random(m * k, 21).reshape(m, k)
+    b = oracle.fill_random(k * n, 22).reshape(k, n)
+    bias = oracle.fill_random(n, 23)
+    want = oracle.bias_act(oracle.gemm(a, b), bias, "gelu_tanh")
+    for devices in ([0], [0, 0]):
+        g = host.Graph()
+        ta, tb, tbias = g.input("A", (m, k)), g.input("B", (k, n)), g.input("bias", (n,))
+        c = g.gemm(ta, tb, bias=tbias, act="gelu_tanh", variant=host.GEMM_VARIANT_TCGEN05_TF32X3)
+        g.output(c)
+        g.finalize()
+        ex = host.Executor(g, devices=devices)
+        ex.plan()
+        for t, arr in ((ta, a), (tb, b), (tbias, bias)):
+            ex.set_input(t, arr)
+        ex.run()
+        r = oracle.compare(ex.output(c), want, oracle.tol_gemm(k), oracle.abs_tol_gemm(k))
+        assert r["mismatches"] == 0, (devices, r)

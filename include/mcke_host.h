@@ -57,9 +57,12 @@ mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_d
 /* As mcke_executor_create, with option flags:
  *   MCKE_EXECUTOR_CUDA_GRAPH  capture the first run into one CUDA graph per GPU
  *                             and replay it (devices all distinct or one GPU repeated);
- *   MCKE_EXECUTOR_POISON      fill intermediates with 0xFF before each run (tests). */
+ *   MCKE_EXECUTOR_POISON      fill intermediates with 0xFF before each run (tests);
+ *   MCKE_EXECUTOR_NCCL_EXCHANGE  on distinct GPUs, all-gather a full reduce's partials
+ *                             with NCCL instead of the one-kernel peer-to-peer combine. */
 #define MCKE_EXECUTOR_CUDA_GRAPH 1u
 #define MCKE_EXECUTOR_POISON 2u
+#define MCKE_EXECUTOR_NCCL_EXCHANGE 4u
 mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
                                        unsigned flags);
 void mcke_executor_destroy(mcke_executor* e);

@@ -178,10 +178,13 @@ int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count
  * peer_buffers: DEVICE array of `world` pointers to the ranks' exchange
  * buffers as mapped in this process (this rank's own at index `rank`), each
  * mcke_sm100_reduce_p2p_buffer_bytes(world) bytes (2 * world 64-byte exchange
- * slots, then 444 slots for this rank's pass-1 partials; every 8-byte word
- * carries 4 data bytes and the epoch, so no fence orders data and flag),
- * zeroed before first use.  epoch: 1, 2, 3, ... < 2^32, one per call, the same
- * on every rank; calls of one rank are ordered on one stream.  Every rank must
+ * slots, then 444 slots for this rank's pass-1 partials, then an epoch
+ * counter; every 8-byte word of a slot carries 4 data bytes and the epoch, so
+ * no fence orders data and flag), zeroed before first use.  epoch: 1, 2, 3,
+ * ... < 2^32, one per call, the same on every rank; or 0 on every call: the
+ * kernel then takes the next value of the counter in this rank's buffer and
+ * advances it (what a captured CUDA graph needs, since it replays its launch
+ * arguments).  Calls of one rank are ordered on one stream.  Every rank must
  * make the call for each epoch; a rank that does not arrive makes the others
  * give up after 1 s with argmax -1 and MCKE_INTERNAL from
  * mcke_sm100_check_device_errors(). */

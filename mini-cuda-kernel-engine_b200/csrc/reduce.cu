@@ -179,7 +179,27 @@ struct P2pArgs {
   uint32_t parity;
   int world;
   int rank;
+  int auto_epoch;  // 1: the epoch is the counter after the part area, advanced by each call
 };
+
+// Counter of the automatic epochs: the 64-byte slot after the part area.
+__device__ __forceinline__ unsigned long long* epoch_counter(const P2pArgs& a) {
+  return reinterpret_cast<unsigned long long*>(a.peers[a.rank] + 2 * a.world + kFullCtaCap);
+}
+
+// With automatic epochs, resolve this call's tag (every CTA reads the counter
+// before it publishes; CTA 0 advances it only after all CTAs have published).
+__device__ __forceinline__ void resolve_tag(P2pArgs& a) {
+  if (!a.auto_epoch) return;
+  __shared__ uint32_t s_tag;
+  if (threadIdx.x == 0) {
+    uint32_t t = static_cast<uint32_t>(*reinterpret_cast<volatile unsigned long long*>(epoch_counter(a)) + 1ull);
+    s_tag = t == 0u ? 1u : t;  // 0 marks an empty slot
+  }
+  __syncthreads();
+  a.tag = s_tag;
+  a.parity = a.tag & 1u;
+}
 
 __device__ __forceinline__ void ll_store(LLSlot* slot, const Part& p, uint32_t tag) {
   const unsigned long long t = static_cast<unsigned long long>(tag) << 32;
@@ -257,13 +277,15 @@ __device__ void p2p_publish_and_combine(const Part& mine, const P2pArgs& a, Part
     res.max = t.m;
     res.argmax = all_ok ? t.i : -1;
     *a.out = res;
+    if (a.auto_epoch) *reinterpret_cast<volatile unsigned long long*>(epoch_counter(a)) = a.tag;
   }
 }
 
 template <bool kP2p>
 __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
-                                                                      Part* __restrict__ parts, P2pArgs p2p) {
+                                                                      Part* __restrict__ parts, P2pArgs p2p_in) {
+  P2pArgs p2p = p2p_in;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ Part red[kWarps];
   const float4* ring = reinterpret_cast<const float4*>(smem);
@@ -364,6 +386,7 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
     // so the rest are the identity) -- which makes the shard partial
     // bit-identical to the two-launch path, and runs the exchange.  Only CTA 0
     // waits, on CTAs that never wait, so the grid cannot deadlock.
+    resolve_tag(p2p);
     LLSlot* local = p2p.peers[p2p.rank] + 2 * p2p.world;
     if (tid == 0) ll_store(local + blockIdx.x, p, p2p.tag);
     if (blockIdx.x != 0) return;
@@ -802,15 +825,17 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
 namespace mcke_sm100 {
 namespace {
 // Only for an empty shard (no pass-1 CTA to run the exchange).
-__global__ void __launch_bounds__(kThreads) reduce_p2p_empty_kernel(P2pArgs a) {
+__global__ void __launch_bounds__(kThreads) reduce_p2p_empty_kernel(P2pArgs a_in) {
   extern __shared__ __align__(16) uint8_t scratch[];
+  P2pArgs a = a_in;
+  resolve_tag(a);
   p2p_publish_and_combine(part_identity(), a, reinterpret_cast<Part*>(scratch));
 }
 }  // namespace
 }  // namespace mcke_sm100
 
 extern "C" size_t mcke_sm100_reduce_p2p_buffer_bytes(int world) {
-  return world > 0 ? static_cast<size_t>(2 * world + kFullCtaCap) * sizeof(LLSlot) : 0;
+  return world > 0 ? static_cast<size_t>(2 * world + kFullCtaCap + 1) * sizeof(LLSlot) : 0;
 }
 
 extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
@@ -821,8 +846,7 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   if (!out || !peer_buffers) return fail(MCKE_INVALID_ARGUMENT, "%s: null output or peer table", who);
   if (world < 1 || world > 1024 || rank < 0 || rank >= world)
     return fail(MCKE_INVALID_ARGUMENT, "%s: bad world/rank %d/%d", who, world, rank);
-  if (epoch == 0 || epoch > 0xffffffffull)
-    return fail(MCKE_INVALID_ARGUMENT, "%s: epoch must be in [1, 2^32) (0 marks an empty slot)", who);
+  if (epoch > 0xffffffffull) return fail(MCKE_INVALID_ARGUMENT, "%s: epoch must be below 2^32", who);
   if (n < 0 || (n > 0 && !x)) return fail(MCKE_INVALID_ARGUMENT, "%s: bad input", who);
   if (index_base < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative index_base", who);
   if (n > 0 && !aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
@@ -834,6 +858,7 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   a.parity = static_cast<uint32_t>(epoch & 1);
   a.world = world;
   a.rank = rank;
+  a.auto_epoch = epoch == 0 ? 1 : 0;
   if (n == 0) {
     reduce_p2p_empty_kernel<<<1, kThreads, static_cast<size_t>(world) * sizeof(Part), s>>>(a);
     return check_launch(who);

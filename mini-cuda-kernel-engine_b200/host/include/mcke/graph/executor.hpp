@@ -55,6 +55,10 @@ struct ExecutorOptions {
   // Capture the first run_async into CUDA graphs and replay them.  Needs a
   // device list that is all distinct GPUs or one GPU repeated.
   bool use_graph = false;
+  // Distinct GPUs: exchange a full reduce's partials with the one-kernel
+  // peer-to-peer combine (needs peer access between every pair; otherwise,
+  // or when false, NCCL all-gathers them).
+  bool p2p_exchange = true;
 };
 
 struct TensorPlan {

@@ -57,6 +57,10 @@ struct OpContext {
   int num_shards = 1;
   std::int64_t index_base = 0;  // flat index of this shard's first element (range shards)
   void* exchange = nullptr;     // exchange_bytes() of device scratch for the partial
+  // Set when the executor exchanges this node's partials peer to peer: a
+  // device array of the shards' exchange buffers; the op then does the whole
+  // step (no exchange/finish).
+  void* const* p2p_peers = nullptr;
 };
 
 struct OpCost {

@@ -81,6 +81,12 @@ struct GemmTile {
 [[nodiscard]] Status launch_reduce_full_partial_f32(const float* x, std::int64_t n, std::int64_t index_base,
                                                    void* partial, void* workspace, std::size_t workspace_bytes,
                                                    rt::StreamHandle stream);
+// New: one rank's step of a sharded full reduce with the peer-to-peer combine
+// (epoch taken from the counter in this rank's exchange buffer).
+[[nodiscard]] std::size_t reduce_p2p_buffer_bytes(int world) noexcept;
+[[nodiscard]] Status launch_reduce_full_p2p_f32(const float* x, std::int64_t n, std::int64_t index_base,
+                                                void* const* peer_buffers, int world, int rank, void* out,
+                                                rt::StreamHandle stream);
 [[nodiscard]] Status launch_reduce_combine(const void* partials, std::int64_t count, void* out,
                                           rt::StreamHandle stream);
 

@@ -113,6 +113,7 @@ mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int nu
   o.streams_per_device = streams_per_device > 0 ? streams_per_device : 4;
   o.use_graph = (flags & MCKE_EXECUTOR_CUDA_GRAPH) != 0;
   o.poison_buffers = (flags & MCKE_EXECUTOR_POISON) != 0;
+  o.p2p_exchange = (flags & MCKE_EXECUTOR_NCCL_EXCHANGE) == 0;
   auto* e = new mcke_executor();
   e->ex = std::make_unique<mcke::GraphExecutor>(g->g, o);
   return e;

@@ -55,11 +55,22 @@ struct GraphExecutor::Impl {
   std::vector<Dev> devs;
   bool ran_once = false;
   bool peer_copy = false;
+  // Peer-to-peer exchange: per exchanging node and device, the exchange
+  // buffer and the device table of all devices' buffers.
+  bool p2p = false;
+  std::vector<std::vector<void*>> p2p_buf;    // [node][device]
+  std::vector<std::vector<void*>> p2p_table;  // [node][device]
   // Graph mode: one instantiated graph per capture group (a GPU); origin[i] is
   // the device entry whose stream 0 launches execs[i] and carries its timing.
   std::vector<cudaGraphExec_t> execs;
   std::vector<int> origins;
   ~Impl() {
+    for (std::size_t nid = 0; nid < p2p_buf.size(); ++nid)
+      for (std::size_t d = 0; d < p2p_buf[nid].size(); ++d) {
+        rt::DeviceGuard g(devs[d].device);
+        if (p2p_buf[nid][d]) cudaFree(p2p_buf[nid][d]);
+        if (p2p_table[nid][d]) cudaFree(p2p_table[nid][d]);
+      }
     for (std::size_t i = 0; i < execs.size(); ++i) {
       rt::DeviceGuard g(devs[origins[i]].device);
       cudaGraphExecDestroy(execs[i]);
@@ -402,7 +413,46 @@ Status GraphExecutor::plan() {
         }
     }
   }
-  if (any_exchange && D > 1 && !impl_->peer_copy) {
+  if (any_exchange && D > 1 && !impl_->peer_copy && opts_.p2p_exchange) {
+    bool can = true;
+    for (int a = 0; a < D && can; ++a)
+      for (int b = 0; b < D && can; ++b) {
+        int ok = 0;
+        if (a != b && (cudaDeviceCanAccessPeer(&ok, opts_.devices[a], opts_.devices[b]) != cudaSuccess || !ok)) can = false;
+      }
+    cudaGetLastError();
+    if (can) {
+      for (int a = 0; a < D; ++a) {
+        rt::DeviceGuard g(opts_.devices[a]);
+        for (int b = 0; b < D; ++b) {
+          if (a == b) continue;
+          const cudaError_t e = cudaDeviceEnablePeerAccess(opts_.devices[b], 0);
+          if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+            return InternalError(std::string("cudaDeviceEnablePeerAccess: ") + cudaGetErrorString(e));
+          cudaGetLastError();
+        }
+      }
+      const std::size_t bytes = kernels::reduce_p2p_buffer_bytes(D);
+      impl_->p2p_buf.assign(g_.num_nodes(), std::vector<void*>(D, nullptr));
+      impl_->p2p_table.assign(g_.num_nodes(), std::vector<void*>(D, nullptr));
+      for (NodeId nid = 0; nid < g_.num_nodes(); ++nid) {
+        if (g_.node(nid).op->exchange_bytes() == 0) continue;
+        for (int d = 0; d < D; ++d) {
+          rt::DeviceGuard g(opts_.devices[d]);
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMalloc(&impl_->p2p_buf[nid][d], bytes));
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMemset(impl_->p2p_buf[nid][d], 0, bytes));
+        }
+        for (int d = 0; d < D; ++d) {
+          rt::DeviceGuard g(opts_.devices[d]);
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMalloc(&impl_->p2p_table[nid][d], D * sizeof(void*)));
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMemcpy(impl_->p2p_table[nid][d], impl_->p2p_buf[nid].data(), D * sizeof(void*),
+                                               cudaMemcpyHostToDevice));
+        }
+      }
+      impl_->p2p = true;
+    }
+  }
+  if (any_exchange && D > 1 && !impl_->peer_copy && !impl_->p2p) {
     std::vector<ncclComm_t> comms(D);
     MCKE_RETURN_IF_ERROR(nccl_status(ncclCommInitAll(comms.data(), D, opts_.devices.data()), "ncclCommInitAll"));
     for (int d = 0; d < D; ++d) impl_->devs[d].comm = comms[d];
@@ -597,6 +647,8 @@ Status GraphExecutor::enqueue(bool capturing) {
           ctx[d].index_base = (full.rank() >= 2 ? full.rows() : full.numel()) * d / D * inner;
       }
       if (exchange_offset_[d][nid] >= 0) ctx[d].exchange = static_cast<char*>(dv.arena) + exchange_offset_[d][nid];
+      if (impl_->p2p && !impl_->p2p_table.empty() && impl_->p2p_table[nid][d])
+        ctx[d].p2p_peers = static_cast<void* const*>(impl_->p2p_table[nid][d]);
     }
     for (int d = 0; d < D; ++d) {
       rt::DeviceGuard g(impl_->devs[d].device);
@@ -604,7 +656,7 @@ Status GraphExecutor::enqueue(bool capturing) {
       if (!st.ok()) return Status(st.code(), "node '" + n.name + "' on device " + std::to_string(ctx[d].device) + ": " + st.message());
     }
     const std::size_t eb = n.op->exchange_bytes();
-    if (eb > 0) {
+    if (eb > 0 && !(impl_->p2p && D > 1)) {
       std::vector<void*> gathered(D);
       for (int d = 0; d < D; ++d) gathered[d] = static_cast<char*>(ctx[d].exchange) + eb;
       if (D > 1 && impl_->peer_copy) {

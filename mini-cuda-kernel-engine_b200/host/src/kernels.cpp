@@ -83,6 +83,14 @@ Status launch_reduce_full_partial_f32(const float* x, std::int64_t n, std::int64
                                                       workspace, workspace_bytes, st(stream)));
 }
 
+std::size_t reduce_p2p_buffer_bytes(int world) noexcept { return mcke_sm100_reduce_p2p_buffer_bytes(world); }
+
+Status launch_reduce_full_p2p_f32(const float* x, std::int64_t n, std::int64_t index_base, void* const* peer_buffers,
+                                  int world, int rank, void* out, rt::StreamHandle stream) {
+  return from_capi(mcke_sm100_reduce_full_p2p_f32(x, n, index_base, peer_buffers, world, rank, 0,
+                                                  static_cast<mcke_reduce_result*>(out), st(stream)));
+}
+
 Status launch_reduce_combine(const void* partials, std::int64_t count, void* out, rt::StreamHandle stream) {
   return from_capi(mcke_sm100_reduce_combine(static_cast<const mcke_reduce_partial*>(partials), count,
                                              static_cast<mcke_reduce_result*>(out), st(stream)));

@@ -268,10 +268,15 @@ std::size_t FullReduceOp::workspace_bytes(const std::vector<TensorDesc>& in) con
   return in.empty() ? 0 : kernels::reduce_full_workspace_bytes(in[0].shape.numel());
 }
 
-Status FullReduceOp::launch(const OpContext& ctx, const std::vector<Tensor>& in, const std::vector<Tensor>&) {
+Status FullReduceOp::launch(const OpContext& ctx, const std::vector<Tensor>& in, const std::vector<Tensor>& outs) {
   if (in.size() != 1) return InvalidArgumentError("FullReduceOp::launch: expects 1 input");
   const float* x = in[0].data_as<float>();
   if (!x && in[0].shape.numel() > 0) return InvalidArgumentError("FullReduceOp::launch: x undefined or not f32");
+  if (ctx.p2p_peers) {
+    if (outs.size() != 1 || !outs[0].data) return InvalidArgumentError("FullReduceOp::launch: no output");
+    return kernels::launch_reduce_full_p2p_f32(x, in[0].shape.numel(), ctx.index_base, ctx.p2p_peers,
+                                               ctx.num_shards, ctx.shard, outs[0].data, ctx.stream);
+  }
   if (!ctx.exchange) return InternalError("FullReduceOp::launch: no exchange buffer planned");
   return kernels::launch_reduce_full_partial_f32(x, in[0].shape.numel(), ctx.index_base, ctx.exchange, ctx.workspace,
                                                  ctx.workspace_bytes, ctx.stream);

@@ -139,10 +139,10 @@ class Executor:
     """mcke::GraphExecutor over the given CUDA device ordinals."""
 
     def __init__(self, graph: Graph, devices=(0,), streams_per_device: int = 4, cuda_graph: bool = False,
-                 poison: bool = False):
+                 poison: bool = False, nccl_exchange: bool = False):
         self.graph = graph
         devs = (ctypes.c_int * len(devices))(*devices)
-        flags = (1 if cuda_graph else 0) | (2 if poison else 0)
+        flags = (1 if cuda_graph else 0) | (2 if poison else 0) | (4 if nccl_exchange else 0)
         self._h = lib().mcke_executor_create_ex(graph._h, devs, len(devices), streams_per_device, flags)
         if not self._h:
             raise MckeError(2, "mcke_executor_create failed")

@@ -161,7 +161,8 @@ def test_dag_on_two_gpus_matches_one():
 
 
 @two_gpus
-def test_nccl_sharded_full_reduce_on_two_gpus():
+@pytest.mark.parametrize("nccl", [False, True])
+def test_sharded_full_reduce_on_two_gpus(nccl):
     n = 2_000_003
     v = oracle.fill_random(n, 8)
     v[1_999_990] = v[40] = np.float32(1.75)
@@ -170,10 +171,10 @@ def test_nccl_sharded_full_reduce_on_two_gpus():
     r = g.reduce_full(x)
     g.output(r)
     g.finalize()
-    ex = host.Executor(g, devices=[0, 1])
+    ex = host.Executor(g, devices=[0, 1], nccl_exchange=nccl)
     ex.plan()
     ex.set_input(x, v)
-    for _ in range(2):
+    for _ in range(3):
         ex.run()
         import mcke
         s, m, i = mcke.decode_result(ex.output(r).tobytes())

@@ -33,6 +33,20 @@ def test_library_exports_every_declared_symbol(mcke):
     assert exported == set(names)
 
 
+def test_host_library_exports_every_declared_symbol(mcke):
+    # include/mcke_host.h (graph / executor C-ABI over the C++ host layer)
+    import re
+    lib_path = os.path.join(PKG, "lib", "libmcke_host.so")
+    if not os.path.exists(lib_path):
+        subprocess.run(["make", "-s", "-C", os.path.join(PKG, "host")], check=True)
+    with open(os.path.join(ROOT, "include", "mcke_host.h")) as f:
+        names = sorted(set(re.findall(r"\b(mcke_(?:graph|executor|host)_\w+)\s*\(", f.read())))
+    assert len(names) >= 20
+    l = ctypes.CDLL(lib_path)
+    missing = [n for n in names if not hasattr(l, n)]
+    assert not missing, missing
+
+
 def test_argument_validation_needs_no_device(mcke):
     l = mcke.lib()
     assert l.mcke_sm100_version() >= 100

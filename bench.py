@@ -600,16 +600,32 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         ach = loc_flops / (kms * 1e-3) / 1e12
         fs = max(2, min(steps, 3))
         ms_s, per_s = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c, variant="simt"), fs, 1, None)
+        # Library ceilings on the same shard, measured here as denominators:
+        # cuBLAS fp32 (FFMA) and cuBLAS with TF32 tensor cores (one pass).
+        prev = torch.backends.cuda.matmul.allow_tf32
+        try:
+            torch.backends.cuda.matmul.allow_tf32 = False
+            ms_cs, _ = timed_steps(torch, dist, lambda: torch.matmul(a, b, out=c), fs, 1, None)
+            torch.backends.cuda.matmul.allow_tf32 = True
+            ms_ct, _ = timed_steps(torch, dist, lambda: torch.matmul(a, b, out=c), fs, 1, None)
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
+        cublas_sgemm = loc_flops * fs / (ms_cs * 1e-3) / 1e12
+        cublas_tf32 = loc_flops * fs / (ms_ct * 1e-3) / 1e12
         out["gemm_f32_8192^3"] = {
             "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "kernel_ms": round(kms, 3),
             "path": "3xTF32 on tcgen05 (split pass + kind::tf32 MMAs, fp32 partial sums promoted every 128 k)",
             "tf32_mma_tflops": round(3 * ach, 1),
             "frac_of_tf32_nominal": round(3 * ach / TF32_NOMINAL_TFLOPS, 4),
-            "frac_of_bf16_peak_scaled": round(3 * ach / (peaks["bf16_tflops"] * TF32_NOMINAL_TFLOPS / 2250.0), 4),
+            "cublas_tf32_one_pass_tflops_per_gpu": round(cublas_tf32, 1),
+            "frac_of_cublas_tf32_mma_rate": round(3 * ach / cublas_tf32, 4),
             "ffma_kernel_tflops": round(GEMM_FLOPS * fs / (ms_s * 1e-3) / 1e12, 2),
-            "note": "tf32 MMA rate = 3 x fp32 flops; peak: nominal dense tf32 (1100 TFLOP/s) and the measured bf16 "
-                    "burst scaled by the nominal tf32/bf16 ratio"}
+            "cublas_sgemm_tflops_per_gpu": round(cublas_sgemm, 2),
+            "ffma_frac_of_cublas_sgemm": round(GEMM_FLOPS / g * fs / (ms_s * 1e-3) / 1e12 / cublas_sgemm, 4),
+            "note": "tf32 MMA rate = 3 x fp32 flops, compared with nominal dense tf32 (1100 TFLOP/s) and with "
+                    "cuBLAS's one-pass TF32 GEMM on the same shard (torch.matmul, allow_tf32); the FFMA kernel "
+                    "compared with cuBLAS SGEMM (the reference's kCublasRef ceiling row)"}
         del a, b, c, ws
     return out
 

@@ -430,23 +430,49 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                 mcke.reduce_combine(mshard.exchange_partials(part, g), g, out=res)
             ms_n, _ = timed_steps(torch, dist, launch_nccl, steps, warm, flush)
             nccl_ms = ms_n / steps
+            nccl_result = mcke.decode_result(res)
             p2p = mshard.P2PExchange(dev)
             launch = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
         ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
         kms = statistics.mean(per)
         ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9
+        p2p_matches = None
         if p2p is not None:
             torch.cuda.synchronize()
             mcke.check_device_errors()
             p2p.close()
+            got = mcke.decode_result(res)
+            # max and argmax bit for bit; the sums fold the same partials in
+            # two fixed orders, so within a float ulp
+            p2p_matches = bool(got[1:] == nccl_result[1:] and
+                               abs(got[0] - nccl_result[0]) <= float(np.spacing(np.float32(abs(nccl_result[0])))))
         out["reduce_full_fp32_2^28"] = {
             "value": round(REDUCE_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
             "step_ms": round(kms, 5),
             "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
             "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
+            "p2p_result_matches_nccl": p2p_matches,
             "traffic": traffic.get("reduce_full_stream_kernel")}
         del xr
+
+    if "row_reduce" in want:
+        # the reference's ReduceOp (row-wise sum over the last dim) on config
+        # 2's shape: rows sharded, 128 MiB read per full batch
+        r0, r1 = shard(ROWS)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(3)
+        xr = torch.rand(r1 - r0, COLS, generator=gen, device=dev) * 2 - 1
+        yr = torch.empty(r1 - r0, device=dev)
+        ms, per = timed_steps(torch, dist, lambda: mcke.reduce_row(xr, "sum", out=yr), steps, warm, flush)
+        kms = statistics.mean(per)
+        moved = ROWS * COLS * 4 + ROWS * 4
+        ach = ((r1 - r0) * COLS * 4 + (r1 - r0) * 4) / (kms * 1e-3) / 1e9
+        out["row_reduce_sum_fp32_32768x1024"] = {
+            "value": round(moved * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
+            "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
+            "kernel_ms": round(kms, 5), "algorithmic_bytes": moved}
+        del xr, yr
 
     if "gemm_bf16" in want:
         n0, n1 = shard(GEMM_N)
@@ -690,7 +716,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mcke", "reference"], default="mcke")
-    ap.add_argument("--ops", default="bias_gelu,reduce,gemm_bf16,dag_fused,dag_unfused,dag_fanout,gemm_f32",
+    ap.add_argument("--ops", default="bias_gelu,reduce,row_reduce,gemm_bf16,dag_fused,dag_unfused,dag_fanout,gemm_f32",
                     help="comma list of extra configs to report under 'ops' ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default="", help="run one small case per named kernel for ncu and exit")

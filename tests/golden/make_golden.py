@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Regenerate the committed golden fixtures under tests/golden/.
 
-Run in a container where the reference tree exists (default /root/reference):
+Run where the reference tree exists (its path with --ref; the default is the
+build container's checkout):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref PATH_TO_REFERENCE_TREE]
 
 It writes two files, both consumed by tests/test_oracle.py and the GPU parity
 tests, none of which read the reference tree at run time:

@@ -60,7 +60,16 @@ typedef enum { MCKE_SOFTMAX_THREE_PASS = 0, MCKE_SOFTMAX_ONLINE = 1 } mcke_softm
  * so its values are not reused).  AUTO picks TCGEN05 for bf16 when the shape
  * meets the TMA rules (K % 8 == 0, N % 8 == 0, 16-byte aligned A and B),
  * else SIMT; for f32 it picks SIMT. */
-typedef enum { MCKE_GEMM_AUTO = 0, MCKE_GEMM_SIMT = 1, MCKE_GEMM_TCGEN05 = 2 } mcke_gemm_variant;
+/* TCGEN05_WIDE / TCGEN05_NARROW: the tcgen05 kernel with its pair tile forced
+ * to 256 x 512 / 256 x 256 (AUTO and TCGEN05 choose; shapes that cannot use the
+ * pair tile ignore the choice). */
+typedef enum {
+  MCKE_GEMM_AUTO = 0,
+  MCKE_GEMM_SIMT = 1,
+  MCKE_GEMM_TCGEN05 = 2,
+  MCKE_GEMM_TCGEN05_WIDE = 3,
+  MCKE_GEMM_TCGEN05_NARROW = 4
+} mcke_gemm_variant;
 /* Element type of a GEMM output. */
 typedef enum { MCKE_DTYPE_F32 = 0, MCKE_DTYPE_BF16 = 2 } mcke_dtype;
 

@@ -67,8 +67,10 @@ int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m
     return fail(MCKE_INVALID_ARGUMENT, "%s: beta must be 0 for a bf16 output", who);
   if (act < MCKE_ACT_NONE || act > MCKE_ACT_GELU_TANH)
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
-  if (variant != MCKE_GEMM_AUTO && variant != MCKE_GEMM_SIMT && variant != MCKE_GEMM_TCGEN05)
+  if (variant < MCKE_GEMM_AUTO || variant > MCKE_GEMM_TCGEN05_NARROW)
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
+  const int tile = variant == MCKE_GEMM_TCGEN05_WIDE ? 2 : variant == MCKE_GEMM_TCGEN05_NARROW ? 1 : 0;
+  if (tile != 0) variant = MCKE_GEMM_TCGEN05;
   if (!bf16_in && variant == MCKE_GEMM_TCGEN05)
     return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands; no fallback is applied", who);
 
@@ -89,7 +91,7 @@ int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m
                 who);
   if (tc_ok && variant != MCKE_GEMM_SIMT) {
     MCKE_RETURN_IF(launch_gemm_tcgen05(static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b),
-                                       c, m, n, k, ep, s, nullptr, nullptr));
+                                       c, m, n, k, ep, s, nullptr, nullptr, tile));
   } else {
     MCKE_RETURN_IF(launch_gemm_simt(a, b, c, m, n, k, bf16_in, ep, s, nullptr));
   }

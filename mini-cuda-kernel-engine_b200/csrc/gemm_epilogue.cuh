@@ -66,9 +66,10 @@ __device__ __forceinline__ void epilogue_store4(const EpilogueParams& ep, void* 
 int launch_gemm_simt(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k,
                      bool bf16_in, const EpilogueParams& ep, cudaStream_t s,
                      const void** kernel_out);
+// tile: 0 = choose the pair tile, 1 = 256 x 256, 2 = 256 x 512.
 int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m, int64_t n,
                         int64_t k, const EpilogueParams& ep, cudaStream_t s,
-                        const void** kernel_out, std::size_t* smem_out);
+                        const void** kernel_out, std::size_t* smem_out, int tile = 0);
 bool tcgen05_shape_ok(const void* a, const void* b, const void* c, int64_t m, int64_t n, int64_t k,
                       bool out_bf16);
 // fp32 GEMM on the tensor cores in the 3xTF32 form (split kernels, then the

@@ -66,8 +66,9 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // 320
 constexpr int kGroupM = 16;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
-template <bool kPair, bool kTf32 = false>
+template <bool kPair, bool kTf32 = false, bool kWide = false>
 struct Cfg {
+  static_assert(!kWide || (kPair && !kTf32), "the wide tile is a bf16 pair shape");
   static constexpr int ELEM = kTf32 ? 4 : 2;          // operand bytes
   static constexpr int BK = 128 / ELEM;               // k-block: one 128-byte swizzle row
   static constexpr int UMMA_K = 32 / ELEM;            // k per MMA: 32 bytes of a row
@@ -76,13 +77,17 @@ struct Cfg {
   static_assert(B_BOX_BYTES == 128 * BK, "a B box is BK rows of 128 bytes");
   static constexpr int OPS = kTf32 ? 2 : 1;           // hi (+ lo) copies of each operand
   static constexpr int BM = 128;                      // rows of A per CTA
-  static constexpr int BN = 256;                      // output columns per tile
+  static constexpr int MMA_N = 256;                   // columns per MMA instruction
+  static constexpr int BN = kWide ? 512 : 256;        // output columns per tile
+  static constexpr int NH = BN / MMA_N;               // MMA instructions per k-step (N halves)
+  static constexpr int NACC = kWide ? 1 : 2;          // TMEM accumulators (512 columns in all)
   static constexpr int TILE_M = kPair ? 2 * BM : BM;  // output rows per tile
   static constexpr int B_COLS = kPair ? BN / 2 : BN;  // columns of B per CTA
+  static constexpr int B_HALF_COLS = B_COLS / NH;     // this CTA's columns of one MMA's B
   static constexpr int A_STAGE = BM * BK * ELEM;
   static constexpr int B_STAGE = B_COLS * BK * ELEM;
   static constexpr int STAGE = OPS * (A_STAGE + B_STAGE);  // A, B, then A_lo, B_lo
-  static constexpr int STAGES = kTf32 ? (kPair ? 3 : 2) : (kPair ? 6 : 4);
+  static constexpr int STAGES = kTf32 ? (kPair ? 3 : 2) : (kWide ? 4 : (kPair ? 6 : 4));
   // k-blocks per tensor-memory accumulation unit: tf32 partial sums are moved
   // to registers every PROMOTE k-blocks (128 k); bf16 accumulates a whole tile.
   static constexpr int PROMOTE = kTf32 ? 4 : 0;
@@ -97,11 +102,13 @@ struct Cfg {
   static constexpr uint32_t FMT = kTf32 ? 2u : 1u;
   static constexpr uint32_t B_MN_MAJOR = kTf32 ? 0u : 1u;  // tf32: B^T, K-major
   static constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | (0u << 15) | (B_MN_MAJOR << 16) |
-                                    (static_cast<uint32_t>(BN >> 3) << 17) |
+                                    (static_cast<uint32_t>(MMA_N >> 3) << 17) |
                                     (static_cast<uint32_t>(TILE_M >> 4) << 24);
+  static_assert(IDESC != 0u && NH >= 1 && B_HALF_COLS > 0 && FMT > 0u && B_MN_MAJOR <= 1u, "configuration");
 };
 static_assert(Cfg<false>::SMEM <= 232448 && Cfg<true>::SMEM <= 232448, "shared memory budget");
 static_assert(Cfg<false, true>::SMEM <= 232448 && Cfg<true, true>::SMEM <= 232448, "shared memory budget");
+static_assert(Cfg<true, false, true>::SMEM <= 232448, "shared memory budget");
 static_assert(Cfg<true, true>::B_STAGE % 1024 == 0 && Cfg<false, true>::A_STAGE % 1024 == 0, "stage alignment");
 
 // Sites reported through the watchdog word (1-based).
@@ -404,12 +411,12 @@ __device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int
 
 // ---- the kernel -------------------------------------------------------------------
 
-template <bool kPair, bool kTf32, bool kBf16Out, bool kBias, int kAct>
+template <bool kPair, bool kTf32, bool kWide, bool kBf16Out, bool kBias, int kAct>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
                         void* __restrict__ c, int M, int N, int K, EpilogueParams ep, int fast) {
-  using C = Cfg<kPair, kTf32>;
+  using C = Cfg<kPair, kTf32, kWide>;
   constexpr int BK = C::BK;
   constexpr int UMMA_K = C::UMMA_K;
   extern __shared__ uint8_t smem_raw[];
@@ -497,10 +504,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d<kPair>(smem_u32(sAlo(stage)), &tmap_alo, fb, kb * BK, row0);
             tma_load_2d<kPair>(smem_u32(sBlo(stage)), &tmap_blo, fb, kb * BK, col0);
           } else {
+            // per MMA half h: this CTA's B_HALF_COLS columns of that half
 #pragma unroll
-            for (int j = 0; j < C::B_COLS / C::BOX_COLS; ++j)
-              tma_load_2d<kPair>(smem_u32(sB(stage) + j * C::B_BOX_BYTES), &tmap_b, fb, col0 + C::BOX_COLS * j,
-                                 kb * BK);
+            for (int h = 0; h < C::NH; ++h) {
+              const int hc = nb * C::BN + h * C::MMA_N + static_cast<int>(rank) * C::B_HALF_COLS;
+#pragma unroll
+              for (int j = 0; j < C::B_HALF_COLS / C::BOX_COLS; ++j)
+                tma_load_2d<kPair>(smem_u32(sB(stage) + (h * (C::B_HALF_COLS / C::BOX_COLS) + j) * C::B_BOX_BYTES),
+                                   &tmap_b, fb, hc + C::BOX_COLS * j, kb * BK);
+            }
           }
           issued_mask |= 1u << stage;
           parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
@@ -531,8 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int unit_kb = kTf32 ? C::PROMOTE : kblocks;
       for (int t = unit; t < num_tiles && ok; t += units) {
         for (int kb0 = 0; kb0 < kblocks && ok; kb0 += unit_kb, ++lc) {
-          const int acc = lc & 1;
-          const uint32_t aphase = static_cast<uint32_t>(lc >> 1) & 1u;
+          const int acc = lc % C::NACC;
+          const uint32_t aphase = static_cast<uint32_t>(lc / C::NACC) & 1u;
           if (!wait_bounded(tempty_bar(acc), aphase ^ 1u, abort_flag, kSiteMmaEmpty, true)) {
             ok = false;
             break;
@@ -564,9 +576,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 umma<kPair, true>(d_tmem, adesc, bdesc, 1u);
               } else {
                 // B: N-major SW128, +UMMA_K rows x 128 B per step; LBO = one
-                // BOX_COLS-wide N box, SBO = 8 k-rows x 128 B.
-                const uint64_t bdesc = smem_desc(b_base + k * (UMMA_K * 128), C::B_BOX_BYTES, 1024);
-                umma<kPair, false>(d_tmem, adesc, bdesc, accum);
+                // BOX_COLS-wide N box, SBO = 8 k-rows x 128 B.  One MMA per
+                // 256-column half of the tile, into its own TMEM columns.
+#pragma unroll
+                for (int h = 0; h < C::NH; ++h) {
+                  const uint32_t hb = b_base + h * (C::B_HALF_COLS / C::BOX_COLS) * C::B_BOX_BYTES;
+                  const uint64_t bdesc = smem_desc(hb + k * (UMMA_K * 128), C::B_BOX_BYTES, 1024);
+                  umma<kPair, false>(d_tmem + h * C::MMA_N, adesc, bdesc, accum);
+                }
               }
             }
             umma_commit_all<kPair>(empty_bar(stage));
@@ -594,7 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_unit = [&](int lc) {
       int ok = 1;
       if (lane == 0)
-        ok = wait_bounded(tfull_bar(lc & 1), static_cast<uint32_t>(lc >> 1) & 1u, abort_flag, kSiteEpilogue, true)
+        ok = wait_bounded(tfull_bar(lc % C::NACC), static_cast<uint32_t>(lc / C::NACC) & 1u, abort_flag,
+                          kSiteEpilogue, true)
                  ? 1
                  : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -605,8 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if constexpr (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * (lc & 1));
-        else mbar_arrive(tempty_bar(lc & 1));
+        if constexpr (kPair) mbar_arrive_cluster(tempty_leader0 + 8u * (lc % C::NACC));
+        else mbar_arrive(tempty_bar(lc % C::NACC));
       }
     };
     int lc = 0;
@@ -617,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
       if constexpr (!kTf32) {
         if (!wait_unit(lc)) break;
-        const uint32_t tacc = trow + static_cast<uint32_t>((lc & 1) * C::BN);
+        const uint32_t tacc = trow + static_cast<uint32_t>((lc % C::NACC) * C::BN);
 #pragma unroll 1
         for (int chunk = half; chunk < C::BN / 32; chunk += 2) {
           uint32_t r[32];
@@ -640,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const uint32_t tacc = trow + static_cast<uint32_t>((lc & 1) * C::BN);
+          const uint32_t tacc = trow + static_cast<uint32_t>((lc % C::NACC) * C::BN);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint32_t r[32];
@@ -703,25 +721,26 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, void*, int,
                           int, int, EpilogueParams, int);
 
-template <bool kPair, bool kTf32, bool kBf16, bool kBias>
+template <bool kPair, bool kTf32, bool kWide, bool kBf16, bool kBias>
 KernelFn pick_act(int act) {
   switch (act) {
-    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_RELU>;
-    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_GELU_ERF>;
-    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_GELU_TANH>;
-    default: return gemm_tcgen05_kernel<kPair, kTf32, kBf16, kBias, MCKE_ACT_NONE>;
+    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_RELU>;
+    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_ERF>;
+    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_TANH>;
+    default: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_NONE>;
   }
 }
 
 // bf16 operands: every output type; fp32 operands (3xTF32): fp32 output.
-template <bool kPair, bool kTf32>
+template <bool kPair, bool kTf32, bool kWide = false>
 KernelFn pick(bool bf16, bool bias, int act) {
   if constexpr (kTf32) {
     (void)bf16;
-    return bias ? pick_act<kPair, true, false, true>(act) : pick_act<kPair, true, false, false>(act);
+    return bias ? pick_act<kPair, true, false, false, true>(act) : pick_act<kPair, true, false, false, false>(act);
   } else {
-    if (bf16) return bias ? pick_act<kPair, false, true, true>(act) : pick_act<kPair, false, true, false>(act);
-    return bias ? pick_act<kPair, false, false, true>(act) : pick_act<kPair, false, false, false>(act);
+    if (bf16)
+      return bias ? pick_act<kPair, false, kWide, true, true>(act) : pick_act<kPair, false, kWide, true, false>(act);
+    return bias ? pick_act<kPair, false, kWide, false, true>(act) : pick_act<kPair, false, kWide, false, false>(act);
   }
 }
 
@@ -787,17 +806,56 @@ bool tcgen05_shape_ok(const void* a, const void* b, const void* c, int64_t m, in
 
 namespace {
 
+// Whether the 256 x 512 pair tile beats the 256 x 256 one.  Both run in
+// waves of one tile per CTA pair.  Per k the wide tile does twice the work at
+// kWideMain of the time (a third fewer L2 bytes per flop), but its single
+// accumulator leaves the epilogue un-overlapped, worth about kWideEpiK k of
+// main loop.  Fitted on B200 at 8192 x {1024, 2048, 8192, 16384} x 8192 and
+// 8192 x 16384 x 4096 (wide 9% faster at K = 8192, 3% slower at K = 4096).
+constexpr double kWideMain = 0.80;
+constexpr double kWideEpiK = 934.0;
+bool wide_pays(int64_t m, int64_t n, int64_t k) {
+  const int64_t units = sm_count() / 2;
+  const int64_t rows = (m + 255) / 256;
+  const int64_t narrow = rows * ((n + 255) / 256), wide = rows * ((n + 511) / 512);
+  const double t_narrow = static_cast<double>((narrow + units - 1) / units);
+  const double per_wide = 2.0 * (kWideMain + kWideEpiK / static_cast<double>(k > 0 ? k : 1));
+  const double t_wide = per_wide * static_cast<double>((wide + units - 1) / units);
+  return t_wide < t_narrow;
+}
+
 // Common launcher of both operand types: bf16 (a, b) or 3xTF32 (a, b = the hi
 // parts, alo, blo = the lo parts).
 template <bool kTf32>
 int launch_tc(const void* a, const void* b, const void* alo, const void* blo, void* c, int64_t m, int64_t n,
-              int64_t k, const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out) {
+              int64_t k, const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out,
+              int tile = 0) {
   // A pair tile is 256 rows; below that the single-CTA shape wastes less.
   const bool pair = m > Cfg<false, kTf32>::BM;
   const bool has_bias = ep.bias != nullptr;
-  KernelFn kfn = pair ? pick<true, kTf32>(ep.out_bf16 != 0, has_bias, ep.act)
-                      : pick<false, kTf32>(ep.out_bf16 != 0, has_bias, ep.act);
-  const std::size_t smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
+  // bf16 pairs: 256 x 256 tiles (two TMEM accumulators, epilogue overlapped
+  // with the next tile) or 256 x 512 (one accumulator, a third fewer bytes
+  // from L2 per flop).  tile: 0 = choose, 1 = 256 x 256, 2 = 256 x 512.
+  bool wide = false;
+  if constexpr (!kTf32) {
+    if (pair && n >= 512) wide = tile == 2 || (tile == 0 && wide_pays(m, n, k));
+  }
+  KernelFn kfn;
+  std::size_t smem;
+  if constexpr (!kTf32) {
+    if (wide) {
+      kfn = pick<true, false, true>(ep.out_bf16 != 0, has_bias, ep.act);
+      smem = Cfg<true, false, true>::SMEM;
+    } else {
+      kfn = pair ? pick<true, kTf32>(ep.out_bf16 != 0, has_bias, ep.act)
+                 : pick<false, kTf32>(ep.out_bf16 != 0, has_bias, ep.act);
+      smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
+    }
+  } else {
+    kfn = pair ? pick<true, kTf32>(ep.out_bf16 != 0, has_bias, ep.act)
+               : pick<false, kTf32>(ep.out_bf16 != 0, has_bias, ep.act);
+    smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
+  }
   if (kernel_out) *kernel_out = reinterpret_cast<const void*>(kfn);
   if (smem_out) *smem_out = smem;
   if (m == 0 || n == 0) return MCKE_OK;
@@ -818,7 +876,8 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   }
   const int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
   const int tile_m = pair ? Cfg<true, kTf32>::TILE_M : Cfg<false, kTf32>::TILE_M;
-  const int64_t tiles = ((m + tile_m - 1) / tile_m) * ((n + 255) / 256);
+  const int tile_n = wide ? 512 : 256;
+  const int64_t tiles = ((m + tile_m - 1) / tile_m) * ((n + tile_n - 1) / tile_n);
   if (tiles > 2147483647LL) return fail(MCKE_INVALID_ARGUMENT, "gemm (tcgen05): too many tiles");
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
   if (!pair) {
@@ -908,8 +967,8 @@ std::size_t split_bytes(int64_t elems) {
 
 int launch_gemm_tcgen05(const uint16_t* a, const uint16_t* b, void* c, int64_t m, int64_t n,
                         int64_t k, const EpilogueParams& ep, cudaStream_t s,
-                        const void** kernel_out, std::size_t* smem_out) {
-  return launch_tc<false>(a, b, nullptr, nullptr, c, m, n, k, ep, s, kernel_out, smem_out);
+                        const void** kernel_out, std::size_t* smem_out, int tile) {
+  return launch_tc<false>(a, b, nullptr, nullptr, c, m, n, k, ep, s, kernel_out, smem_out, tile);
 }
 
 std::size_t gemm_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k) {

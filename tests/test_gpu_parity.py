@@ -430,6 +430,29 @@ def test_gemm_bf16_tcgen05_matches_oracle(m, n, k):
         assert r["mismatches"] == 0, r
 
 
+@pytest.mark.parametrize("m,n,k", [(256, 512, 128), (1000, 712, 520), (300, 1544, 264), (2048, 2048, 1024)])
+def test_gemm_bf16_wide_tile_matches_narrow_and_oracle(m, n, k):
+    # the 256 x 512 pair tile (forced): same k order per output as the
+    # 256 x 256 tile, so the results agree bit for bit
+    a = oracle.fill_random(m * k, 4).reshape(m, k)
+    b = oracle.fill_random(k * n, 5).reshape(k, n)
+    ta, tb = _bf16(a), _bf16(b)
+    wide = host(mcke.gemm(ta, tb, variant="tcgen05_wide"))
+    narrow = host(mcke.gemm(ta, tb, variant="tcgen05_narrow"))
+    mcke.check_device_errors()
+    assert np.array_equal(wide.view(np.uint32), narrow.view(np.uint32))
+    r = oracle.spot_check_gemm(oracle.round_bf16(a), oracle.round_bf16(b), wide, samples=1024, seed=2,
+                               rel_tol=4 * oracle.tol_gemm(k), abs_tol=4 * oracle.abs_tol_gemm(k))
+    assert r["mismatches"] == 0, r
+    # fused epilogue and bf16 output on the wide tile
+    bias = torch.from_numpy(oracle.fill_random(n, 6)).to(DEV)
+    w2 = host(mcke.gemm(ta, tb, bias=bias, act="gelu_tanh", out_dtype=torch.bfloat16,
+                        variant="tcgen05_wide").view(torch.int16))
+    n2 = host(mcke.gemm(ta, tb, bias=bias, act="gelu_tanh", out_dtype=torch.bfloat16,
+                        variant="tcgen05_narrow").view(torch.int16))
+    assert np.array_equal(w2, n2)
+
+
 def test_gemm_bf16_fused_epilogue():
     m, n, k = 256, 512, 192
     a = oracle.fill_normal(m * k, 4).reshape(m, k)

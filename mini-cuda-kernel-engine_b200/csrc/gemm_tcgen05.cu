@@ -94,7 +94,11 @@ struct Cfg {
   static constexpr int TX = kPair ? 2 * STAGE : STAGE;  // bytes landing on the leader's full barrier
   static constexpr int EPI_ARRIVALS = kPair ? 2 * kEpiWarps : kEpiWarps;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
-  static constexpr std::size_t SMEM = static_cast<std::size_t>(STAGES) * STAGE + 1024 + 256;
+  // bf16 operands: one 32-row x 128-byte output box per epilogue warp, staged
+  // for a TMA store (SWIZZLE_128B, 1024-byte aligned after the stages).
+  static constexpr int EPI_BOX_BYTES = 32 * 128;
+  static constexpr int EPI_STAGE = kTf32 ? 0 : kEpiWarps * EPI_BOX_BYTES;
+  static constexpr std::size_t SMEM = static_cast<std::size_t>(STAGES) * STAGE + EPI_STAGE + 1024 + 256;
   // Instruction descriptor, .kind::f16 / .kind::tf32: D f32 (bits 4-5 = 1),
   // A and B bf16 (1) or tf32 (2) at bits 7-9 and 10-12, A K-major (bit 15 = 0),
   // B N-major (bit 16 = 1; bf16) or K-major (0; tf32), N >> 3 at bits 17-22,
@@ -201,6 +205,29 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
         : "memory");
   }
+}
+
+// TMA store of one box from this CTA's shared memory, tracked by this
+// thread's bulk async-group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// This thread's bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy writes to shared memory become visible to the async proxy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -400,6 +427,34 @@ __device__ __forceinline__ void epi_vals(const EpilogueParams& ep, void* c, int 
   }
 }
 
+// alpha, bias and activation on 32 values of columns gn0.. (beta == 0; the
+// columns past N, clipped by the store, use no bias).  The same arithmetic,
+// in the same order, as epi_vals.
+template <bool kBias, int kAct>
+__device__ __forceinline__ void epi_math(const EpilogueParams& ep, int N, int gn0, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = ep.alpha * v[j];
+  if constexpr (kBias) {
+    if (gn0 + 32 <= N) {
+      const float4* pb = reinterpret_cast<const float4*>(ep.bias + gn0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 b = __ldg(pb + q);
+        v[4 * q] += b.x;
+        v[4 * q + 1] += b.y;
+        v[4 * q + 2] += b.z;
+        v[4 * q + 3] += b.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gn0 + j < N) v[j] += __ldg(ep.bias + gn0 + j);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = epi_act<kAct>(v[j]);
+}
+
 template <bool kBf16Out, bool kBias, int kAct>
 __device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int N, int64_t gm, int gn0,
                                           const uint32_t (&r)[32], bool fast) {
@@ -415,7 +470,8 @@ template <bool kPair, bool kTf32, bool kWide, bool kBf16Out, bool kBias, int kAc
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
-                        void* __restrict__ c, int M, int N, int K, EpilogueParams ep, int fast) {
+                        const __grid_constant__ CUtensorMap tmap_c, void* __restrict__ c, int M, int N, int K,
+                        EpilogueParams ep, int fast) {
   using C = Cfg<kPair, kTf32, kWide>;
   constexpr int BK = C::BK;
   constexpr int UMMA_K = C::UMMA_K;
@@ -427,7 +483,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto sB = [&](int st) { return smem + st * C::STAGE + C::A_STAGE; };
   auto sAlo = [&](int st) { return smem + st * C::STAGE + C::A_STAGE + C::B_STAGE; };
   auto sBlo = [&](int st) { return smem + st * C::STAGE + 2 * C::A_STAGE + C::B_STAGE; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  uint8_t* epi_stage = smem + C::STAGES * C::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + C::EPI_STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::NUM_BARS);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -461,6 +518,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kTf32) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_alo)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_blo)) : "memory");
+    } else {
+      if (fast & 2) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_c)) : "memory");
     }
   }
   if (warp == 1) tmem_alloc<kPair>(smem_u32(tmem_slot));
@@ -636,11 +695,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (!kTf32) {
         if (!wait_unit(lc)) break;
         const uint32_t tacc = trow + static_cast<uint32_t>((lc % C::NACC) * C::BN);
+        if (fast & 2) {
+          // Through shared memory: this thread writes its row of a 32 x 128-byte
+          // box (16-byte granule g at g ^ (row & 7): SWIZZLE_128B, and no bank
+          // conflicts), then lane 0 stores the box with TMA, clipped at M and N.
+          constexpr int UCOLS = kBf16Out ? 64 : 32;  // output columns per box
+          const uint32_t box = smem_u32(epi_stage) + static_cast<uint32_t>((warp - 2) * C::EPI_BOX_BYTES);
+          const uint32_t my_row = box + static_cast<uint32_t>(lane) * 128u;
+          const uint32_t sw = static_cast<uint32_t>(lane & 7);
+          const int row0 = static_cast<int>(gm) - lane;
 #pragma unroll 1
-        for (int chunk = half; chunk < C::BN / 32; chunk += 2) {
-          uint32_t r[32];
-          tmem_ld32(tacc + static_cast<uint32_t>(chunk * 32), r);
-          if (gm < M) epi_chunk<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + chunk * 32, r, fast != 0);
+          for (int u = half; u < C::BN / UCOLS; u += 2) {
+            const int gn0 = nb * C::BN + u * UCOLS;
+            if (lane == 0) bulk_wait_read_all();  // the previous box has left the buffer
+            __syncwarp();
+#pragma unroll
+            for (int sub = 0; sub < UCOLS / 32; ++sub) {
+              uint32_t r[32];
+              tmem_ld32(tacc + static_cast<uint32_t>(u * UCOLS + sub * 32), r);
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              epi_math<kBias, kAct>(ep, N, gn0 + sub * 32, v);
+              if constexpr (kBf16Out) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t g = static_cast<uint32_t>(4 * sub + q);
+                  st_shared_v4(my_row + ((g ^ sw) << 4), pack_bf16x2(v[8 * q], v[8 * q + 1]),
+                               pack_bf16x2(v[8 * q + 2], v[8 * q + 3]), pack_bf16x2(v[8 * q + 4], v[8 * q + 5]),
+                               pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+                }
+              } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  st_shared_v4(my_row + ((static_cast<uint32_t>(q) ^ sw) << 4), __float_as_uint(v[4 * q]),
+                               __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                               __float_as_uint(v[4 * q + 3]));
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row0 < M && gn0 < N) {
+              tma_store_2d(&tmap_c, box, gn0, row0);
+              bulk_commit();
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int chunk = half; chunk < C::BN / 32; chunk += 2) {
+            uint32_t r[32];
+            tmem_ld32(tacc + static_cast<uint32_t>(chunk * 32), r);
+            if (gm < M) epi_chunk<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + chunk * 32, r, fast != 0);
+          }
         }
         release_unit(lc);
         ++lc;
@@ -675,6 +781,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             epi_vals<kBf16Out, kBias, kAct>(ep, c, N, gm, nb * C::BN + (half + 2 * q) * 32, sum[q], fast != 0);
         }
       }
+    }
+    // the staged boxes have been written before the CTA's shared memory goes
+    if constexpr (!kTf32) {
+      if ((fast & 2) && lane == 0) bulk_wait_all();
     }
   }
 
@@ -718,8 +828,8 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
   return MCKE_OK;
 }
 
-using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, void*, int,
-                          int, int, EpilogueParams, int);
+using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                          const CUtensorMap, void*, int, int, int, EpilogueParams, int);
 
 template <bool kPair, bool kTf32, bool kWide, bool kBf16, bool kBias>
 KernelFn pick_act(int act) {
@@ -809,11 +919,12 @@ namespace {
 // Whether the 256 x 512 pair tile beats the 256 x 256 one.  Both run in
 // waves of one tile per CTA pair.  Per k the wide tile does twice the work at
 // kWideMain of the time (a third fewer L2 bytes per flop), but its single
-// accumulator leaves the epilogue un-overlapped, worth about kWideEpiK k of
-// main loop.  Fitted on B200 at 8192 x {1024, 2048, 8192, 16384} x 8192 and
-// 8192 x 16384 x 4096 (wide 9% faster at K = 8192, 3% slower at K = 4096).
-constexpr double kWideMain = 0.80;
-constexpr double kWideEpiK = 934.0;
+// accumulator leaves the epilogue (TMA stores) un-overlapped, worth about
+// kWideEpiK k of main loop.  Fitted on B200 at 8192 x 8192 x {2048, 8192},
+// 8192 x 16384 x 4096, 8192 x 4096 x 16384 and 8192 x 2048 x 8192 (wide 13%
+// faster at K = 8192, 9% at K = 4096, even at K = 2048).
+constexpr double kWideMain = 0.82;
+constexpr double kWideEpiK = 350.0;
 bool wide_pays(int64_t m, int64_t n, int64_t k) {
   const int64_t units = sm_count() / 2;
   const int64_t rows = (m + 255) / 256;
@@ -874,7 +985,18 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
     talo = ta;
     tblo = tb;
   }
-  const int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
+  int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
+  // bf16 operands: the output leaves through shared memory and TMA stores of
+  // 32 x 128-byte boxes (bit 1) when C is written, not read (beta == 0).
+  CUtensorMap tc = ta;
+  if constexpr (!kTf32) {
+    if (fast && ep.beta == 0.0f) {
+      const bool bf16_out = ep.out_bf16 != 0;
+      MCKE_RETURN_IF(make_map(&tc, c, static_cast<uint64_t>(m), static_cast<uint64_t>(n), bf16_out ? 64u : 32u, 32u,
+                              !bf16_out));
+      fast |= 2;
+    }
+  }
   const int tile_m = pair ? Cfg<true, kTf32>::TILE_M : Cfg<false, kTf32>::TILE_M;
   const int tile_n = wide ? 512 : 256;
   const int64_t tiles = ((m + tile_m - 1) / tile_m) * ((n + tile_n - 1) / tile_n);
@@ -883,7 +1005,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   if (!pair) {
     int grid = sm_count();
     if (tiles < grid) grid = static_cast<int>(tiles);
-    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, c, mi, ni, ki, ep, fast);
+    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast);
     return MCKE_OK;
   }
   int pairs = max_pairs(kfn);
@@ -900,7 +1022,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, c, mi, ni, ki, ep, fast);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast);
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
   return MCKE_OK;
 }

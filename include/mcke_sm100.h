@@ -61,14 +61,21 @@ typedef enum { MCKE_SOFTMAX_THREE_PASS = 0, MCKE_SOFTMAX_ONLINE = 1 } mcke_softm
  * meets the TMA rules (K % 8 == 0, N % 8 == 0, 16-byte aligned A and B),
  * else SIMT; for f32 it picks SIMT. */
 /* TCGEN05_WIDE / TCGEN05_NARROW: the tcgen05 kernel with its pair tile forced
- * to 256 x 512 / 256 x 256 (AUTO and TCGEN05 choose; shapes that cannot use the
- * pair tile ignore the choice). */
+ * to 256 x 512 / 256 x 256, one tile per CTA pair at a time (AUTO and TCGEN05
+ * choose; shapes that cannot use the pair tile ignore the choice).  The two
+ * give bit-identical results.  TCGEN05_SPLIT: the 256 x 512 tile with the
+ * split-k schedule wherever it applies (fp32 output, beta == 0, M % 256 == 0,
+ * N % 512 == 0): the k-blocks of the tiles past the last whole wave are divided
+ * evenly over all CTA pairs and cut tiles are summed in C in k order
+ * (deterministic; within the bf16 tolerance of the unsplit result).  AUTO and
+ * TCGEN05 use it when whole waves would leave more than 5% of the pairs idle. */
 typedef enum {
   MCKE_GEMM_AUTO = 0,
   MCKE_GEMM_SIMT = 1,
   MCKE_GEMM_TCGEN05 = 2,
   MCKE_GEMM_TCGEN05_WIDE = 3,
-  MCKE_GEMM_TCGEN05_NARROW = 4
+  MCKE_GEMM_TCGEN05_NARROW = 4,
+  MCKE_GEMM_TCGEN05_SPLIT = 5
 } mcke_gemm_variant;
 /* Element type of a GEMM output. */
 typedef enum { MCKE_DTYPE_F32 = 0, MCKE_DTYPE_BF16 = 2 } mcke_dtype;

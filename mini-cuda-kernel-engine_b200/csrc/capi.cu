@@ -67,9 +67,14 @@ int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m
     return fail(MCKE_INVALID_ARGUMENT, "%s: beta must be 0 for a bf16 output", who);
   if (act < MCKE_ACT_NONE || act > MCKE_ACT_GELU_TANH)
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
-  if (variant < MCKE_GEMM_AUTO || variant > MCKE_GEMM_TCGEN05_NARROW)
+  if (variant < MCKE_GEMM_AUTO || variant > MCKE_GEMM_TCGEN05_SPLIT)
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
-  const int tile = variant == MCKE_GEMM_TCGEN05_WIDE ? 2 : variant == MCKE_GEMM_TCGEN05_NARROW ? 1 : 0;
+  // launch_gemm_tcgen05's tile word: bits 0-1 the pair tile (1 = 256 x 256,
+  // 2 = 256 x 512), bits 2-3 the split-k schedule (1 = never, 2 = where it applies)
+  const int tile = variant == MCKE_GEMM_TCGEN05_WIDE     ? (2 | 4)
+                   : variant == MCKE_GEMM_TCGEN05_NARROW ? (1 | 4)
+                   : variant == MCKE_GEMM_TCGEN05_SPLIT  ? (2 | 8)
+                                                         : 0;
   if (tile != 0) variant = MCKE_GEMM_TCGEN05;
   if (!bf16_in && variant == MCKE_GEMM_TCGEN05)
     return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands; no fallback is applied", who);

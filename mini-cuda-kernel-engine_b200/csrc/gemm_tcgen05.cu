@@ -53,6 +53,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "gemm_epilogue.cuh"
@@ -93,7 +94,7 @@ struct Cfg {
   static constexpr int PROMOTE = kTf32 ? 4 : 0;
   static constexpr int TX = kPair ? 2 * STAGE : STAGE;  // bytes landing on the leader's full barrier
   static constexpr int EPI_ARRIVALS = kPair ? 2 * kEpiWarps : kEpiWarps;
-  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int NUM_BARS = 2 * STAGES + 6;
   // bf16 operands: one 32-row x 128-byte output box per epilogue warp, staged
   // for a TMA store (SWIZZLE_128B, 1024-byte aligned after the stages).
   static constexpr int EPI_BOX_BYTES = 32 * 128;
@@ -116,9 +117,94 @@ static_assert(Cfg<true, false, true>::SMEM <= 232448, "shared memory budget");
 static_assert(Cfg<true, true>::B_STAGE % 1024 == 0 && Cfg<false, true>::A_STAGE % 1024 == 0, "stage alignment");
 
 // Sites reported through the watchdog word (1-based).
-enum : uint32_t { kSiteProducer = 1, kSiteMmaFull = 2, kSiteMmaEmpty = 3, kSiteEpilogue = 4, kSiteDrain = 5 };
+enum : uint32_t {
+  kSiteProducer = 1,
+  kSiteMmaFull = 2,
+  kSiteMmaEmpty = 3,
+  kSiteEpilogue = 4,
+  kSiteDrain = 5,
+  kSiteSplitFlag = 6
+};
 
 __device__ uint32_t g_tc_watchdog;
+
+// ---- split-k schedule (stream-K) ---------------------------------------------
+//
+// Whole waves of tiles run one tile per CTA pair; the k-blocks of the tiles
+// left over are then divided evenly over all pairs, each pair taking one
+// contiguous range of (tile, k-block) in tile-major order.  A tile whose range
+// is cut between pairs is summed through its own region of C: contributor j
+// (in k order) waits until j contributors have written, adds the sum found
+// there to its own partial and writes it back (flag j + 1); the last one adds,
+// applies the epilogue and stores.  The sum order is fixed by k, so results do
+// not depend on timing.  A pair walks its segments from its last tile down:
+// the head of a cut tile is the first thing its owner computes and the tail
+// the last thing the next pair computes, so waits are short.
+//
+// Flags: one 32-bit word per (launch slot, tile, CTA rank), (tag << 8) | j
+// while in use, reset to 0 by the last contributor; the host gives every
+// launch the next slot of the ring and a fresh tag.
+constexpr int kSplitSlots = 32;
+constexpr int kSplitMaxTiles = 1024;
+__device__ uint32_t g_split_flags[kSplitSlots * kSplitMaxTiles * 2];
+
+struct SplitK {
+  int tiles_dp;   // tiles [0, tiles_dp) one per pair; the rest split
+  int w;          // k-blocks per pair over the split tiles; 0 = no split
+  int slot;       // flag slot of this launch
+  uint32_t tag;   // 24-bit launch tag, non-zero
+};
+
+struct Seg {
+  int tile, kb0, kb1;  // k-blocks [kb0, kb1) of tile
+};
+
+// The segments of one pair, in the order every role walks them.
+struct SegIter {
+  int t, units, dp_end, kblocks;
+  int64_t g_beg, g;
+  __device__ __forceinline__ SegIter(int unit, int units_, int num_tiles, int kblocks_, const SplitK& sk)
+      : t(unit), units(units_), kblocks(kblocks_) {
+    dp_end = sk.w > 0 ? sk.tiles_dp : num_tiles;
+    if (sk.w > 0) {
+      const int64_t total = static_cast<int64_t>(num_tiles - dp_end) * kblocks;
+      g_beg = min(static_cast<int64_t>(unit) * sk.w, total);
+      g = min(g_beg + sk.w, total);
+    } else {
+      g_beg = g = 0;
+    }
+  }
+  __device__ __forceinline__ bool next(Seg& sg) {
+    if (t < dp_end) {
+      sg.tile = t;
+      sg.kb0 = 0;
+      sg.kb1 = kblocks;
+      t += units;
+      return true;
+    }
+    if (g > g_beg) {
+      const int64_t tl = (g - 1) / kblocks;
+      const int64_t ts = tl * kblocks;
+      const int64_t s0 = max(ts, g_beg);
+      sg.tile = dp_end + static_cast<int>(tl);
+      sg.kb0 = static_cast<int>(s0 - ts);
+      sg.kb1 = static_cast<int>(g - ts);
+      g = s0;
+      return true;
+    }
+    return false;
+  }
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -184,6 +270,21 @@ __device__ __noinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatil
         atomicCAS(&g_tc_watchdog, 0u, site);
         return false;
       }
+    }
+  }
+}
+
+// Bounded wait for a split-tile flag; a timeout is recorded (site 6) and the
+// caller carries on, so no CTA is left waiting.
+__device__ __noinline__ void split_wait(const uint32_t* flag, uint32_t want) {
+  if (ld_acquire_u32(flag) == want) return;
+  const unsigned long long t0 = gtimer();
+  for (;;) {
+    __nanosleep(64);
+    if (ld_acquire_u32(flag) == want) return;
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(&g_tc_watchdog, 0u, kSiteSplitFlag);
+      return;
     }
   }
 }
@@ -471,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
                         const __grid_constant__ CUtensorMap tmap_c, void* __restrict__ c, int M, int N, int K,
-                        EpilogueParams ep, int fast) {
+                        EpilogueParams ep, int fast, SplitK sk) {
   using C = Cfg<kPair, kTf32, kWide>;
   constexpr int BK = C::BK;
   constexpr int UMMA_K = C::UMMA_K;
@@ -494,6 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
   const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 4);
+  const uint32_t epi_bar = bar0 + 8u * (2 * C::STAGES + 5);  // the eight epilogue warps
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
@@ -511,6 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty_bar(a), C::EPI_ARRIVALS);
     }
     mbar_init(drain_bar, 1);
+    mbar_init(epi_bar, kEpiWarps);
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
@@ -543,12 +646,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, parity_mask = 0;  // for the drain on abort (leader)
       bool ok = true;
-      for (int t = unit; t < num_tiles && ok; t += units) {
+      SegIter it(unit, units, num_tiles, kblocks, sk);
+      Seg sg;
+      while (ok && it.next(sg)) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(sg.tile, num_m, num_n, mb, nb);
         const int row0 = mb * C::TILE_M + static_cast<int>(rank) * C::BM;
         const int col0 = nb * C::BN + static_cast<int>(rank) * C::B_COLS;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, kSiteProducer, true)) {
             ok = false;
             break;
@@ -600,8 +705,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int lc = 0;
       const int unit_kb = kTf32 ? C::PROMOTE : kblocks;
-      for (int t = unit; t < num_tiles && ok; t += units) {
-        for (int kb0 = 0; kb0 < kblocks && ok; kb0 += unit_kb, ++lc) {
+      SegIter it(unit, units, num_tiles, kblocks, sk);
+      Seg sg;
+      while (ok && it.next(sg)) {
+        for (int kb0 = sg.kb0; kb0 < sg.kb1 && ok; kb0 += unit_kb, ++lc) {
           const int acc = lc % C::NACC;
           const uint32_t aphase = static_cast<uint32_t>(lc / C::NACC) & 1u;
           if (!wait_bounded(tempty_bar(acc), aphase ^ 1u, abort_flag, kSiteMmaEmpty, true)) {
@@ -610,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
-          const int kb1 = min(kb0 + unit_kb, kblocks);
+          const int kb1 = min(kb0 + unit_kb, sg.kb1);
           for (int kb = kb0; kb < kb1; ++kb) {
             if (!wait_bounded(full_bar(stage), phase, abort_flag, kSiteMmaFull, true)) {
               ok = false;
@@ -686,16 +793,103 @@ __global__ void __launch_bounds__(kThreads, 1)
         else mbar_arrive(tempty_bar(lc % C::NACC));
       }
     };
+    // The eight epilogue warps meet on an mbarrier (one arrival per warp) with
+    // the kernel's bounded wait, so a warp that left early on an abort cannot
+    // hold the others.
+    uint32_t epi_uses = 0;
+    auto epi_sync = [&]() {
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(epi_bar);
+        wait_bounded(epi_bar, epi_uses & 1u, abort_flag, kSiteSplitFlag, false);
+      }
+      __syncwarp();
+      ++epi_uses;
+    };
     int lc = 0;
-    for (int t = unit; t < num_tiles; t += units) {
+    SegIter it(unit, units, num_tiles, kblocks, sk);
+    Seg sg;
+    while (it.next(sg)) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(sg.tile, num_m, num_n, mb, nb);
       const int64_t gm = static_cast<int64_t>(mb) * C::TILE_M + static_cast<int>(rank) * C::BM + quad * 32 + lane;
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
       if constexpr (!kTf32) {
         if (!wait_unit(lc)) break;
         const uint32_t tacc = trow + static_cast<uint32_t>((lc % C::NACC) * C::BN);
-        if (fast & 2) {
+        const bool whole = sg.kb0 == 0 && sg.kb1 == kblocks;
+        if (!whole) {
+          if constexpr (!kBf16Out) {
+            // A cut tile (fp32 output, beta = 0, M and N whole tiles: the
+            // host splits nothing else).  Contributor j of the tile in k order.
+            const int tl = sg.tile - sk.tiles_dp;
+            const uint32_t j =
+                static_cast<uint32_t>(unit - static_cast<int>(static_cast<int64_t>(tl) * kblocks / sk.w));
+            const bool last = sg.kb1 == kblocks;
+            uint32_t* flag = g_split_flags + (static_cast<size_t>(sk.slot) * kSplitMaxTiles + sg.tile) * 2 + rank;
+            if (j > 0) {
+              if (warp == 2 && lane == 0) split_wait(flag, (sk.tag << 8) | j);
+              epi_sync();
+              if (last && warp == 2 && lane == 0) st_release_u32(flag, 0u);  // every waiter has passed
+            }
+            // The running sum of value (row r0 + lane, column u*32 + jj) is kept
+            // at (row r0 + jj, column u*32 + lane) of the tile's own region of
+            // C: 128 contiguous bytes per warp access.
+            const int row0 = static_cast<int>(gm) - lane;
+            float* region = static_cast<float*>(c) + static_cast<int64_t>(row0) * N + nb * C::BN + lane;
+            const uint32_t box = smem_u32(epi_stage) + static_cast<uint32_t>((warp - 2) * C::EPI_BOX_BYTES);
+            const uint32_t my_row = box + static_cast<uint32_t>(lane) * 128u;
+            const uint32_t sw = static_cast<uint32_t>(lane & 7);
+            if (j > 0) {
+              // the running sums were written a while ago: bring every line
+              // this warp will read into L2 at once (lane l: line of row l)
+#pragma unroll
+              for (int u = half; u < C::BN / 32; u += 2)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(region - lane + static_cast<int64_t>(lane) * N + u * 32));
+            }
+#pragma unroll 1
+            for (int u = half; u < C::BN / 32; u += 2) {
+              uint32_t r[32];
+              tmem_ld32(tacc + static_cast<uint32_t>(u * 32), r);
+              float v[32];
+              float* blk = region + u * 32;
+              if (j > 0) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] = __ldcg(blk + static_cast<int64_t>(jj) * N) + __uint_as_float(r[jj]);
+              } else {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] = __uint_as_float(r[jj]);
+              }
+              if (!last) {
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) __stcg(blk + static_cast<int64_t>(jj) * N, v[jj]);
+              } else {
+                const int gn0 = nb * C::BN + u * 32;
+                if (lane == 0) bulk_wait_read_all();
+                __syncwarp();
+                epi_math<kBias, kAct>(ep, N, gn0, v);
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  st_shared_v4(my_row + ((static_cast<uint32_t>(q) ^ sw) << 4), __float_as_uint(v[4 * q]),
+                               __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                               __float_as_uint(v[4 * q + 3]));
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                  tma_store_2d(&tmap_c, box, gn0, row0);
+                  bulk_commit();
+                }
+              }
+            }
+            if (!last) {
+              epi_sync();  // all eight warps have written
+              if (warp == 2 && lane == 0) {
+                __threadfence();
+                st_release_u32(flag, (sk.tag << 8) | (j + 1u));
+              }
+            }
+          }
+        } else if (fast & 2) {
           // Through shared memory: this thread writes its row of a 32 x 128-byte
           // box (16-byte granule g at g ^ (row & 7): SWIZZLE_128B, and no bank
           // conflicts), then lane 0 stores the box with TMA, clipped at M and N.
@@ -709,7 +903,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int gn0 = nb * C::BN + u * UCOLS;
             if (lane == 0) bulk_wait_read_all();  // the previous box has left the buffer
             __syncwarp();
-#pragma unroll
+            // one 32-column TMEM load at a time (bf16: two per box), which keeps
+            // the erf GELU's registers within the launch's 168
+#pragma unroll 1
             for (int sub = 0; sub < UCOLS / 32; ++sub) {
               uint32_t r[32];
               tmem_ld32(tacc + static_cast<uint32_t>(u * UCOLS + sub * 32), r);
@@ -759,7 +955,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) sum[q][j] = 0.f;
         bool ok = true;
-        for (int kb0 = 0; kb0 < kblocks; kb0 += C::PROMOTE, ++lc) {
+        for (int kb0 = sg.kb0; kb0 < sg.kb1; kb0 += C::PROMOTE, ++lc) {
           if (!wait_unit(lc)) {
             ok = false;
             break;
@@ -829,7 +1025,7 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
 }
 
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
-                          const CUtensorMap, void*, int, int, int, EpilogueParams, int);
+                          const CUtensorMap, void*, int, int, int, EpilogueParams, int, SplitK);
 
 template <bool kPair, bool kTf32, bool kWide, bool kBf16, bool kBias>
 KernelFn pick_act(int act) {
@@ -925,14 +1121,60 @@ namespace {
 // faster at K = 8192, 9% at K = 4096, even at K = 2048).
 constexpr double kWideMain = 0.82;
 constexpr double kWideEpiK = 350.0;
-bool wide_pays(int64_t m, int64_t n, int64_t k) {
+// The split-k schedule (see SplitK) needs an fp32 output written through TMA
+// boxes with beta = 0 (cut tiles keep their running sums in C) and whole tiles
+// in M and N; it is chosen when whole waves would leave more than kSplitBelow
+// of the pairs idle.
+constexpr double kSplitBelow = 0.95;
+// ... and when at least kSplitMinWaves whole waves exist: measured on B200,
+// the split pays after data-parallel waves (8192 x 4096 x 8192: 5% faster)
+// but not in place of them (8192 x {1024, 2048} x 8192: 8-20% slower), where
+// pairs no longer walk k together and the cut tiles' sums leave L2.
+constexpr int64_t kSplitMinWaves = 2;
+bool split_shape_ok(int64_t m, int64_t n, int tile_n, int64_t tiles, bool tma_fp32_out) {
+  return tma_fp32_out && m % 256 == 0 && n % tile_n == 0 && tiles <= kSplitMaxTiles;
+}
+double busy_fraction(int64_t tiles, int64_t units) {
+  const int64_t waves = (tiles + units - 1) / units;
+  return static_cast<double>(tiles) / static_cast<double>(waves * units);
+}
+// Time of a tile count in tile-times: whole waves, or the exact share when the
+// split schedule will take the launch.
+double tile_waves(int64_t tiles, int64_t units, bool split) {
+  if (split && busy_fraction(tiles, units) < kSplitBelow && tiles >= kSplitMinWaves * units)
+    return static_cast<double>(tiles) / units;
+  return static_cast<double>((tiles + units - 1) / units);
+}
+bool wide_pays(int64_t m, int64_t n, int64_t k, bool can_split) {
   const int64_t units = sm_count() / 2;
   const int64_t rows = (m + 255) / 256;
   const int64_t narrow = rows * ((n + 255) / 256), wide = rows * ((n + 511) / 512);
-  const double t_narrow = static_cast<double>((narrow + units - 1) / units);
+  const double t_narrow = tile_waves(narrow, units, can_split && split_shape_ok(m, n, 256, narrow, true));
   const double per_wide = 2.0 * (kWideMain + kWideEpiK / static_cast<double>(k > 0 ? k : 1));
-  const double t_wide = per_wide * static_cast<double>((wide + units - 1) / units);
+  const double t_wide = per_wide * tile_waves(wide, units, can_split && split_shape_ok(m, n, 512, wide, true));
   return t_wide < t_narrow;
+}
+
+// The split-k schedule of a pair launch, or none (w = 0).  Whole waves but
+// the last run unsplit, so most tiles keep the data-parallel order.
+SplitK plan_split(int64_t tiles, int pairs, int64_t k, int tile_n, int64_t m, int64_t n, bool tma_fp32_out,
+                  bool force) {
+  SplitK sk = {0, 0, 0, 0u};
+  if (!split_shape_ok(m, n, tile_n, tiles, tma_fp32_out) || pairs < 2) return sk;
+  if (!force && (busy_fraction(tiles, pairs) >= kSplitBelow || tiles < kSplitMinWaves * pairs)) return sk;
+  const int64_t kblocks = (k + Cfg<true>::BK - 1) / Cfg<true>::BK;
+  const int64_t dp = tiles / pairs >= 2 ? (tiles / pairs - 1) * pairs : 0;
+  const int64_t total = (tiles - dp) * kblocks;
+  const int64_t w = (total + pairs - 1) / pairs;
+  // short ranges, or more contributors to a tile than the flag's 8 bits count
+  if (w < 4 || (kblocks + w - 1) / w + 1 >= 255) return sk;
+  static std::atomic<uint32_t> launches{0};
+  const uint32_t seq = launches.fetch_add(1u, std::memory_order_relaxed);
+  sk.tiles_dp = static_cast<int>(dp);
+  sk.w = static_cast<int>(w);
+  sk.slot = static_cast<int>(seq % kSplitSlots);
+  sk.tag = (seq / kSplitSlots) % 0xFFFFFFu + 1u;
+  return sk;
 }
 
 // Common launcher of both operand types: bf16 (a, b) or 3xTF32 (a, b = the hi
@@ -946,10 +1188,18 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   const bool has_bias = ep.bias != nullptr;
   // bf16 pairs: 256 x 256 tiles (two TMEM accumulators, epilogue overlapped
   // with the next tile) or 256 x 512 (one accumulator, a third fewer bytes
-  // from L2 per flop).  tile: 0 = choose, 1 = 256 x 256, 2 = 256 x 512.
+  // from L2 per flop).  tile bits 0-1: 0 = choose, 1 = 256 x 256, 2 = 256 x 512;
+  // bits 2-3, the split-k schedule: 0 = choose, 1 = never, 2 = wherever it applies.
+  const int tile_sel = tile & 3, split_sel = (tile >> 2) & 3;
+  // C 16-byte aligned rows and bias: vector epilogue (fast bit 0); with
+  // beta == 0 and bf16 operands, TMA-store epilogue (bit 1)
+  int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
+  if (!kTf32 && fast && ep.beta == 0.0f) fast |= 2;
+  const bool tma_fp32_out = (fast & 2) && !ep.out_bf16;
   bool wide = false;
   if constexpr (!kTf32) {
-    if (pair && n >= 512) wide = tile == 2 || (tile == 0 && wide_pays(m, n, k));
+    if (pair && n >= 512)
+      wide = tile_sel == 2 || (tile_sel == 0 && wide_pays(m, n, k, split_sel != 1 && tma_fp32_out));
   }
   KernelFn kfn;
   std::size_t smem;
@@ -985,31 +1235,31 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
     talo = ta;
     tblo = tb;
   }
-  int fast = aligned(c, 16) && n % 8 == 0 && (!has_bias || aligned(ep.bias, 16)) ? 1 : 0;
   // bf16 operands: the output leaves through shared memory and TMA stores of
-  // 32 x 128-byte boxes (bit 1) when C is written, not read (beta == 0).
+  // 32 x 128-byte boxes (fast bit 1) when C is written, not read (beta == 0).
   CUtensorMap tc = ta;
-  if constexpr (!kTf32) {
-    if (fast && ep.beta == 0.0f) {
-      const bool bf16_out = ep.out_bf16 != 0;
-      MCKE_RETURN_IF(make_map(&tc, c, static_cast<uint64_t>(m), static_cast<uint64_t>(n), bf16_out ? 64u : 32u, 32u,
-                              !bf16_out));
-      fast |= 2;
-    }
+  if (fast & 2) {
+    const bool bf16_out = ep.out_bf16 != 0;
+    MCKE_RETURN_IF(make_map(&tc, c, static_cast<uint64_t>(m), static_cast<uint64_t>(n), bf16_out ? 64u : 32u, 32u,
+                            !bf16_out));
   }
   const int tile_m = pair ? Cfg<true, kTf32>::TILE_M : Cfg<false, kTf32>::TILE_M;
   const int tile_n = wide ? 512 : 256;
   const int64_t tiles = ((m + tile_m - 1) / tile_m) * ((n + tile_n - 1) / tile_n);
   if (tiles > 2147483647LL) return fail(MCKE_INVALID_ARGUMENT, "gemm (tcgen05): too many tiles");
   const int mi = static_cast<int>(m), ni = static_cast<int>(n), ki = static_cast<int>(k);
+  SplitK sk = {0, 0, 0, 0u};
   if (!pair) {
     int grid = sm_count();
     if (tiles < grid) grid = static_cast<int>(tiles);
-    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast);
+    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast, sk);
     return MCKE_OK;
   }
   int pairs = max_pairs(kfn);
-  if (tiles < pairs) pairs = static_cast<int>(tiles);
+  if constexpr (!kTf32) {
+    if (split_sel != 1) sk = plan_split(tiles, pairs, k, tile_n, m, n, tma_fp32_out, split_sel == 2);
+  }
+  if (sk.w == 0 && tiles < pairs) pairs = static_cast<int>(tiles);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1022,7 +1272,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast, sk);
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
   return MCKE_OK;
 }

@@ -26,7 +26,7 @@ ACT = {"none": 0, "relu": 1, "gelu_erf": 2, "gelu_tanh": 3}
 REDUCE_KIND = {"sum": 0, "max": 1, "mean": 2}
 REDUCE_VARIANT = {"smem_tree": 0, "warp_shuffle": 1, "two_pass": 2}
 SOFTMAX_VARIANT = {"three_pass": 0, "online": 1}
-GEMM_VARIANT = {"auto": 0, "simt": 1, "tcgen05": 2, "tcgen05_wide": 3, "tcgen05_narrow": 4}
+GEMM_VARIANT = {"auto": 0, "simt": 1, "tcgen05": 2, "tcgen05_wide": 3, "tcgen05_narrow": 4, "tcgen05_split": 5}
 DTYPE = {"f32": 0, "bf16": 2}
 RESULT_BYTES = 16   # mcke_reduce_result
 PARTIAL_BYTES = 24  # mcke_reduce_partial

@@ -453,6 +453,63 @@ def test_gemm_bf16_wide_tile_matches_narrow_and_oracle(m, n, k):
     assert np.array_equal(w2, n2)
 
 
+@pytest.mark.parametrize("m,n,k", [(512, 1024, 4096), (2048, 1024, 8192), (8192, 1024, 2048), (8192, 4096, 1024),
+                                   (768, 1536, 2056)])
+def test_gemm_bf16_split_k_schedule(m, n, k):
+    # Tiles cut between CTA pairs, 2 to 17 contributors per tile (k order
+    # sums through C), after whole data-parallel waves for (8192, 4096, 1024).
+    # Deterministic, within tolerance of the unsplit kernel and the oracle.
+    a = oracle.fill_random(m * k, 7).reshape(m, k)
+    b = oracle.fill_random(k * n, 8).reshape(k, n)
+    ta, tb = _bf16(a), _bf16(b)
+    dp = host(mcke.gemm(ta, tb, variant="tcgen05_wide"))
+    s1 = host(mcke.gemm(ta, tb, variant="tcgen05_split"))
+    s2 = host(mcke.gemm(ta, tb, variant="tcgen05_split"))
+    mcke.check_device_errors()
+    assert np.array_equal(s1.view(np.uint32), s2.view(np.uint32))
+    tol, atol = 4 * oracle.tol_gemm(k), 4 * oracle.abs_tol_gemm(k)
+    r = oracle.spot_check_gemm(oracle.round_bf16(a), oracle.round_bf16(b), s1, samples=2048, seed=3,
+                               rel_tol=tol, abs_tol=atol)
+    assert r["mismatches"] == 0, r
+    assert np.all(np.abs(s1.astype(np.float64) - dp) <= 2 * (atol + tol * np.abs(dp)))
+    # every element was written by the split schedule (no stale partial sums)
+    assert np.isfinite(s1).all()
+    # fused bias + GELU on the last contributor
+    bias = torch.from_numpy(oracle.fill_random(n, 9)).to(DEV)
+    e_dp = host(mcke.gemm(ta, tb, bias=bias, act="gelu_tanh", variant="tcgen05_wide"))
+    e_sp = host(mcke.gemm(ta, tb, bias=bias, act="gelu_tanh", variant="tcgen05_split"))
+    mcke.check_device_errors()
+    assert np.all(np.abs(e_sp.astype(np.float64) - e_dp) <= 2 * (atol + tol * np.abs(e_dp)))
+
+
+def test_gemm_bf16_split_k_chosen_and_concurrent():
+    # 256 tiles of 256 x 512 for 74 CTA pairs: AUTO runs two data-parallel
+    # waves and splits the rest (it differs from the unsplit result in the
+    # last bits); two launches in flight on two streams use separate flag slots
+    m, n, k = 8192, 4096, 4096
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(12)
+    ta = (torch.rand(m, k, generator=gen, device=DEV) * 2 - 1).to(torch.bfloat16)
+    tb = (torch.rand(k, n, generator=gen, device=DEV) * 2 - 1).to(torch.bfloat16)
+    ref = mcke.gemm(ta, tb, variant="tcgen05_split")
+    auto = mcke.gemm(ta, tb, variant="tcgen05")
+    dp = mcke.gemm(ta, tb, variant="tcgen05_wide")
+    torch.cuda.synchronize()
+    assert torch.equal(auto, ref)
+    assert not torch.equal(auto, dp)
+    assert torch.allclose(ref, dp, rtol=4 * oracle.tol_gemm(k), atol=8 * oracle.abs_tol_gemm(k))
+    s1, s2 = torch.cuda.Stream(DEV), torch.cuda.Stream(DEV)
+    outs = []
+    for _ in range(3):
+        for st in (s1, s2):
+            with torch.cuda.stream(st):
+                outs.append(mcke.gemm(ta, tb, variant="tcgen05_split"))
+    torch.cuda.synchronize()
+    mcke.check_device_errors()
+    for o in outs:
+        assert torch.equal(o, ref)
+
+
 def test_gemm_bf16_fused_epilogue():
     m, n, k = 256, 512, 192
     a = oracle.fill_normal(m * k, 4).reshape(m, k)

@@ -172,6 +172,9 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def min(self, torch, v: float) -> float:
+        return -self.max(torch, -v)
+
     def close(self):
         if self.pg is not None:
             self.pg.destroy_process_group()
@@ -386,11 +389,49 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
     out = {}
     steps = max(3, min(args.steps, 50))
     warm = max(3, min(args.warmup, 5))
+    ffma_peak = None  # set by the peaks op
 
     from mcke import shard as mshard
 
     def shard(n):
         return mshard.bounds(n, g, r)
+
+    if "peaks" in want:
+        # The roofline denominators measured by the library's own probes on
+        # this GPU in this run (the reference's bench/stream_triad.cu and
+        # bench/fma_peak.cu), beside the driver's MEASURED_PEAKS.json figures
+        # that the fractions in this line use.  Arrays of 1 GiB each (far
+        # larger than L2), so no flush is needed.
+        n = 1 << 28
+        pa = torch.empty(n, device=dev)
+        pb = torch.full((n,), 1.5, device=dev)
+        pc = torch.full((n,), 0.25, device=dev)
+        ps = max(3, min(steps, 10))
+        ms_t, per_t = timed_steps(torch, dist, lambda: mcke.peak_triad(pa, pb, pc, 3.0), ps, warm, None)
+        ms_c, per_c = timed_steps(torch, dist, lambda: mcke.peak_copy(pa, pb), ps, warm, None)
+        del pa, pb, pc
+        nt = mcke.peak_fma_threads()
+        seed = (torch.arange(nt, device=dev, dtype=torch.float32) % 13)
+        fo = torch.empty(nt, device=dev)
+        iters = 40000
+        ms_f, per_f = timed_steps(torch, dist, lambda: mcke.peak_fma(seed, fo, iters), max(3, min(steps, 5)), warm,
+                                  None)
+        del seed, fo
+        sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        triad = 12 * n / (min(per_t) * 1e-3) / 1e9   # best step, as a peak is taken
+        copy = 8 * n / (min(per_c) * 1e-3) / 1e9
+        ffma = mcke.PEAK_FMA_FLOP_PER_THREAD_STEP * nt * iters / (min(per_f) * 1e-3) / 1e12
+        nominal_ffma = sm * 128 * 2 * 1.965
+        triad, copy, ffma = (dist.min(torch, v) for v in (triad, copy, ffma))
+        out["peaks"] = {
+            "triad_gbs": round(triad, 1), "copy_gbs": round(copy, 1), "ffma_tflops": round(ffma, 2),
+            "driver_hbm_copy_gbs": peaks["hbm_gbs"], "triad_over_driver_copy": round(triad / peaks["hbm_gbs"], 4),
+            "copy_over_driver_copy": round(copy / peaks["hbm_gbs"], 4),
+            "ffma_over_nominal": round(ffma / (nominal_ffma / 1000.0), 4),
+            "note": "mcke_sm100_peak_{triad,copy,fma}_f32: a = b + 3c and a = b over 2^28 floats (12 and 8 B per "
+                    "element), 8 FMA chains per thread x 40000 steps (16 flop per thread-step); best step, "
+                    "minimum over ranks; nominal FFMA = SMs x 128 lanes x 2 x 1.965 GHz"}
+        ffma_peak = ffma
 
     if "bias_gelu" in want:
         r0, r1 = shard(BIAS_ROWS)
@@ -649,6 +690,8 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "ffma_kernel_tflops": round(GEMM_FLOPS * fs / (ms_s * 1e-3) / 1e12, 2),
             "cublas_sgemm_tflops_per_gpu": round(cublas_sgemm, 2),
             "ffma_frac_of_cublas_sgemm": round(GEMM_FLOPS / g * fs / (ms_s * 1e-3) / 1e12 / cublas_sgemm, 4),
+            "ffma_frac_of_measured_ffma_peak": (round(GEMM_FLOPS / g * fs / (ms_s * 1e-3) / 1e12 / ffma_peak, 4)
+                                                if ffma_peak else None),
             "note": "tf32 MMA rate = 3 x fp32 flops, compared with nominal dense tf32 (1100 TFLOP/s) and with "
                     "cuBLAS's one-pass TF32 GEMM on the same shard (torch.matmul, allow_tf32); the FFMA kernel "
                     "compared with cuBLAS SGEMM (the reference's kCublasRef ceiling row)"}
@@ -716,7 +759,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mcke", "reference"], default="mcke")
-    ap.add_argument("--ops", default="bias_gelu,reduce,row_reduce,gemm_bf16,dag_fused,dag_unfused,dag_fanout,gemm_f32",
+    ap.add_argument("--ops", default="peaks,bias_gelu,reduce,row_reduce,gemm_bf16,dag_fused,dag_unfused,dag_fanout,gemm_f32",
                     help="comma list of extra configs to report under 'ops' ('' for none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", default="", help="run one small case per named kernel for ncu and exit")

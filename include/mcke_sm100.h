@@ -264,6 +264,20 @@ int mcke_sm100_gemm_bf16_ex(const uint16_t* a, const uint16_t* b, void* c, int c
  * (variant, dtype) selects for a large aligned shape. */
 int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm_attrs* out);
 
+/* ---- roofline denominators (replace bench/stream_triad.cu and bench/fma_peak.cu) ----
+ * Measurement probes, timed by the caller: a = b + scalar * c (12 bytes per
+ * element moved) and a = b (8 bytes per element) with 128-bit streaming loads
+ * and evict-first stores; n % 4 == 0 and 16-byte aligned arrays. */
+int mcke_sm100_peak_triad_f32(float* a, const float* b, const float* c, float scalar, int64_t n,
+                              mcke_stream_t stream);
+int mcke_sm100_peak_copy_f32(float* a, const float* b, int64_t n, mcke_stream_t stream);
+/* FFMA throughput: `threads` threads (a multiple of 256; the suggested count,
+ * 8 blocks of 256 per SM, comes from mcke_sm100_peak_fma_threads) each run 8
+ * independent chains acc = fma(acc, 0.999, 1.0) for `iters` steps from
+ * seed[thread] and store one sum to out[thread]: 16 flop per thread per step. */
+int64_t mcke_sm100_peak_fma_threads(void);
+int mcke_sm100_peak_fma_f32(const float* seed, float* out, int64_t threads, int iters, mcke_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,10 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_check_device_errors": (i32, [vp]),
             "mcke_sm100_watchdog_selftest": (i32, [vp]),
             "mcke_sm100_vector_add_f32": (i32, [vp, vp, vp, sz, vp]),
+            "mcke_sm100_peak_triad_f32": (i32, [vp, vp, vp, f32, i64, vp]),
+            "mcke_sm100_peak_copy_f32": (i32, [vp, vp, i64, vp]),
+            "mcke_sm100_peak_fma_threads": (i64, []),
+            "mcke_sm100_peak_fma_f32": (i32, [vp, vp, i64, i32, vp]),
             "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
             "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),
             "mcke_sm100_activation_f32": (i32, [vp, vp, i64, i32, i32, vp]),
@@ -131,6 +135,37 @@ def vector_add(a, b, out=None, stream=None):
     _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
     out = torch.empty_like(a) if out is None else out
     _check(lib().mcke_sm100_vector_add_f32(_ptr(a), _ptr(b), _ptr(out), a.numel(), _stream(a, stream)))
+    return out
+
+
+# ---- roofline denominators ---------------------------------------------------
+
+PEAK_FMA_FLOP_PER_THREAD_STEP = 16  # 8 chains x (multiply + add)
+
+
+def peak_triad(a, b, c, scalar: float = 3.0, stream=None):
+    """a = b + scalar * c (float32, 12 bytes moved per element)."""
+    for t, nm in ((a, "a"), (b, "b"), (c, "c")):
+        _need(t, torch.float32, nm)
+    _check(lib().mcke_sm100_peak_triad_f32(_ptr(a), _ptr(b), _ptr(c), float(scalar), a.numel(), _stream(a, stream)))
+    return a
+
+
+def peak_copy(a, b, stream=None):
+    """a = b (float32, 8 bytes moved per element)."""
+    _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
+    _check(lib().mcke_sm100_peak_copy_f32(_ptr(a), _ptr(b), a.numel(), _stream(a, stream)))
+    return a
+
+
+def peak_fma_threads() -> int:
+    return int(lib().mcke_sm100_peak_fma_threads())
+
+
+def peak_fma(seed, out, iters: int, stream=None):
+    """FFMA probe: PEAK_FMA_FLOP_PER_THREAD_STEP * seed.numel() * iters flop."""
+    _need(seed, torch.float32, "seed"); _need(out, torch.float32, "out")
+    _check(lib().mcke_sm100_peak_fma_f32(_ptr(seed), _ptr(out), seed.numel(), int(iters), _stream(seed, stream)))
     return out
 
 

@@ -567,3 +567,31 @@ def test_bounded_wait_expiry_is_reported_and_the_context_survives():
     mcke.check_device_errors()  # the word was cleared
     x = dev(oracle.fill_random(4096, 3))
     assert mcke.decode_result(mcke.reduce_full(x))[2] == int(np.argmax(host(x)))
+
+
+def test_peak_probes():
+    # the roofline probes (triad, copy, FFMA) compute what they claim
+    n = 1 << 20
+    idx = torch.arange(n, device=DEV, dtype=torch.float32)
+    b = idx % 97
+    c = (idx % 13) * 0.5
+    a = torch.empty(n, device=DEV)
+    mcke.peak_triad(a, b, c, 3.0)
+    assert torch.equal(a, b + 3.0 * c)  # small integers and halves: exact either way
+    a2 = torch.empty(n, device=DEV)
+    mcke.peak_copy(a2, b)
+    assert torch.equal(a2, b)
+    with pytest.raises(mcke.MckeError):
+        mcke.peak_copy(a2[:7], b[:7])  # n % 4 != 0
+    nt = mcke.peak_fma_threads()
+    assert nt > 0 and nt % 256 == 0
+    seed = (torch.arange(512, device=DEV, dtype=torch.float32) % 13)
+    out = torch.empty(512, device=DEV)
+    mcke.peak_fma(seed, out, 100)
+    mcke.check_device_errors()
+    s = seed.cpu().numpy().astype(np.float64)
+    acc = np.stack([s + j for j in range(8)])
+    for _ in range(100):  # fma(acc, m, 1): acc * m is exact in float64
+        acc = (acc * np.float64(np.float32(0.999)) + 1.0).astype(np.float32).astype(np.float64)
+    want = acc.astype(np.float32).sum(axis=0, dtype=np.float32)
+    np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5)

@@ -190,12 +190,12 @@ int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, int64_t count
  * slot `rank` of every rank's exchange buffer over peer memory, waits (bounded,
  * 1 s) for all ranks' slots in its own buffer and writes the combined result,
  * folded in rank order.  One kernel per call and no workspace: the pass-1
- * partials go to this rank's own buffer, whose CTA 0 folds them.
+ * partials go to this rank's own buffer, and the CTA that finishes last folds them.
  * peer_buffers: DEVICE array of `world` pointers to the ranks' exchange
  * buffers as mapped in this process (this rank's own at index `rank`), each
  * mcke_sm100_reduce_p2p_buffer_bytes(world) bytes (2 * world 64-byte exchange
  * slots, then 444 slots for this rank's pass-1 partials, then an epoch
- * counter; every 8-byte word of a slot carries 4 data bytes and the epoch, so
+ * counter and the CTAs' arrival count; every 8-byte word of a slot carries 4 data bytes and the epoch, so
  * no fence orders data and flag), zeroed before first use.  epoch: 1, 2, 3,
  * ... < 2^32, one per call, the same on every rank; or 0 on every call: the
  * kernel then takes the next value of the counter in this rank's buffer and

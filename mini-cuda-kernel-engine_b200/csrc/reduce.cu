@@ -106,51 +106,23 @@ int64_t full_blocks(int64_t n) {
   return g < 1 ? 1 : g;
 }
 
-// Pass 1.  Each CTA walks its
-// chunks of 1024 float4 (16 KB; chunk c goes to CTA c mod G) through a 4-stage
-// ring in shared memory filled by bulk asynchronous copies (cp.async.bulk,
-// completion counted on an mbarrier per stage), so a CTA keeps 64 KB of reads
-// in flight with almost no registers and 3 CTAs per SM keep ~190 KB per SM in
-// flight -- enough to stream HBM at full rate.  Threads read their float4s
-// from shared memory in per-thread increasing index order (thread t takes
-// float4 t, t+256, ... of each chunk, chunks in increasing order).  The
-// running maximum is updated once per float4; on an update the float4's index
-// and its first element equal to the maximum (its own bits, so a -0 ahead of
-// a +0 wins) are remembered.  A later float4 with an equal maximum never replaces an
-// earlier one, so the lowest index survives.  Head and tail elements (outside
-// whole 16-byte float4s) go to global thread 0: head first, tail last.  Waits on
-// the ring are bounded: on expiry the CTA records the site in a device word
-// (read by mcke_sm100_check_device_errors), waits for the copies it issued,
-// and stops.
-constexpr int kStreamStages = 4;
-constexpr int kChunkVec = 1024;                        // float4 per chunk (16 KB)
-constexpr std::size_t kStreamSmem = kStreamStages * kChunkVec * 16 + 64;
-constexpr unsigned long long kStreamWaitNs = 2000000000ull;
+// Pass 1.  Thread g of the grid (G CTAs of 256) reads float4 g, g + 256 G,
+// g + 512 G, ... of the 16-byte aligned body, kLoads of them in flight at a
+// time (128-bit loads that bypass L1), and accumulates them in per-thread
+// increasing index order: the sum in double, the running maximum once per
+// float4.  On an update the float4's index and its first element equal to
+// the maximum (its own bits, so a -0 ahead of a +0 wins) are remembered; a
+// later float4 with an equal maximum never replaces an earlier one, so the
+// lowest index survives.  Head and tail elements (outside whole 16-byte
+// float4s) go to global thread 0: head first, tail last.  Measured on B200
+// (events, L2 flushed, both launches) against the first version, a ring of
+// 16 KB bulk copies into shared memory per CTA with two CTA barriers per
+// chunk: 2^23 floats 21.5 -> 17.4 us, 2^25 35.8 -> 33.8 us, 2^28 175.1 ->
+// 166.9 us (6.43 TB/s): no barrier per chunk, and a round's loads overlap
+// the previous round's FP64 adds.
+constexpr int kLoads = 4;
 
 __device__ uint32_t g_reduce_watchdog;
-
-__device__ __forceinline__ uint32_t s_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ bool stream_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  unsigned long long t0 = 0;
-  for (uint32_t it = 0;; ++it) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    if (it == 0) t0 = t;
-    else if (t - t0 > kStreamWaitNs) return false;
-  }
-}
 
 // ---- peer-to-peer combine of a sharded full reduce ----------------------------
 //
@@ -182,9 +154,14 @@ struct P2pArgs {
   int auto_epoch;  // 1: the epoch is the counter after the part area, advanced by each call
 };
 
-// Counter of the automatic epochs: the 64-byte slot after the part area.
+// Counter of the automatic epochs: the 64-byte slot after the part area
+// (first 8 bytes); the CTAs' arrival count of the current call follows it
+// (bytes 8-11, back at 0 between calls).
 __device__ __forceinline__ unsigned long long* epoch_counter(const P2pArgs& a) {
   return reinterpret_cast<unsigned long long*>(a.peers[a.rank] + 2 * a.world + kFullCtaCap);
+}
+__device__ __forceinline__ unsigned int* arrival_count(const P2pArgs& a) {
+  return reinterpret_cast<unsigned int*>(epoch_counter(a) + 1);
 }
 
 // With automatic epochs, resolve this call's tag (every CTA reads the counter
@@ -282,42 +259,16 @@ __device__ void p2p_publish_and_combine(const Part& mine, const P2pArgs& a, Part
 }
 
 template <bool kP2p>
-__global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
+__global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
                                                                       Part* __restrict__ parts, P2pArgs p2p_in) {
   P2pArgs p2p = p2p_in;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(16) uint8_t smem[];  // P2P: the ranks' collected partials
   __shared__ Part red[kWarps];
-  const float4* ring = reinterpret_cast<const float4*>(smem);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStreamStages * kChunkVec * 16);
   const int tid = threadIdx.x;
   const float* xa = x + head;
   const int64_t nv = (n - head) / 4;
-  const int64_t nchunks = (nv + kChunkVec - 1) / kChunkVec;
-  const int64_t G = gridDim.x;
-  const int64_t mine = nchunks > static_cast<int64_t>(blockIdx.x) ? (nchunks - blockIdx.x + G - 1) / G : 0;
-
-  if (tid == 0) {
-    for (int s = 0; s < kStreamStages; ++s)
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(s_addr(full + s)) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  __syncthreads();
-
-  auto issue = [&](int64_t i) {  // thread 0: my i-th chunk into stage i % kStreamStages
-    const int64_t v0 = (static_cast<int64_t>(blockIdx.x) + i * G) * kChunkVec;
-    const int64_t cnt = (nv - v0 < kChunkVec) ? nv - v0 : kChunkVec;
-    const uint32_t bytes = static_cast<uint32_t>(cnt * 16);
-    const uint32_t bar = s_addr(full + (i % kStreamStages));
-    const uint32_t dst = s_addr(ring + (i % kStreamStages) * kChunkVec);
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(xa + 4 * v0), "r"(bytes), "r"(bar)
-                 : "memory");
-  };
-  if (tid == 0)
-    for (int64_t i = 0; i < mine && i < kStreamStages; ++i) issue(i);
+  const int64_t S = static_cast<int64_t>(gridDim.x) * kThreads;  // grid stride, in float4
 
   Part p = part_identity();
   if (blockIdx.x == 0 && tid == 0)
@@ -328,46 +279,38 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
   int lbest = 0;
   float mbest = 0.f;
   const bool have_index = p.i >= 0;
-  bool failed = false;
-  int64_t i = 0;
-  for (; i < mine; ++i) {
-    const int stage = static_cast<int>(i % kStreamStages);
-    const bool ok = stream_wait(s_addr(full + stage), static_cast<uint32_t>((i / kStreamStages) & 1));
-    if (__syncthreads_or(!ok)) {
-      failed = true;
-      break;
-    }
-    const int64_t v0 = (static_cast<int64_t>(blockIdx.x) + i * G) * kChunkVec;
-    const int cnt = static_cast<int>((nv - v0 < kChunkVec) ? nv - v0 : kChunkVec);
-    const float4* buf = ring + stage * kChunkVec;
-#pragma unroll 4
-    for (int j = tid; j < cnt; j += kThreads) {
-      const float4 q = buf[j];
-      s += static_cast<double>(q.x);
-      s += static_cast<double>(q.y);
-      s += static_cast<double>(q.z);
-      s += static_cast<double>(q.w);
-      const float lm = fmaxf(fmaxf(q.x, q.y), fmaxf(q.z, q.w));
+  // Thread g reads float4 g, g + S, ... in increasing order, kLoads per
+  // round, the next round's loads issued before this round's arithmetic.
+  int64_t v0 = static_cast<int64_t>(blockIdx.x) * kThreads + tid;
+  float4 q[kLoads], nxt[kLoads];
+#pragma unroll
+  for (int u = 0; u < kLoads; ++u)
+    if (v0 + u * S < nv) q[u] = ld_stream_f4(xa + 4 * (v0 + u * S));
+  for (; v0 < nv; v0 += kLoads * S) {
+    const int64_t v1 = v0 + kLoads * S;
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u)
+      if (v1 + u * S < nv) nxt[u] = ld_stream_f4(xa + 4 * (v1 + u * S));
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+      const int64_t v = v0 + u * S;
+      if (v >= nv) break;
+      s += static_cast<double>(q[u].x);
+      s += static_cast<double>(q[u].y);
+      s += static_cast<double>(q[u].z);
+      s += static_cast<double>(q[u].w);
+      const float lm = fmaxf(fmaxf(q[u].x, q[u].y), fmaxf(q[u].z, q[u].w));
       if (lm > m || (vbest < 0 && !have_index && lm == m)) {
         m = lm;
-        vbest = v0 + j;
+        vbest = v;
         // the float4's first element equal to its maximum, with its own bits
         // (so a -0 ahead of a +0 wins)
-        lbest = (q.x == lm) ? 0 : (q.y == lm) ? 1 : (q.z == lm) ? 2 : 3;
-        mbest = lbest == 0 ? q.x : lbest == 1 ? q.y : lbest == 2 ? q.z : q.w;
+        lbest = (q[u].x == lm) ? 0 : (q[u].y == lm) ? 1 : (q[u].z == lm) ? 2 : 3;
+        mbest = lbest == 0 ? q[u].x : lbest == 1 ? q[u].y : lbest == 2 ? q[u].z : q[u].w;
       }
     }
-    __syncthreads();  // every thread is done with this stage before it is refilled
-    if (tid == 0 && i + kStreamStages < mine) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // reads before the async refill
-      issue(i + kStreamStages);
-    }
-  }
-  if (failed && tid == 0) {
-    atomicCAS(&g_reduce_watchdog, 0u, 1u);
-    // Let the copies already issued land before the CTA exits.
-    for (int64_t k = i; k < mine && k < i + kStreamStages; ++k)
-      stream_wait(s_addr(full + (k % kStreamStages)), static_cast<uint32_t>((k / kStreamStages) & 1));
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) q[u] = nxt[u];
   }
   p.s = s;
   if (vbest >= 0) {
@@ -379,23 +322,35 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
   p = block_combine(p, red);
   if (!kP2p && tid == 0) parts[blockIdx.x] = p;
   if constexpr (kP2p) {
-    // Hand-off without an atomic or a fence: every CTA stores its partial in
-    // its slot of this rank's part area (low-latency format); CTA 0 collects
-    // them as they arrive -- thread t the virtual lanes t and t+256 of
+    // Every CTA stores its partial in its slot of this rank's part area
+    // (low-latency format) and counts itself in; the CTA that arrives last
+    // collects the slots -- thread t the virtual lanes t and t+256 of
     // reduce_full_combine_kernel's 1024-thread fold (G <= kFullCtaCap < 512,
-    // so the rest are the identity) -- which makes the shard partial
-    // bit-identical to the two-launch path, and runs the exchange.  Only CTA 0
-    // waits, on CTAs that never wait, so the grid cannot deadlock.
+    // so the rest are the identity), which makes the shard partial
+    // bit-identical to the two-launch path -- and runs the exchange.  No CTA
+    // waits for another CTA of the grid.
     resolve_tag(p2p);
     LLSlot* local = p2p.peers[p2p.rank] + 2 * p2p.world;
-    if (tid == 0) ll_store(local + blockIdx.x, p, p2p.tag);
-    if (blockIdx.x != 0) return;
+    __shared__ int is_last;
+    if (tid == 0) {
+      ll_store(local + blockIdx.x, p, p2p.tag);
+      __threadfence();
+      is_last = atomicAdd(arrival_count(p2p), 1u) == gridDim.x - 1u ? 1 : 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
     __shared__ Part red32[16];
     __shared__ Part shard;
     __shared__ int parts_ok;
-    if (tid == 0) parts_ok = 1;
-    __syncthreads();
     const int G = static_cast<int>(gridDim.x);
+    if (tid == 0) {
+      parts_ok = 1;
+      *arrival_count(p2p) = 0u;  // the next call counts from 0
+    }
+    __syncthreads();
+    // Every slot is written (each CTA stored before counting itself in), so
+    // all 256 threads read their two slots at once: one round trip.  The
+    // tags are checked all the same (bounded wait).
     Part v0 = part_identity(), v1 = part_identity(), q0, q1;
     const bool got = ll_wait(tid < G ? local + tid : nullptr, tid + kThreads < G ? local + tid + kThreads : nullptr,
                              p2p.tag, q0, q1);
@@ -421,8 +376,7 @@ __global__ void __launch_bounds__(kThreads) reduce_full_stream_kernel(const floa
       }
     }
     __syncthreads();
-    // the ring is idle now (every bulk copy has landed): its shared memory
-    // holds the collected slots
+    // dynamic shared memory: the ranks' results, collected in rank order
     p2p_publish_and_combine(shard, p2p, reinterpret_cast<Part*>(smem));
   }
 }
@@ -574,25 +528,6 @@ using namespace mcke_sm100;
 
 namespace mcke_sm100 {
 namespace {
-// The streamed pass 1 needs 64 KB of dynamic shared memory: opt in once per device.
-std::mutex g_stream_mu;
-bool g_stream_attr[64] = {};
-int ensure_stream_smem(const char* who) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
-    return fail(MCKE_CUDA_ERROR, "%s: no usable current device", who);
-  std::lock_guard<std::mutex> lk(g_stream_mu);
-  if (!g_stream_attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(reduce_full_stream_kernel<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kStreamSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(reduce_full_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(kStreamSmem));
-    if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
-    g_stream_attr[dev] = true;
-  }
-  return MCKE_OK;
-}
 }  // namespace
 
 // Reads and clears the streamed reduce's watchdog word on the current device.
@@ -642,8 +577,7 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   Part* parts = static_cast<Part*>(workspace);
-  MCKE_RETURN_IF(ensure_stream_smem(who));
-  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, index_base, parts, P2pArgs{});
+  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, index_base, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
   if (final_result) reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   else reduce_full_combine_kernel<false><<<1, 1024, 0, s>>>(parts, g, out);
@@ -814,8 +748,7 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   // array's leftover contents from an earlier call are never read and nothing
   // needs clearing.
   Part* parts = static_cast<Part*>(scratch);
-  MCKE_RETURN_IF(ensure_stream_smem(who));
-  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(x, n, head, 0, parts, P2pArgs{});
+  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, 0, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
   reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
   return check_launch(who);
@@ -867,8 +800,8 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   const uintptr_t addr = reinterpret_cast<uintptr_t>(x);
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
-  MCKE_RETURN_IF(ensure_stream_smem(who));
-  reduce_full_stream_kernel<true><<<static_cast<unsigned>(g), kThreads, kStreamSmem, s>>>(
+  // dynamic shared memory: the ranks' collected partials (world <= 1024: 24 KB)
+  reduce_full_stream_kernel<true><<<static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s>>>(
       x, n, head, index_base, nullptr, a);
   return check_launch(who);
 }

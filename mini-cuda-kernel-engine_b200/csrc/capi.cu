@@ -125,7 +125,8 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site == 2)
     return fail(MCKE_INTERNAL, "reduce (p2p exchange): a peer's partial did not arrive within 1 s; the result is incomplete");
   if (site != 0)
-    return fail(MCKE_INTERNAL, "reduce (streamed): a bounded wait expired; the result is incomplete");
+    return fail(MCKE_INTERNAL,
+                "reduce (one-kernel step): a CTA's partial did not arrive within 1 s; the result is incomplete");
   MCKE_RETURN_IF(read_softmax_watchdog(&site));
   if (site != 0)
     return fail(MCKE_INTERNAL, "softmax (streamed): a bounded wait expired; the result is incomplete");

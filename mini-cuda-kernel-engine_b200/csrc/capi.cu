@@ -217,7 +217,9 @@ extern "C" int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm
   int threads = 0;
   EpilogueParams ep{1.0f, 0.0f, nullptr, 0, 0, 1};
   if (bf16 && variant != MCKE_GEMM_SIMT) {
-    launch_gemm_tcgen05(nullptr, nullptr, nullptr, 0, 0, 0, ep, nullptr, &kernel, &dyn);
+    // M > 128 selects the 2-CTA pair kernel that large shapes run; N = 0 stops
+    // the launcher after the choice (both pair tiles have the same footprint).
+    launch_gemm_tcgen05(nullptr, nullptr, nullptr, 8192, 0, 0, ep, nullptr, &kernel, &dyn);
     threads = 320;
   } else if (variant == MCKE_GEMM_TCGEN05) {
     return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands", who);

@@ -315,7 +315,7 @@ def test_reduce_row_golden_vectors(vectors):
 
 
 @pytest.mark.parametrize("rows,cols", [(7, 333), (256, 4096), (64, 65536), (3, 1), (5, 17), (4099, 1024),
-                                       (60001, 12), (9, 1020)])
+                                       (60001, 12), (9, 1020), (5000, 128), (333, 256), (71, 512), (3, 1024)])
 def test_reduce_row_matches_oracle(rows, cols):
     x = oracle.fill_random(rows * cols, 13).reshape(rows, cols)
     for kind in ("sum", "max", "mean"):

@@ -264,6 +264,21 @@ int mcke_sm100_gemm_bf16_ex(const uint16_t* a, const uint16_t* b, void* c, int c
  * (variant, dtype) selects for a large aligned shape. */
 int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm_attrs* out);
 
+/* The schedule mcke_sm100_gemm_bf16_ex(variant, c_dtype) takes for an m x n x k
+ * product on a GPU with `sm_count` SMs, assuming 16-byte aligned A, B and C
+ * and beta == 0: host arithmetic only (no device is touched), for tests and
+ * for callers that size work to whole waves. */
+typedef struct {
+  int kernel;         /* 0: CUDA-core kernel, 1: tcgen05 one CTA per tile, 2: tcgen05 CTA pairs */
+  int tile_m, tile_n; /* output tile */
+  int64_t tiles;      /* tiles of C */
+  int64_t ctas;       /* CTAs launched */
+  int split_dp_tiles; /* split-k schedule: tiles run whole before it (0 when not split) */
+  int split_kblocks;  /* split-k schedule: 64-deep k-blocks per CTA pair after them; 0 = not split */
+} mcke_gemm_plan;
+int mcke_sm100_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int c_dtype, int sm_count,
+                         mcke_gemm_plan* out);
+
 /* ---- roofline denominators (replace bench/stream_triad.cu and bench/fma_peak.cu) ----
  * Measurement probes, timed by the caller: a = b + scalar * c (12 bytes per
  * element moved) and a = b (8 bytes per element) with 128-bit streaming loads

@@ -49,6 +49,16 @@ int read_softmax_watchdog(uint32_t* site);
 
 namespace {
 
+// The variant word of mcke_sm100_gemm_bf16_ex as launch_gemm_tcgen05's tile
+// word: bits 0-1 the pair tile (1 = 256 x 256, 2 = 256 x 512), bits 2-3 the
+// split-k schedule (1 = never, 2 = where it applies), 0 = choose.
+static int tile_word(int variant) {
+  return variant == MCKE_GEMM_TCGEN05_WIDE     ? (2 | 4)
+         : variant == MCKE_GEMM_TCGEN05_NARROW ? (1 | 4)
+         : variant == MCKE_GEMM_TCGEN05_SPLIT  ? (2 | 8)
+                                               : 0;
+}
+
 int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m, int64_t n,
                int64_t k, bool bf16_in, int c_dtype, float alpha, float beta, const float* bias,
                int act, int variant, mcke_stream_t stream) {
@@ -69,12 +79,7 @@ int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
   if (variant < MCKE_GEMM_AUTO || variant > MCKE_GEMM_TCGEN05_SPLIT)
     return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
-  // launch_gemm_tcgen05's tile word: bits 0-1 the pair tile (1 = 256 x 256,
-  // 2 = 256 x 512), bits 2-3 the split-k schedule (1 = never, 2 = where it applies)
-  const int tile = variant == MCKE_GEMM_TCGEN05_WIDE     ? (2 | 4)
-                   : variant == MCKE_GEMM_TCGEN05_NARROW ? (1 | 4)
-                   : variant == MCKE_GEMM_TCGEN05_SPLIT  ? (2 | 8)
-                                                         : 0;
+  const int tile = tile_word(variant);
   if (tile != 0) variant = MCKE_GEMM_TCGEN05;
   if (!bf16_in && variant == MCKE_GEMM_TCGEN05)
     return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel takes bf16 operands; no fallback is applied", who);
@@ -203,6 +208,43 @@ extern "C" int mcke_sm100_gemm_bf16_ex(const uint16_t* a, const uint16_t* b, voi
                                        mcke_stream_t stream) {
   return gemm_front("mcke_sm100_gemm_bf16_ex", a, b, c, m, n, k, true, c_dtype, alpha, beta, bias,
                     act, variant, stream);
+}
+
+extern "C" int mcke_sm100_gemm_plan(int64_t m, int64_t n, int64_t k, int variant, int c_dtype, int sm_count,
+                                    mcke_gemm_plan* out) {
+  static const char* who = "mcke_sm100_gemm_plan";
+  clear_error();
+  if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
+  if (m < 0 || n < 0 || k < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (m > 2147483647LL || n > 2147483647LL || k > 2147483647LL)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: extent exceeds INT32_MAX", who);
+  if (variant < MCKE_GEMM_AUTO || variant > MCKE_GEMM_TCGEN05_SPLIT)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown variant %d", who, variant);
+  if (c_dtype != MCKE_DTYPE_F32 && c_dtype != MCKE_DTYPE_BF16)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown output dtype %d", who, c_dtype);
+  if (sm_count < 2) return fail(MCKE_INVALID_ARGUMENT, "%s: sm_count must be at least 2", who);
+  const bool tc_ok = k > 0 && k % 8 == 0 && n % 8 == 0;
+  const bool want_tc = variant != MCKE_GEMM_AUTO && variant != MCKE_GEMM_SIMT;
+  if (want_tc && !tc_ok)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: the tcgen05 kernel needs k > 0, K %% 8 == 0 and N %% 8 == 0", who);
+  *out = mcke_gemm_plan{};
+  if (tc_ok && variant != MCKE_GEMM_SIMT) {
+    const TcSchedule r = tc_schedule(m, n, k, tile_word(variant), c_dtype == MCKE_DTYPE_BF16, sm_count);
+    out->kernel = r.pair ? 2 : 1;
+    out->tile_m = r.tile_m;
+    out->tile_n = r.tile_n;
+    out->tiles = r.tiles;
+    out->ctas = (m == 0 || n == 0) ? 0 : r.ctas;
+    out->split_dp_tiles = r.split_dp_tiles;
+    out->split_kblocks = r.split_kblocks;
+  } else {
+    out->kernel = 0;
+    out->tile_m = 128;
+    out->tile_n = 128;
+    out->tiles = ((m + 127) / 128) * ((n + 127) / 128);
+    out->ctas = out->tiles;
+  }
+  return MCKE_OK;
 }
 
 extern "C" int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm_attrs* out) {

@@ -74,6 +74,15 @@ bool tcgen05_shape_ok(const void* a, const void* b, const void* c, int64_t m, in
                       bool out_bf16);
 // fp32 GEMM on the tensor cores in the 3xTF32 form (split kernels, then the
 // tcgen05 kernel); workspace holds the hi/lo parts of A and B.
+// Host-only view of a bf16 tcgen05 launch's schedule (mcke_sm100_gemm_plan).
+struct TcSchedule {
+  bool pair, wide;
+  int tile_m, tile_n;
+  int64_t tiles, ctas;
+  int split_dp_tiles, split_kblocks;
+};
+TcSchedule tc_schedule(int64_t m, int64_t n, int64_t k, int tile, bool out_bf16, int sms);
+
 std::size_t gemm_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
                        const EpilogueParams& ep, void* workspace, cudaStream_t s, const void** kernel_out,

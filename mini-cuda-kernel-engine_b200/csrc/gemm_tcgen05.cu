@@ -1145,8 +1145,7 @@ double tile_waves(int64_t tiles, int64_t units, bool split) {
     return static_cast<double>(tiles) / units;
   return static_cast<double>((tiles + units - 1) / units);
 }
-bool wide_pays(int64_t m, int64_t n, int64_t k, bool can_split) {
-  const int64_t units = sm_count() / 2;
+bool wide_pays(int64_t m, int64_t n, int64_t k, bool can_split, int64_t units) {
   const int64_t rows = (m + 255) / 256;
   const int64_t narrow = rows * ((n + 255) / 256), wide = rows * ((n + 511) / 512);
   const double t_narrow = tile_waves(narrow, units, can_split && split_shape_ok(m, n, 256, narrow, true));
@@ -1158,7 +1157,7 @@ bool wide_pays(int64_t m, int64_t n, int64_t k, bool can_split) {
 // The split-k schedule of a pair launch, or none (w = 0).  Whole waves but
 // the last run unsplit, so most tiles keep the data-parallel order.
 SplitK plan_split(int64_t tiles, int pairs, int64_t k, int tile_n, int64_t m, int64_t n, bool tma_fp32_out,
-                  bool force) {
+                  bool force, bool take_slot = true) {
   SplitK sk = {0, 0, 0, 0u};
   if (!split_shape_ok(m, n, tile_n, tiles, tma_fp32_out) || pairs < 2) return sk;
   if (!force && (busy_fraction(tiles, pairs) >= kSplitBelow || tiles < kSplitMinWaves * pairs)) return sk;
@@ -1168,14 +1167,45 @@ SplitK plan_split(int64_t tiles, int pairs, int64_t k, int tile_n, int64_t m, in
   const int64_t w = (total + pairs - 1) / pairs;
   // short ranges, or more contributors to a tile than the flag's 8 bits count
   if (w < 4 || (kblocks + w - 1) / w + 1 >= 255) return sk;
-  static std::atomic<uint32_t> launches{0};
-  const uint32_t seq = launches.fetch_add(1u, std::memory_order_relaxed);
   sk.tiles_dp = static_cast<int>(dp);
   sk.w = static_cast<int>(w);
+  if (!take_slot) return sk;
+  static std::atomic<uint32_t> launches{0};
+  const uint32_t seq = launches.fetch_add(1u, std::memory_order_relaxed);
   sk.slot = static_cast<int>(seq % kSplitSlots);
   sk.tag = (seq / kSplitSlots) % 0xFFFFFFu + 1u;
   return sk;
 }
+
+}  // namespace
+
+// The schedule a bf16 launch of this shape takes on a GPU with `sms` SMs
+// (one CTA per SM), by the same rules as launch_tc and with no device query:
+// A, B and C 16-byte aligned, beta == 0.
+TcSchedule tc_schedule(int64_t m, int64_t n, int64_t k, int tile, bool out_bf16, int sms) {
+  TcSchedule r{};
+  const int tile_sel = tile & 3, split_sel = (tile >> 2) & 3;
+  const bool tma_fp32_out = (n % 8 == 0) && !out_bf16;
+  const int pairs = sms / 2;
+  r.pair = m > Cfg<false>::BM;
+  r.wide = r.pair && n >= 512 &&
+           (tile_sel == 2 || (tile_sel == 0 && wide_pays(m, n, k, split_sel != 1 && tma_fp32_out, pairs)));
+  r.tile_m = r.pair ? 256 : 128;
+  r.tile_n = r.wide ? 512 : 256;
+  r.tiles = ((m + r.tile_m - 1) / r.tile_m) * ((n + r.tile_n - 1) / r.tile_n);
+  if (!r.pair) {
+    r.ctas = r.tiles < sms ? r.tiles : sms;
+    return r;
+  }
+  SplitK sk = {0, 0, 0, 0u};
+  if (split_sel != 1) sk = plan_split(r.tiles, pairs, k, r.tile_n, m, n, tma_fp32_out, split_sel == 2, false);
+  r.split_dp_tiles = sk.tiles_dp;
+  r.split_kblocks = sk.w;
+  r.ctas = 2 * (sk.w == 0 && r.tiles < pairs ? r.tiles : pairs);
+  return r;
+}
+
+namespace {
 
 // Common launcher of both operand types: bf16 (a, b) or 3xTF32 (a, b = the hi
 // parts, alo, blo = the lo parts).
@@ -1199,7 +1229,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   bool wide = false;
   if constexpr (!kTf32) {
     if (pair && n >= 512)
-      wide = tile_sel == 2 || (tile_sel == 0 && wide_pays(m, n, k, split_sel != 1 && tma_fp32_out));
+      wide = tile_sel == 2 || (tile_sel == 0 && wide_pays(m, n, k, split_sel != 1 && tma_fp32_out, sm_count() / 2));
   }
   KernelFn kfn;
   std::size_t smem;

@@ -89,6 +89,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_gemm_bf16": (i32, [vp, vp, vp, i64, i64, i64, f32, f32, i32, vp]),
             "mcke_sm100_gemm_bf16_ex": (i32, [vp, vp, vp, i32, i64, i64, i64, f32, f32, vp, i32, i32, vp]),
             "mcke_sm100_gemm_kernel_attrs": (i32, [i32, i32, vp]),
+            "mcke_sm100_gemm_plan": (i32, [i64, i64, i64, i32, i32, i32, vp]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(l, name)
@@ -396,6 +397,21 @@ def gemm_kernel_attrs(variant="auto", dtype="bf16") -> dict:
     v = GEMM_VARIANT[variant] if isinstance(variant, str) else int(variant)
     _check(lib().mcke_sm100_gemm_kernel_attrs(v, DTYPE[dtype], ctypes.byref(out)))
     return {f: getattr(out, f) for f, _ in GemmAttrs._fields_}
+
+
+class GemmPlan(ctypes.Structure):
+    _fields_ = [("kernel", ctypes.c_int), ("tile_m", ctypes.c_int), ("tile_n", ctypes.c_int),
+                ("tiles", ctypes.c_int64), ("ctas", ctypes.c_int64), ("split_dp_tiles", ctypes.c_int),
+                ("split_kblocks", ctypes.c_int)]
+
+
+def gemm_plan(m: int, n: int, k: int, variant="auto", out_dtype="f32", sm_count: int = 148) -> dict:
+    """The schedule mcke_sm100_gemm_bf16_ex takes for this shape (host arithmetic
+    only: aligned operands and beta == 0 assumed; no GPU needed)."""
+    out = GemmPlan()
+    v = GEMM_VARIANT[variant] if isinstance(variant, str) else int(variant)
+    _check(lib().mcke_sm100_gemm_plan(int(m), int(n), int(k), v, DTYPE[out_dtype], int(sm_count), ctypes.byref(out)))
+    return {f: getattr(out, f) for f, _ in GemmPlan._fields_}
 
 
 def check_device_errors(stream=None) -> None:

@@ -595,3 +595,24 @@ def test_peak_probes():
         acc = (acc * np.float64(np.float32(0.999)) + 1.0).astype(np.float32).astype(np.float64)
     want = acc.astype(np.float32).sum(axis=0, dtype=np.float32)
     np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5)
+
+
+@pytest.mark.parametrize("m,n,k", [(8192, 4096, 4096), (4096, 8192, 2048), (2048, 4096, 1024), (8192, 1024, 2048),
+                                   (300, 512, 256)])
+def test_gemm_plan_matches_the_launch(m, n, k):
+    # AUTO's result is bit-identical to the forced variant that
+    # mcke_sm100_gemm_plan names (split and unsplit differ in the last bits)
+    p = mcke.gemm_plan(m, n, k, "auto", "f32", torch.cuda.get_device_properties(DEV).multi_processor_count)
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(m + n + k)
+    ta = (torch.rand(m, k, generator=gen, device=DEV) * 2 - 1).to(torch.bfloat16)
+    tb = (torch.rand(k, n, generator=gen, device=DEV) * 2 - 1).to(torch.bfloat16)
+    auto = mcke.gemm(ta, tb, variant="tcgen05")
+    if p["split_kblocks"]:
+        assert p["tile_n"] == 512
+        forced = mcke.gemm(ta, tb, variant="tcgen05_split")
+    else:
+        forced = mcke.gemm(ta, tb, variant="tcgen05_wide" if p["tile_n"] == 512 else "tcgen05_narrow")
+    torch.cuda.synchronize()
+    mcke.check_device_errors()
+    assert torch.equal(auto, forced), p

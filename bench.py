@@ -726,6 +726,16 @@ def run_profile(args) -> None:
             ws = torch.empty(mcke.reduce_full_workspace_bytes(REDUCE_N), dtype=torch.uint8, device=dev)
             res = torch.empty(16, dtype=torch.uint8, device=dev)
             fn = lambda: mcke.reduce_full(x, out=res, workspace=ws)  # noqa: E731
+        elif name == "row_reduce":
+            x = torch.rand(ROWS, COLS, generator=gen, device=dev) * 2 - 1
+            y = torch.empty(ROWS, device=dev)
+            fn = lambda: mcke.reduce_row(x, "sum", out=y)  # noqa: E731
+        elif name == "bias_gelu_bf16":
+            # the DAG's H (config 5): 8192 x 16384 bf16, bias over 16384 columns
+            x = torch.randn(8192, 16384, generator=gen, device=dev).to(torch.bfloat16)
+            b = torch.rand(16384, generator=gen, device=dev) * 2 - 1
+            y = torch.empty_like(x)
+            fn = lambda: mcke.bias_act(x, b, "gelu_tanh", out=y)  # noqa: E731
         elif name == "gemm_bf16":
             a = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
             b = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)

@@ -68,7 +68,11 @@ typedef enum { MCKE_SOFTMAX_THREE_PASS = 0, MCKE_SOFTMAX_ONLINE = 1 } mcke_softm
  * N % 512 == 0): the k-blocks of the tiles past the last whole wave are divided
  * evenly over all CTA pairs and cut tiles are summed in C in k order
  * (deterministic; within the bf16 tolerance of the unsplit result).  AUTO and
- * TCGEN05 use it when whole waves would leave more than 5% of the pairs idle. */
+ * TCGEN05 use it when at least two whole waves exist and whole waves would
+ * leave more than 5% of the pairs idle.  Split launches that run at the same
+ * time on one device must be fewer than 128 split launches apart (a captured
+ * CUDA graph keeps its launch's flag slot); otherwise one may give up after
+ * 2 s and report MCKE_INTERNAL from mcke_sm100_check_device_errors(). */
 typedef enum {
   MCKE_GEMM_AUTO = 0,
   MCKE_GEMM_SIMT = 1,

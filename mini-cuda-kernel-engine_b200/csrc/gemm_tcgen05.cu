@@ -143,8 +143,12 @@ __device__ uint32_t g_tc_watchdog;
 //
 // Flags: one 32-bit word per (launch slot, tile, CTA rank), (tag << 8) | j
 // while in use, reset to 0 by the last contributor; the host gives every
-// launch the next slot of the ring and a fresh tag.
-constexpr int kSplitSlots = 32;
+// launch the next slot of the ring and a fresh tag.  Two split launches that
+// run at the same time on one device must be fewer than kSplitSlots launches
+// apart (a CUDA graph keeps the slot it was captured with); otherwise a
+// waiter can miss its flag and give up after 2 s with watchdog site 6.
+// 128 slots x 1024 tiles x 2 CTAs x 4 bytes = 1 MiB per device.
+constexpr int kSplitSlots = 128;
 constexpr int kSplitMaxTiles = 1024;
 __device__ uint32_t g_split_flags[kSplitSlots * kSplitMaxTiles * 2];
 

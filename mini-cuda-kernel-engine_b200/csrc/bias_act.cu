@@ -104,22 +104,6 @@ __global__ void __launch_bounds__(kThreads) activation_f32_kernel(const float* _
     V::store(y + i * VW, V::template act<F>(V::load(x + i * VW)));
 }
 
-// GELU (tanh form) for a bf16 output: v / (1 + e^{-2z}) as in ActGeluTanh,
-// with e^{-2z} = 2^{v (c0 + c1 v^2)}: c0 = -2 sqrt(2/pi) log2(e) and
-// c1 = 0.044715 c0, one hardware base-2 exponential (ex2.approx, ~2 ulp), then
-// the fast divide; the result is rounded to bf16's 8 significant bits right
-// after.  At the DAG's 8192 x 16384 this kernel is issue-bound: CUDA's
-// accurate expf took it from 94.2 us (fast exponential) to 102.4 us.
-struct ActGeluTanhBf16 {
-  static __device__ __forceinline__ float apply(float v) {
-    constexpr float c0 = -2.302208198144325;
-    constexpr float c1 = -0.1029432395800235;
-    const float t = v * fmaf(c1, v * v, c0);
-    float e;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
-    return __fdividef(v, 1.0f + e);
-  }
-};
 
 // bf16 x/y, float bias and math.  8 elements (16 bytes) per thread per row.
 template <class F>

@@ -459,10 +459,15 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 
 // ---- compile-time epilogue ----------------------------------------------------
 
-template <int kAct>
+// A bf16 output takes the GELU (tanh) with one hardware exponential
+// (ActGeluTanhBf16, ~2 fp32 ulp before the bf16 rounding): the wide tile's
+// epilogue does not overlap the main loop, and with expf it cost the fused
+// DAG more than the separate bias kernel did.
+template <int kAct, bool kBf16Out = false>
 __device__ __forceinline__ float epi_act(float v) {
   if constexpr (kAct == MCKE_ACT_RELU) return ActRelu::apply(v);
   else if constexpr (kAct == MCKE_ACT_GELU_ERF) return ActGeluErf::apply(v);
+  else if constexpr (kAct == MCKE_ACT_GELU_TANH && kBf16Out) return ActGeluTanhBf16::apply(v);
   else if constexpr (kAct == MCKE_ACT_GELU_TANH) return ActGeluTanh::apply(v);
   else return v;
 }
@@ -502,7 +507,7 @@ __device__ __forceinline__ void epi_vals(const EpilogueParams& ep, void* c, int 
       }
     }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = epi_act<kAct>(v[j]);
+    for (int j = 0; j < 32; ++j) v[j] = epi_act<kAct, kBf16Out>(v[j]);
     if constexpr (kBf16Out) {
       uint4* pc = reinterpret_cast<uint4*>(static_cast<uint16_t*>(c) + base);
 #pragma unroll
@@ -526,7 +531,7 @@ __device__ __forceinline__ void epi_vals(const EpilogueParams& ep, void* c, int 
       if (ep.beta != 0.0f) x = fmaf(ep.beta, static_cast<const float*>(c)[base + j], x);
     }
     if constexpr (kBias) x += __ldg(ep.bias + gn0 + j);
-    x = epi_act<kAct>(x);
+    x = epi_act<kAct, kBf16Out>(x);
     if constexpr (kBf16Out) static_cast<uint16_t*>(c)[base + j] = to_bf16(x);
     else static_cast<float*>(c)[base + j] = x;
   }
@@ -535,7 +540,7 @@ __device__ __forceinline__ void epi_vals(const EpilogueParams& ep, void* c, int 
 // alpha, bias and activation on 32 values of columns gn0.. (beta == 0; the
 // columns past N, clipped by the store, use no bias).  The same arithmetic,
 // in the same order, as epi_vals.
-template <bool kBias, int kAct>
+template <bool kBias, int kAct, bool kBf16Out>
 __device__ __forceinline__ void epi_math(const EpilogueParams& ep, int N, int gn0, float (&v)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = ep.alpha * v[j];
@@ -557,7 +562,7 @@ __device__ __forceinline__ void epi_math(const EpilogueParams& ep, int N, int gn
     }
   }
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = epi_act<kAct>(v[j]);
+  for (int j = 0; j < 32; ++j) v[j] = epi_act<kAct, kBf16Out>(v[j]);
 }
 
 template <bool kBf16Out, bool kBias, int kAct>
@@ -871,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int gn0 = nb * C::BN + u * 32;
                 if (lane == 0) bulk_wait_read_all();
                 __syncwarp();
-                epi_math<kBias, kAct>(ep, N, gn0, v);
+                epi_math<kBias, kAct, false>(ep, N, gn0, v);
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
                   st_shared_v4(my_row + ((static_cast<uint32_t>(q) ^ sw) << 4), __float_as_uint(v[4 * q]),
@@ -916,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-              epi_math<kBias, kAct>(ep, N, gn0 + sub * 32, v);
+              epi_math<kBias, kAct, kBf16Out>(ep, N, gn0 + sub * 32, v);
               if constexpr (kBf16Out) {
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {

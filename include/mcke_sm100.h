@@ -18,7 +18,7 @@
  *
  * Each declaration names the reference interface it replaces (path:line within
  * mini-cuda-kernel-engine).  The C++ launchers of include/mcke/kernels/kernels.hpp
- * become thin wrappers over these; the wrapper source is shown in INTEGRATION.md.
+ * become thin wrappers over these (mini-cuda-kernel-engine_b200/integration/kernels_sm100.cpp).
  */
 #ifndef MCKE_SM100_H_
 #define MCKE_SM100_H_
@@ -124,7 +124,7 @@ int mcke_sm100_check_device_errors(mcke_stream_t stream);
 /* Diagnostic with no counterpart in the reference: enqueues a one-thread kernel
  * that waits on a barrier nothing arrives on, so its bounded wait (2 s) expires
  * and records itself; the next mcke_sm100_check_device_errors() then returns
- * MCKE_INTERNAL naming site 6, and the context stays usable.  For testing the
+ * MCKE_INTERNAL naming site 9 (a site no other wait uses), and the context stays usable.  For testing the
  * failure path of the library's bounded waits without faulting a GPU. */
 int mcke_sm100_watchdog_selftest(mcke_stream_t stream);
 
@@ -223,13 +223,15 @@ int mcke_sm100_ipc_buffer_close(void* dev_ptr, int opened);
  * manager owns every device allocation, or a foreign-language binding that
  * holds only its own input and output buffers -- and so cannot pass a
  * workspace.  Same result as mcke_sm100_reduce_full_f32; allocates nothing.
- * Its scratch is a fixed 28,416-byte array (1184 partials of 24 bytes) inside
- * the library, which every GPU that loads the library keeps until the process
- * exits; a request needing more partials than that is rejected with
- * MCKE_INVALID_ARGUMENT (the kernel's grid never needs more, so every n fits).
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture.  All calls share the one array: calls that overlap on the
+ * Its scratch is a fixed 10,656-byte array (444 partials of 24 bytes, one per
+ * block of the kernel's largest grid) inside the library, which every GPU that
+ * loads the library keeps until the process exits; a request needing more
+ * partials than that is rejected with MCKE_INVALID_ARGUMENT (the grid never
+ * needs more, so every n fits).  The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress) with that device current and
+ * keeps it for the life of the process; make that first call before any stream
+ * capture, and do not call this entry point on a device after resetting it
+ * (cudaDeviceReset), which leaves the kept address stale.  All calls share the one array: calls that overlap on the
  * GPU (other streams, other host threads) race and must be serialised by the
  * caller.  Nothing in the array needs to start at zero. */
 int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mcke_reduce_result* out,

@@ -123,9 +123,14 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "check_device_errors: %s", cudaGetErrorString(e));
   uint32_t site = 0;
   MCKE_RETURN_IF(read_tc_watchdog(&site));
-  if (site != 0)
-    return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u); the kernel stopped early",
-                site);
+  if (site == 9) return fail(MCKE_INTERNAL, "watchdog self-test: its bounded wait expired as intended (site 9)");
+  if (site != 0) {
+    static const char* const kWhere[] = {"", "producer: free stage", "mma: loaded stage", "mma: free accumulator",
+                                         "epilogue: full accumulator", "drain", "split-k: previous contributor's flag",
+                                         "epilogue warps' meeting"};
+    return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u, %s); the kernel stopped early",
+                site, site < 8 ? kWhere[site] : "unknown");
+  }
   MCKE_RETURN_IF(read_reduce_watchdog(&site));
   if (site == 2)
     return fail(MCKE_INTERNAL, "reduce (p2p exchange): a peer's partial did not arrive within 1 s; the result is incomplete");

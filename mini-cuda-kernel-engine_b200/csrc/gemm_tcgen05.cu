@@ -123,7 +123,9 @@ enum : uint32_t {
   kSiteMmaEmpty = 3,
   kSiteEpilogue = 4,
   kSiteDrain = 5,
-  kSiteSplitFlag = 6
+  kSiteSplitFlag = 6,  // a split-k tile's flag from the previous contributor
+  kSiteEpiMeet = 7,    // the epilogue warps' meeting on their mbarrier
+  kSiteSelfTest = 9    // mcke_sm100_watchdog_selftest only
 };
 
 __device__ uint32_t g_tc_watchdog;
@@ -810,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(epi_bar);
-        wait_bounded(epi_bar, epi_uses & 1u, abort_flag, kSiteSplitFlag, false);
+        wait_bounded(epi_bar, epi_uses & 1u, abort_flag, kSiteEpiMeet, false);
       }
       __syncwarp();
       ++epi_uses;
@@ -1409,7 +1411,6 @@ int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int6
 // The bounded wait gives up after its limit, records kSiteSelfTest and the
 // kernel returns normally, so the context stays usable.
 namespace {
-constexpr uint32_t kSiteSelfTest = 6;
 __global__ void watchdog_selftest_kernel() {
   __shared__ uint64_t bar;
   __shared__ uint32_t abort_word;

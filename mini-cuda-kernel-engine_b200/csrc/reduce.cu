@@ -684,19 +684,23 @@ extern "C" int mcke_sm100_reduce_row_f32(const float* x, float* out, int64_t row
 // memory instead.  The array lives in this library's module: every GPU that
 // loads the library holds these bytes until the process exits.
 //
-// Capacity: one partial per pass-1 block, and the pass-1 grid never exceeds
-// kMaxBlocks (1184) blocks, so the array is 1184 x 24 = 28,416 bytes and every
-// n fits.  The capacity check below still rejects any request that would need
-// more, with a clear error, should the grid cap ever grow past the array.
+// Capacity: one partial per pass-1 block, and full_blocks() caps the pass-1
+// grid at kFullCtaCap (444) blocks, so the array is 444 x 24 = 10,656 bytes and
+// every n fits.  The capacity check below still rejects, with a clear error,
+// any request that would need more, should the grid cap ever grow past the array.
 namespace mcke_sm100 {
 namespace {
 
-constexpr int64_t kStaticParts = kMaxBlocks;
+constexpr int64_t kStaticParts = kFullCtaCap;
+static_assert(kFullCtaCap <= kStaticParts, "the built-in scratch must hold one partial per pass-1 block");
 static __device__ __align__(256) Part g_static_parts[kStaticParts];
 
 // Device address of g_static_parts for each device, looked up once per device
 // with that device current (the host-side name is only a stand-in; a kernel
-// must be handed the device address).
+// must be handed the device address).  The address belongs to the device's
+// primary context: after cudaDeviceReset() (or any reset of that context) the
+// library module is loaded again and the cached address is stale, so a process
+// that resets a device must not call this entry point on it afterwards.
 std::mutex g_static_mu;
 void* g_static_addr[64] = {};
 

@@ -110,7 +110,9 @@ def make_ref_fixtures() -> dict[str, np.ndarray]:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get(
+        "MCKE_REFERENCE_TREE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "..", "reference")),
+        help="the reference source tree (default: MCKE_REFERENCE_TREE, else `reference` beside this repository)")
     args = ap.parse_args()
     src = os.path.join(args.ref, "tests", "data", "reference_vectors.txt")
     cases = parse_vectors(src)

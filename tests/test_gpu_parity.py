@@ -563,7 +563,7 @@ def test_bounded_wait_expiry_is_reported_and_the_context_survives():
     assert mcke.lib().mcke_sm100_watchdog_selftest(s) == mcke.OK
     with pytest.raises(mcke.MckeError) as e:
         mcke.check_device_errors()
-    assert e.value.code == mcke.INTERNAL and "site 6" in e.value.message
+    assert e.value.code == mcke.INTERNAL and "site 9" in e.value.message and "self-test" in e.value.message
     mcke.check_device_errors()  # the word was cleared
     x = dev(oracle.fill_random(4096, 3))
     assert mcke.decode_result(mcke.reduce_full(x))[2] == int(np.argmax(host(x)))

@@ -17,7 +17,9 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "mini-cuda-kernel-engine_b200")
-REF = os.environ.get("MCKE_REFERENCE_TREE", "/root/reference")
+# the reference source tree: MCKE_REFERENCE_TREE, else a checkout named
+# `reference` beside this repository
+REF = os.environ.get("MCKE_REFERENCE_TREE", os.path.join(os.path.dirname(ROOT), "reference"))
 SHIM = os.path.join(PKG, "integration", "kernels_sm100.cpp")
 
 pytestmark = pytest.mark.skipif(not os.path.exists(os.path.join(REF, "include", "mcke", "kernels", "kernels.hpp")),

@@ -5,8 +5,10 @@ output buffers), so they cannot pass the workspace mcke_sm100_reduce_full_f32
 needs.  It keeps its scratch in a fixed array inside the library instead.
 
 Checked through the C-ABI against the existing entry point on the same inputs,
-on two calls in a row with different sizes (so the second call must not read
-anything the first left in the shared array).  Tolerances are those of
+on three calls in a row of falling sizes (pass-1 grids of 444, 50 and 1
+blocks).  The first input's unique maximum sits in a partial slot beyond the
+later calls' grids, so a combine that folded leftover slots from the shared
+array would report it.  Tolerances are those of
 tests/test_gpu_parity.py: max and argmax bit for bit, the double-accumulated
 sum within one float ulp.  This file sorts last so that a run stopping at the
 first failure has already run every other test.
@@ -46,8 +48,13 @@ def test_noalloc_matches_the_workspace_entry_point_on_two_calls_in_a_row():
     stream = torch.cuda.current_stream(dev).cuda_stream
     big = oracle.fill_random((1 << 22) + 3, 11)
     big[777] = big[3_000_001] = np.float32(1.25)  # tie: lowest index wins
+    # Thread t of pass-1 block j reads float4 j * 256 + t first, so element
+    # 4 * (100 * 256 + 5) lands in partial slot 100: left in the array by this
+    # call, never written by the next two (50 blocks, then 1 block).
+    big[4 * (100 * 256 + 5)] = np.float32(7.0)
+    middle = oracle.fill_random(50 * 4096, 13)  # 50 blocks of 4096 floats
     small = oracle.fill_random(1000, 12)
-    for host in (big, small):
+    for host in (big, middle, small):
         x = torch.from_numpy(host).to(dev)
         out = torch.zeros(16, dtype=torch.uint8, device=dev)
         rc = fn(x.data_ptr(), x.numel(), out.data_ptr(), stream)
@@ -58,6 +65,7 @@ def test_noalloc_matches_the_workspace_entry_point_on_two_calls_in_a_row():
         assert np.float32(m).view(np.uint32) == np.float32(wm).view(np.uint32)
         assert i == wi
         assert abs(s - ws) <= np.spacing(np.float32(abs(ws)))
+        assert i == int(np.argmax(host)) and m == host.max()
     assert mcke.decode_result(out)[2] == int(np.argmax(small))
 
 

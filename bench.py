@@ -206,73 +206,330 @@ def timed_steps(torch, dist, launch, steps: int, warmup: int, flush=None, per_la
     return dist.max(torch, sum(per)), per
 
 
+# ------------------------------------------------------------ CPU baselines
+#
+# The reference's own CPU implementation of each op (tests/reference.hpp,
+# compiled into oracle/_ref; the C restatement in oracle/ if that library is
+# absent) timed on this host's cores.  Each op's function runs on disjoint row
+# (or range) blocks, one block per thread, into preallocated outputs; one
+# untimed pass comes first (page faults, caches, the thread pool), then passes
+# until a time budget is spent.  The same code serves the cpu_baseline entries
+# of this arm and the whole --impl reference arm, so the two agree.  Inputs
+# are synthetic with each config's shapes (values do not change the timing);
+# GEMM-shaped work is timed on a row slice and extrapolated linearly.
+
+class CpuBaselines:
+    def __init__(self, budget_s: float = 2.0):
+        from concurrent.futures import ThreadPoolExecutor
+        import oracle
+        self.oracle = oracle
+        self.impl = "reference" if oracle.have_reference() else "port"
+        self.threads = max(1, min(os.cpu_count() or 1, 64))
+        self.budget = budget_s
+        self.pool = ThreadPoolExecutor(max_workers=self.threads)
+        self.rng = np.random.default_rng(1234)
+
+    def close(self):
+        self.pool.shutdown()
+
+    def _blocks(self, n: int) -> list[tuple[int, int]]:
+        step = -(-n // self.threads)
+        return [(i, min(n, i + step)) for i in range(0, n, step)]
+
+    def _time(self, work, items) -> tuple[float, int]:
+        list(self.pool.map(work, items))  # untimed first pass
+        reps, total = 0, 0.0
+        while reps < 2 or (total < self.budget and reps < 50):
+            t0 = time.perf_counter()
+            list(self.pool.map(work, items))
+            total += time.perf_counter() - t0
+            reps += 1
+        return total / reps, reps
+
+    def _entry(self, value: float, unit: str, sample: str) -> dict:
+        return {"value": round(value, 4 if value < 10 else 2), "unit": unit, "cores": self.threads,
+                "kind": self.impl, "sample": sample}
+
+    def _uniform(self, *shape) -> np.ndarray:
+        return self.rng.random(shape, dtype=np.float32) * np.float32(2) - np.float32(1)
+
+    def softmax(self, rows: int = ROWS, cols: int = COLS) -> dict:
+        o = self.oracle
+        x = o.softmax_config_input(rows, cols, seed=2)
+        y = np.empty_like(x)
+        sec, reps = self._time(lambda b: o.row_softmax(x[b[0]:b[1]], self.impl, out=y[b[0]:b[1]]),
+                               self._blocks(rows))
+        return self._entry(2 * rows * cols * 4 / sec / 1e9, "GB/s",
+                           f"full {rows}x{cols} batch per pass, {reps} timed passes; reference_row_softmax "
+                           f"(tests/reference.hpp:175) over disjoint row blocks on {self.threads} threads")
+
+    def bias_gelu(self) -> dict:
+        o = self.oracle
+        x = o.fill_normal(BIAS_ROWS * BIAS_COLS, 0).reshape(BIAS_ROWS, BIAS_COLS)
+        b = o.fill_random(BIAS_COLS, 1000)
+        y = np.empty_like(x)
+        sec, reps = self._time(lambda r: o.bias_act(x[r[0]:r[1]], b, "gelu_tanh", self.impl, out=y[r[0]:r[1]]),
+                               self._blocks(BIAS_ROWS))
+        return self._entry(BIAS_BYTES / sec / 1e9, "GB/s",
+                           f"full {BIAS_ROWS}x{BIAS_COLS} batch per pass, {reps} timed passes; reference_bias_act "
+                           f"(tests/reference.hpp:143) over disjoint row blocks on {self.threads} threads")
+
+    def reduce_full(self) -> dict:
+        # sum and max: reference_row_reduce with rows = 1 on each thread's
+        # contiguous range (two passes, as two of the reference's ReduceOp
+        # nodes would run); the reference has no argmax, so none is timed
+        o = self.oracle
+        n = 1 << 26
+        x = self._uniform(n)
+        outs = np.empty((self.threads, 2), np.float32)
+        blocks = list(enumerate(self._blocks(n)))
+
+        def work(item):
+            i, (lo, hi) = item
+            seg = x[lo:hi].reshape(1, hi - lo)
+            o.row_reduce(seg, "sum", self.impl, out=outs[i, 0:1])
+            o.row_reduce(seg, "max", self.impl, out=outs[i, 1:2])
+
+        sec, reps = self._time(work, blocks)
+        return self._entry(n * 4 / sec / 1e9, "GB/s",
+                           f"2^26 of config 3's 2^28 floats per pass, {reps} timed passes; reference_row_reduce "
+                           f"(tests/reference.hpp:154, rows = 1) for sum and for max over contiguous ranges on "
+                           f"{self.threads} threads (no argmax: the reference has none)")
+
+    def row_reduce(self) -> dict:
+        o = self.oracle
+        x = self._uniform(ROWS, COLS)
+        y = np.empty(ROWS, np.float32)
+        sec, reps = self._time(lambda r: o.row_reduce(x[r[0]:r[1]], "sum", self.impl, out=y[r[0]:r[1]]),
+                               self._blocks(ROWS))
+        return self._entry((ROWS * COLS * 4 + ROWS * 4) / sec / 1e9, "GB/s",
+                           f"full {ROWS}x{COLS} batch per pass, {reps} timed passes; reference_row_reduce sum "
+                           f"(tests/reference.hpp:154) over disjoint row blocks on {self.threads} threads")
+
+    def gemm(self) -> dict:
+        # one row of C per thread: reference_gemm's i-j-k loop with double
+        # accumulation (tests/reference.hpp:199); the bf16 path's oracle is the
+        # same loop on bf16-rounded inputs, so the one figure serves both
+        o = self.oracle
+        rows = self.threads
+        a = self._uniform(rows, GEMM_N)
+        b = self._uniform(GEMM_N, GEMM_N)
+        c = np.zeros((rows, GEMM_N), np.float32)
+        sec, reps = self._time(lambda i: o.gemm(a[i:i + 1], b, impl=self.impl, out=c[i:i + 1]), range(rows))
+        return self._entry(2 * rows * GEMM_N * GEMM_N / sec / 1e12, "TFLOP/s",
+                           f"{rows} of 8192 rows of C per pass ({reps} timed passes), extrapolated linearly to "
+                           f"8192^3; reference_gemm on {self.threads} threads, one row each")
+
+    def dag_branch(self) -> dict:
+        # one config-5 branch, one token row per thread: GEMM1 -> +b1, GELU ->
+        # GEMM2 -> +b2 -> softmax with the reference's functions (fp32: the
+        # reference has no bf16), extrapolated to 8192 rows x 4 branches
+        o = self.oracle
+        d, f = 4096, 16384
+        rows = self.threads
+        x = self._uniform(rows, d)
+        w1, w2 = self._uniform(d, f) * np.float32(0.02), self._uniform(f, d) * np.float32(0.02)
+        b1, b2 = self._uniform(f), self._uniform(d)
+        lin1, h = np.zeros((rows, f), np.float32), np.zeros((rows, f), np.float32)
+        lin2, y, p = (np.zeros((rows, d), np.float32) for _ in range(3))
+
+        def work(i):
+            s = slice(i, i + 1)
+            o.gemm(x[s], w1, impl=self.impl, out=lin1[s])
+            o.bias_act(lin1[s], b1, "gelu_tanh", self.impl, out=h[s])
+            o.gemm(h[s], w2, impl=self.impl, out=lin2[s])
+            o.bias_act(lin2[s], b2, "none", self.impl, out=y[s])
+            o.row_softmax(y[s], self.impl, out=p[s])
+
+        sec, reps = self._time(work, range(rows))
+        return self._entry(2 * 2 * rows * d * f / sec / 1e12, "TFLOP/s",
+                           f"{rows} of 8192 token rows of one branch per pass ({reps} timed passes), extrapolated "
+                           f"linearly to 8192 rows x 4 branches; reference_gemm / reference_bias_act / "
+                           f"reference_row_softmax on {self.threads} threads, one row each")
+
+    def dag_fanout(self) -> dict:
+        o = self.oracle
+        fb, fd, fr, fc = 4, 4, 2048, 2048
+        x = self._uniform(fr, fc)
+        bias = [self._uniform(fc) for _ in range(fb * fd)]
+        hs = [np.empty((fr, fc), np.float32) for _ in range(2)]
+
+        def work(r):
+            for bi in range(fb):
+                src = x
+                for k in range(fd):
+                    dst = hs[k & 1]
+                    o.bias_act(src[r[0]:r[1]], bias[bi * fd + k], "gelu_tanh", self.impl, out=dst[r[0]:r[1]])
+                    src = dst
+
+        sec, reps = self._time(work, self._blocks(fr))
+        return self._entry(fb * fd * (2 * fr * fc + fc) * 4 / sec / 1e9, "GB/s",
+                           f"all 16 bias+GELU nodes per pass, {reps} timed passes; reference_bias_act over "
+                           f"disjoint row blocks on {self.threads} threads")
+
+
+# keys of the ops entries -> the CpuBaselines method that times the same work
+CPU_FOR_OP = {
+    "bias_gelu_fp32_4096x4096": "bias_gelu",
+    "reduce_full_fp32_2^28": "reduce_full",
+    "row_reduce_sum_fp32_32768x1024": "row_reduce",
+    "gemm_bf16_8192^3": "gemm",
+    "gemm_f32_8192^3": "gemm",
+    "dag_fused_config5": "dag_branch",
+    "dag_unfused_config5": "dag_branch",
+    "dag_fanout_4x4_2048x2048_f32": "dag_fanout",
+}
+
+
+def attach_cpu_baselines(ops: dict, cpu: CpuBaselines) -> None:
+    memo: dict[str, dict] = {}
+    for key, entry in ops.items():
+        meth = CPU_FOR_OP.get(key)
+        if meth is None or not isinstance(entry, dict):
+            continue
+        if meth not in memo:
+            memo[meth] = getattr(cpu, meth)()
+        entry["cpu_baseline"] = memo[meth]
+
+
+def headline_config(g: int) -> dict:
+    return {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows_per_gpu": ROWS,
+            "cols": COLS, "l2": "flushed between timed steps (256 MiB write, then 256 MiB read)",
+            "parallelism": f"rows, weak scaling, {g} x full batch"}
+
+
 # ------------------------------------------------------------ reference arm
 
 def run_reference(args, dist) -> None:
+    """The reference's CPU implementation of the path on this host's cores,
+    on the GPU arm's config, metric and unit: a step is one row softmax pass
+    over the full config-2 batch.  The ops get the same CPU figures as the
+    GPU arm's cpu_baseline entries."""
     if dist.rank != 0:
         return
-    import oracle
-    impl = "reference" if oracle.have_reference() else "port"
-    threads = max(1, min(os.cpu_count() or 1, 64))
-    rows_per_step = ROWS  # full batch per step; a step takes ~1 s of CPU work per thread-second budget
-    x = oracle.softmax_config_input(ROWS, COLS, seed=2)
+    cpu = CpuBaselines(budget_s=0.0)
+    o = cpu.oracle
+    x = o.softmax_config_input(ROWS, COLS, seed=2)
     y = np.empty_like(x)
+    blocks = cpu._blocks(ROWS)
 
     def step():
-        oracle.parallel_rows(lambda xs, ys: ys.__setitem__(slice(None), oracle.row_softmax(xs, impl=impl)),
-                             x[:rows_per_step], y[:rows_per_step], threads)
+        list(cpu.pool.map(lambda b: o.row_softmax(x[b[0]:b[1]], cpu.impl, out=y[b[0]:b[1]]), blocks))
 
-    t0 = time.perf_counter()
-    step()
-    one = time.perf_counter() - t0
-    # keep the whole --steps/--warmup run within ~2 minutes
-    budget = 120.0
-    if one * (args.steps + args.warmup) > budget:
-        rows_per_step = max(64, int(ROWS * budget / (one * (args.steps + args.warmup))) // 64 * 64)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = time.perf_counter() - t0
-    bytes_per_step = 2 * rows_per_step * COLS * 4
-    value = bytes_per_step * args.steps / dt / 1e9
+    value = SOFTMAX_BYTES * args.steps / dt / 1e9
+    ops = {}
+    if args.ops:
+        cpu.budget = 2.0
+        for key, meth in CPU_FOR_OP.items():
+            if any(w in key for w in args.ops.split(",")):
+                ops[key] = {"cpu_baseline": getattr(cpu, meth)()}
+    cpu.close()
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows": ROWS, "cols": COLS,
-                   "rows_per_step": rows_per_step},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "reference" if impl == "reference" else "port",
-                         "sample": f"{rows_per_step} of {ROWS} rows x {COLS} per step, tests/reference.hpp "
-                                   f"reference_row_softmax on {threads} host threads over disjoint row blocks"},
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (N(0, 4^2) logits, every 64th row +80)",
+        "config": headline_config(args.gpus),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cpu.threads, "kind": cpu.impl,
+                         "sample": f"full {ROWS}x{COLS} batch per step; tests/reference.hpp reference_row_softmax "
+                                   f"on {cpu.threads} host threads over disjoint row blocks"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "ops": ops,
     }
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- output checks
+#
+# After each op's timed loop its last output is checked on sampled rows or
+# elements against a float64 recomputation on the device (torch, used only as
+# the checker): the reference's spot-check idea (tests/reference.hpp:401) with
+# the tolerances of the parity tests.  The full parity gate is tests/; this
+# records in the JSON line that the timed output itself is right.
+
+def _gelu_tanh64(v):
+    return 0.5 * v * (1.0 + (0.7978845608028654 * (v + 0.044715 * v * v * v)).tanh())
+
+
+def check_softmax(torch, x, y, rows: int = 64) -> bool:
+    n = x.shape[0]
+    idx = torch.unique(torch.cat([torch.arange(0, n, max(1, n // rows)), torch.arange(0, min(n, 64 * 8), 64)])).to(x.device)
+    ref = torch.softmax(x[idx].double(), dim=1)
+    return bool(((y[idx].double() - ref).abs() <= 1e-8 + 1e-5 * ref.abs()).all())
+
+
+def check_bias_gelu(torch, x, b, y, rows: int = 32) -> bool:
+    idx = torch.arange(0, x.shape[0], max(1, x.shape[0] // rows), device=x.device)
+    ref = _gelu_tanh64(x[idx].double() + b.double())
+    return bool(((y[idx].double() - ref).abs() <= 1e-6 + 1e-5 * ref.abs()).all())
+
+
+def check_row_reduce(torch, x, y, rows: int = 64) -> bool:
+    idx = torch.arange(0, x.shape[0], max(1, x.shape[0] // rows), device=x.device)
+    ref = x[idx].double().sum(dim=1)
+    ulp = torch.finfo(torch.float32).eps * ref.abs()
+    return bool(((y[idx].double() - ref).abs() <= ulp + 1e-30).all())
+
+
+def check_gemm(torch, a, b, c, samples: int = 256, rel: float = 1e-5, seed: int = 0) -> bool:
+    """c[i, j] against sum_k a[i, k] b[k, j] in float64, within `rel` of
+    sum_k |a[i, k] b[k, j]| (the scale of the fp32 accumulation error)."""
+    gen = torch.Generator(device=a.device)
+    gen.manual_seed(seed)
+    ii = torch.randint(0, a.shape[0], (samples,), generator=gen, device=a.device)
+    jj = torch.randint(0, b.shape[1], (samples,), generator=gen, device=a.device)
+    prod = a[ii].double() * b[:, jj].t().double()
+    ref, scale = prod.sum(dim=1), prod.abs().sum(dim=1)
+    got = c[ii, jj].double()
+    return bool(torch.isfinite(got).all() and ((got - ref).abs() <= rel * scale).all())
+
+
+def check_dag_branch(torch, dev, inputs, probs, fused: bool, rows: int = 4) -> bool:
+    """Branch 0 of the config-5 DAG on sampled token rows, recomputed in float64
+    on the device with H rounded to bf16 where the kernels store it (and, in the
+    unfused graph, GEMM1's output too): the softmax rows within 5e-3 relative
+    (a bf16 ulp of H moves the logits by ~1e-4) and summing to one."""
+    x, w1, b1, w2, b2 = inputs
+    idx = np.linspace(0, x.shape[0] - 1, rows).astype(np.int64)
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev).view(torch.bfloat16)  # noqa: E731
+    xs = bf(x[idx]).double()
+    lin1 = xs @ bf(w1).double()
+    if not fused:
+        lin1 = lin1.to(torch.bfloat16).double()
+    h = _gelu_tanh64(lin1 + torch.from_numpy(b1).to(dev).double()).to(torch.bfloat16).double()
+    y = h @ bf(w2).double() + torch.from_numpy(b2).to(dev).double()
+    ref = torch.softmax(y, dim=1)
+    got = torch.from_numpy(probs[idx]).to(dev).double()
+    sums = torch.from_numpy(probs.sum(axis=1, dtype=np.float64))
+    return bool(((got - ref).abs() <= 1e-9 + 5e-3 * ref.abs()).all() and (sums - 1.0).abs().max() < 1e-4)
+
+
+def check_reduce(torch, dist, x, index_base: int, res_bytes) -> bool:
+    """The combined {sum, max, argmax} against every rank's float64 sum, max and
+    first index of the max, gathered and folded in rank order."""
+    import mcke
+    s, m, i = mcke.decode_result(res_bytes)
+    local = torch.tensor([x.double().sum().item(), x.max().item(), float(int(x.argmax().item()) + index_base)],
+                         dtype=torch.float64, device=x.device)
+    if dist.pg is not None:
+        parts = [torch.empty_like(local) for _ in range(dist.world)]
+        dist.pg.all_gather(parts, local)
+    else:
+        parts = [local]
+    rows = [p.tolist() for p in parts]
+    ws = sum(r[0] for r in rows)
+    wm = max(r[1] for r in rows)
+    wi = int(min(r[2] for r in rows if r[1] == wm))
+    return bool(m == np.float32(wm) and i == wi and abs(s - np.float32(ws)) <= np.spacing(np.float32(abs(ws))))
+
+
 # ----------------------------------------------------------------- our arm
-
-def cpu_baseline_softmax() -> dict:
-    import oracle
-    impl = "reference" if oracle.have_reference() else "port"
-    threads = max(1, min(os.cpu_count() or 1, 64))
-    x = oracle.softmax_config_input(ROWS, COLS, seed=2)
-    y = np.empty_like(x)
-    fn = lambda xs, ys: ys.__setitem__(slice(None), oracle.row_softmax(xs, impl=impl))  # noqa: E731
-    reps, t_total = 0, 0.0
-    while reps < 3 or (t_total * threads < 10.0 and reps < 20):
-        t0 = time.perf_counter()
-        oracle.parallel_rows(fn, x, y, threads)
-        t_total += time.perf_counter() - t0
-        reps += 1
-    v = SOFTMAX_BYTES * reps / t_total / 1e9
-    return {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": impl,
-            "sample": f"full {ROWS}x{COLS} batch x {reps} passes on {threads} host threads "
-                      f"(reference_row_softmax over disjoint row blocks)"}
-
 
 def run_mcke(args, dist) -> None:
     import torch
@@ -309,6 +566,7 @@ def run_mcke(args, dist) -> None:
     result: dict = {}
     with ClockSampler(uuid) as clocks:
         total_ms, per = timed_steps(torch, dist, lambda: mcke.softmax(x, out=y), args.steps, args.warmup, flush)
+        headline_checked = check_softmax(torch, x, y)
         kernel_ms = statistics.mean(per)
         achieved = SOFTMAX_BYTES / (kernel_ms * 1e-3) / 1e9
         value = g * SOFTMAX_BYTES * args.steps / (total_ms * 1e-3) / 1e9
@@ -359,9 +617,7 @@ def run_mcke(args, dist) -> None:
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (torch.randn * 4 on device, seed 2 + rank; every 64th row +80)",
-        "config": {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows_per_gpu": ROWS,
-                   "cols": COLS, "l2": "flushed between timed steps (256 MiB write, then 256 MiB read)",
-                   "parallelism": f"rows, weak scaling, {g} x full batch"},
+        "config": headline_config(g),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs"),
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs",
@@ -372,13 +628,17 @@ def run_mcke(args, dist) -> None:
                 "path": "pinned host logits -> H2D -> mcke.softmax (C-ABI) -> D2H, 8 row chunks on 3 streams",
                 "pcie_ceiling_note": "H2D and D2H of 128 MiB each, concurrently: 2.715 ms (49.4 GB/s per direction) "
                                      "on this box, i.e. at most ~99 GB/s of this metric"},
+        "checked": headline_checked,
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
         "ops": ops,
     }
-    if dist.rank == 0 and g == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline_softmax()
     dist.close()
+    if dist.rank == 0 and g == 1 and not args.no_cpu_baseline:
+        cpu = CpuBaselines()
+        result["cpu_baseline"] = cpu.softmax()
+        attach_cpu_baselines(ops, cpu)
+        cpu.close()
     if dist.rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -441,13 +701,14 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         bb = torch.rand(BIAS_COLS, generator=gen, device=dev) * 2 - 1
         yb = torch.empty_like(xb)
         ms, per = timed_steps(torch, dist, lambda: mcke.bias_act(xb, bb, "gelu_tanh", out=yb), steps, warm, flush)
+        checked = check_bias_gelu(torch, xb, bb, yb)
         kms = statistics.mean(per)
         loc = (2 * (r1 - r0) * BIAS_COLS + BIAS_COLS) * 4
         ach = loc / (kms * 1e-3) / 1e9
         out["bias_gelu_fp32_4096x4096"] = {
             "value": round(BIAS_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "kernel_ms": round(kms, 5), "algorithmic_bytes": BIAS_BYTES,
+            "kernel_ms": round(kms, 5), "algorithmic_bytes": BIAS_BYTES, "checked": checked,
             "traffic": traffic.get("bias_act_f32_kernel")}
         del xb, yb
 
@@ -475,6 +736,8 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             p2p = mshard.P2PExchange(dev)
             launch = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
         ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
+        torch.cuda.synchronize()
+        checked = check_reduce(torch, dist, xr, r0, res.cpu().numpy().tobytes())
         kms = statistics.mean(per)
         ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9
         p2p_matches = None
@@ -493,7 +756,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "step_ms": round(kms, 5),
             "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
             "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
-            "p2p_result_matches_nccl": p2p_matches,
+            "p2p_result_matches_nccl": p2p_matches, "checked": checked,
             "traffic": traffic.get("reduce_full_stream_kernel")}
         del xr
 
@@ -506,13 +769,14 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         xr = torch.rand(r1 - r0, COLS, generator=gen, device=dev) * 2 - 1
         yr = torch.empty(r1 - r0, device=dev)
         ms, per = timed_steps(torch, dist, lambda: mcke.reduce_row(xr, "sum", out=yr), steps, warm, flush)
+        checked = check_row_reduce(torch, xr, yr)
         kms = statistics.mean(per)
         moved = ROWS * COLS * 4 + ROWS * 4
         ach = ((r1 - r0) * COLS * 4 + (r1 - r0) * 4) / (kms * 1e-3) / 1e9
         out["row_reduce_sum_fp32_32768x1024"] = {
             "value": round(moved * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "kernel_ms": round(kms, 5), "algorithmic_bytes": moved}
+            "kernel_ms": round(kms, 5), "algorithmic_bytes": moved, "checked": checked}
         del xr, yr
 
     if "gemm_bf16" in want:
@@ -525,13 +789,15 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
         ms, per = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c, variant="tcgen05"), steps, warm, flush)
         mcke.check_device_errors()
+        checked = check_gemm(torch, a, b, c, seed=r)
         kms = statistics.mean(per)
         loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
         ach = loc_flops / (kms * 1e-3) / 1e12
         out["gemm_bf16_8192^3"] = {
             "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_bf16_peak": round(ach / peaks["bf16_tflops"], 4),
-            "peak": peaks["bf16_tflops"], "kernel_ms": round(kms, 4), "parallelism": f"columns of B and C over {g}"}
+            "peak": peaks["bf16_tflops"], "kernel_ms": round(kms, 4), "parallelism": f"columns of B and C over {g}",
+            "checked": checked}
         del a, b, c
 
     for fused in (True, False):
@@ -548,6 +814,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         gr = mhost.Graph()
         x = gr.input("X", (rows, dm), "bf16")
         feeds = {x: bf(torch.randn(rows, dm, generator=cpu))}
+        probs = []
         for i in range(branches):
             w1 = gr.input(f"W1_{i}", (dm, fm), "bf16")
             b1 = gr.input(f"b1_{i}", (fm,), "f32")
@@ -564,7 +831,10 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                 h = gr.bias_act(gr.gemm(x, w1, out_dtype="bf16", name=f"gemm1_{i}"), b1, "gelu_tanh",
                                name=f"bias_gelu_{i}")
                 y = gr.bias_act(gr.gemm(h, w2, name=f"gemm2_{i}"), b2, "none", name=f"bias2_{i}")
-            gr.output(gr.softmax(y, name=f"softmax_{i}"))
+            probs.append(gr.softmax(y, name=f"softmax_{i}"))
+            gr.output(probs[-1])
+            if i == 0:
+                chk_in = (feeds[x], feeds[w1], feeds[b1], feeds[w2], feeds[b2])
         gr.finalize()
         # replayed as a CUDA graph: the device time then excludes the host's
         # enqueue of 12-20 nodes and their events
@@ -584,11 +854,14 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             tot += ex.last_run_ms()
         dist.barrier(torch)
         tot = dist.max(torch, tot)
+        checked = check_dag_branch(torch, dev, chk_in, ex.output(probs[0]), fused)
+        del chk_in
         flops = branches * 2 * 2 * rows_total * dm * fm
         out[key + "_config5"] = {
             "value": round(flops * ds / (tot * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "ms_per_run": round(tot / ds, 3), "branches": branches, "rows_per_gpu": rows,
             "frac_of_bf16_peak": round(flops / g / (tot / ds * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+            "checked": checked,
             "peak": peaks["bf16_tflops_sustained"], "peak_kind": "bf16_tflops_sustained (multi-kernel step)",
             "note": ("GEMM1 with fused bias+GELU (bf16 out) -> GEMM2 with fused +b2 -> softmax" if fused else
                      "GEMM1 -> bias+GELU -> GEMM2 -> +b2 -> softmax, one kernel each") +
@@ -608,13 +881,18 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             gr = mhost.Graph()
             x = gr.input("x", (fr, fc))
             feeds = {x: torch.randn(fr, fc, generator=cpu).numpy()}
+            chain, last = [], None
             for b in range(fb):
                 h = x
                 for k in range(fd):
                     bias = gr.input(f"b{b}_{k}", (fc,))
                     feeds[bias] = (torch.rand(fc, generator=cpu) * 2 - 1).numpy()
+                    if b == 0:
+                        chain.append(feeds[bias])
                     h = gr.bias_act(h, bias, "gelu_tanh", name=f"bias_gelu_{b}_{k}")
                 gr.output(h)
+                if b == 0:
+                    last = h
             gr.finalize()
             ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=(mode == "graph"))
             ex.plan()
@@ -637,8 +915,13 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                 ex.run()
             ex.synchronize()
             wall = (time.perf_counter() - t0) / runs * 1e3
+            ref = torch.from_numpy(feeds[x][::64]).to(dev).double()
+            for bias in chain:
+                ref = _gelu_tanh64(ref + torch.from_numpy(bias).to(dev).double())
+            got = torch.from_numpy(ex.output(last)[::64]).to(dev).double()
+            fan_checked = bool(((got - ref).abs() <= 1e-6 + 4e-5 * ref.abs()).all())
             dist.barrier(torch)
-            modes[mode] = {"device_ms_per_run": round(dist.max(torch, dev_ms / runs), 4),
+            modes[mode] = {"checked": fan_checked, "device_ms_per_run": round(dist.max(torch, dev_ms / runs), 4),
                            "host_enqueue_us_per_run": round(enq / runs * 1e6, 1),
                            "back_to_back_ms_per_run": round(dist.max(torch, wall), 4)}
             del ex, gr
@@ -646,6 +929,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         gms = modes["graph"]["device_ms_per_run"]
         out["dag_fanout_4x4_2048x2048_f32"] = {
             "value": round(moved * g / (gms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "weak",
+            "checked": modes["eager"]["checked"] and modes["graph"]["checked"],
             "algorithmic_bytes_per_gpu": moved, "eager": modes["eager"], "graph": modes["graph"],
             "note": "16 bias+GELU nodes on 4 streams of the C++ GraphExecutor; value from the CUDA-graph replay's "
                     "device time (events around each launch, max over ranks); back_to_back is host wall clock"}
@@ -662,6 +946,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
         ws = torch.empty(mcke.gemm_f32_tc_workspace_bytes(GEMM_N, n1 - n0, GEMM_N), dtype=torch.uint8, device=dev)
         ms, per = timed_steps(torch, dist, lambda: mcke.gemm_f32_tc(a, b, c, workspace=ws), steps, warm, None)
+        checked = check_gemm(torch, a, b, c, rel=1e-6, seed=r)
         kms = statistics.mean(per)
         loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
         ach = loc_flops / (kms * 1e-3) / 1e12
@@ -681,7 +966,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         cublas_tf32 = loc_flops * fs / (ms_ct * 1e-3) / 1e12
         out["gemm_f32_8192^3"] = {
             "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
-            "per_gpu_achieved": round(ach, 1), "kernel_ms": round(kms, 3),
+            "per_gpu_achieved": round(ach, 1), "kernel_ms": round(kms, 3), "checked": checked,
             "path": "3xTF32 on tcgen05 (split pass + kind::tf32 MMAs, fp32 partial sums promoted every 128 k)",
             "tf32_mma_tflops": round(3 * ach, 1),
             "frac_of_tf32_nominal": round(3 * ach / TF32_NOMINAL_TFLOPS, 4),

@@ -141,44 +141,58 @@ def gelu_erf(x: float, impl: str = "port") -> float:
     return _fn(impl, "gelu_erf")(x)
 
 
-def bias_act(x, bias, act: str | int = "gelu_tanh", impl: str = "port"):
+def _into(out, shape) -> np.ndarray:
+    """`out` if given (C-contiguous float32 of `shape`, written in place), else a new array."""
+    if out is None:
+        return np.empty(shape, dtype=np.float32)
+    assert out.dtype == np.float32 and out.flags.c_contiguous and out.shape == tuple(shape)
+    return out
+
+
+def bias_act(x, bias, act: str | int = "gelu_tanh", impl: str = "port", out=None):
     """tests/reference.hpp:143 -- y = act(x + bias[col]) in double, stored float."""
     x = _f32(x)
     bias = _f32(bias)
     rows, cols = x.shape
-    y = np.empty_like(x)
+    y = _into(out, x.shape)
     a = ACT[act] if isinstance(act, str) else int(act)
     _fn(impl, "bias_act")(_p(x), _p(bias), _p(y), rows, cols, a)
     return y
 
 
-def row_reduce(x, kind: str | int = "sum", impl: str = "port"):
+def row_reduce(x, kind: str | int = "sum", impl: str = "port", out=None):
     """tests/reference.hpp:154 -- per-row sum/max/mean in double, stored float."""
     x = _f32(x)
     rows, cols = x.shape
-    out = np.empty(rows, dtype=np.float32)
+    out = _into(out, (rows,))
     k = REDUCE[kind] if isinstance(kind, str) else int(kind)
     _fn(impl, "row_reduce")(_p(x), _p(out), rows, cols, k)
     return out
 
 
-def row_softmax(x, impl: str = "port"):
+def row_softmax(x, impl: str = "port", out=None):
     """tests/reference.hpp:175 -- max-subtracted softmax over the last dim."""
     x = _f32(x)
     rows, cols = x.shape
-    y = np.empty_like(x)
+    y = _into(out, x.shape)
     _fn(impl, "row_softmax")(_p(x), _p(y), rows, cols)
     return y
 
 
-def gemm(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, impl: str = "port"):
-    """tests/reference.hpp:199 -- C = alpha*A@B + beta*C with double accumulation."""
+def gemm(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, impl: str = "port", out=None):
+    """tests/reference.hpp:199 -- C = alpha*A@B + beta*C with double accumulation.
+    With `out` (and no `c`) the product is written into `out`, whose current
+    contents play C's role (the reference reads C even when beta is 0)."""
     a = _f32(a)
     b = _f32(b)
     m, k = a.shape
     k2, n = b.shape
     assert k == k2
-    out = np.zeros((m, n), dtype=np.float32) if c is None else _f32(c).copy()
+    if out is not None:
+        assert c is None
+        out = _into(out, (m, n))
+    else:
+        out = np.zeros((m, n), dtype=np.float32) if c is None else _f32(c).copy()
     _fn(impl, "gemm")(_p(a), _p(b), _p(out), m, n, k, alpha, beta)
     return out
 

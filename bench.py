@@ -10,10 +10,12 @@ Headline (``value``): BASELINE config 2, row softmax fp32 over logits
 [32768 x 1024] ~ N(0, 4^2) with every 64th row shifted by +80.  A step is one
 softmax pass over the whole batch, inputs already resident in HBM.  Bytes per
 step are algorithmic, 2 * 32768 * 1024 * 4 = 268,435,456 (one read of x, one
-write of y).  L2 is flushed (a 256 MiB write, then a 256 MiB read, so no dirty lines
-are left to write back) between timed steps, outside the timed region; each step is timed with CUDA events on the launching stream.
-At N GPUs every rank processes its own full batch (weak scaling) and
-``value`` = N * bytes / (max over ranks of the summed step time).
+write of y).  The K timed steps run back to back between one pair of CUDA
+events on the launching stream, on inputs larger than L2 that rotate over
+three buffer sets; ``cold_step_ms`` beside it is one step timed alone after an
+L2 flush (a 256 MiB write, then a 256 MiB read), which also carries the
+event's own cost.  At N GPUs every rank processes its own full batch (weak
+scaling) and ``value`` = N * bytes * K / (max over ranks of the timed span).
 
 ``e2e``: the same step through the public API with HOST buffers: the pinned
 host logits are copied in, softmax runs, the probabilities are copied back,
@@ -206,6 +208,43 @@ def timed_steps(torch, dist, launch, steps: int, warmup: int, flush=None, per_la
     return dist.max(torch, sum(per)), per
 
 
+def timed_back_to_back(torch, dist, launch, steps: int, warmup: int) -> float:
+    """`warmup` untimed steps, then EXACTLY `steps` steps launched back to back
+    between one pair of CUDA events on the current stream, with a barrier and a
+    synchronize on both sides; launch(i) runs step i.  Returns the total device
+    time in ms, max over ranks.  Recording an event before every kernel costs
+    the next kernel ~4 us of device time on B200 (an empty kernel measured 6.1 us
+    between events, 2.2 us per launch back to back), so memory-bound steps of a
+    few tens of microseconds are timed this way, on inputs larger than L2."""
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        launch(warmup + i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier(torch)
+    torch.cuda.synchronize()
+    return dist.max(torch, e0.elapsed_time(e1))
+
+
+def cold_step_ms(torch, dist, launch, flush, steps: int = 5) -> float:
+    """Mean time of one step with L2 flushed first and events around the step
+    alone (launch latency and the event cost included), max over ranks."""
+    total, _ = timed_steps(torch, dist, launch, steps, 2, flush)
+    return total / steps
+
+
+# Inputs rotate over this many buffer sets in the back-to-back timing, so a
+# step's input was last touched ROTATE - 1 steps (>= 256 MiB of traffic) earlier.
+ROTATE = 3
+
+
 # ------------------------------------------------------------ CPU baselines
 #
 # The reference's own CPU implementation of each op (tests/reference.hpp,
@@ -394,7 +433,10 @@ def attach_cpu_baselines(ops: dict, cpu: CpuBaselines) -> None:
 
 def headline_config(g: int) -> dict:
     return {"workload": "row_softmax_fp32_32768x1024 (BASELINE config 2)", "rows_per_gpu": ROWS,
-            "cols": COLS, "l2": "flushed between timed steps (256 MiB write, then 256 MiB read)",
+            "cols": COLS, "l2": (f"inputs larger than L2: steps run back to back between one event pair, the "
+                                 f"128 MiB input and output rotating over {ROTATE} buffer sets (a step's buffers were "
+                                 f"last touched {ROTATE - 1} steps earlier); cold_step_ms: L2 flushed before one step "
+                                 f"timed alone"),
             "parallelism": f"rows, weak scaling, {g} x full batch"}
 
 
@@ -559,17 +601,25 @@ def run_mcke(args, dist) -> None:
 
     gen = torch.Generator(device=dev)
     gen.manual_seed(2 + dist.rank)
-    x = torch.randn(ROWS, COLS, generator=gen, device=dev) * 4.0
-    x[::64] += 80.0
-    y = torch.empty_like(x)
+    xs, ys = [], []
+    for _ in range(ROTATE):
+        xr = torch.randn(ROWS, COLS, generator=gen, device=dev) * 4.0
+        xr[::64] += 80.0
+        xs.append(xr)
+        ys.append(torch.empty_like(xr))
+    x, y = xs[0], ys[0]
 
     result: dict = {}
     with ClockSampler(uuid) as clocks:
-        total_ms, per = timed_steps(torch, dist, lambda: mcke.softmax(x, out=y), args.steps, args.warmup, flush)
-        headline_checked = check_softmax(torch, x, y)
-        kernel_ms = statistics.mean(per)
+        total_ms = timed_back_to_back(torch, dist, lambda i: mcke.softmax(xs[i % ROTATE], out=ys[i % ROTATE]),
+                                      args.steps, args.warmup)
+        last = (args.warmup + args.steps - 1) % ROTATE
+        headline_checked = check_softmax(torch, xs[last], ys[last])
+        kernel_ms = total_ms / args.steps
         achieved = SOFTMAX_BYTES / (kernel_ms * 1e-3) / 1e9
         value = g * SOFTMAX_BYTES * args.steps / (total_ms * 1e-3) / 1e9
+        cold_ms = cold_step_ms(torch, dist, lambda: mcke.softmax(x, out=y), flush)
+        del xs[1:], ys[1:]
 
         # e2e: host buffers, H2D + kernel + D2H inside the timed region.  The
         # batch moves in 8 row chunks over three streams so the copy in of
@@ -622,7 +672,8 @@ def run_mcke(args, dist) -> None:
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs",
                      "traffic": traffic.get("softmax_stream_row_kernel"),
-                     "algorithmic_bytes_per_launch": SOFTMAX_BYTES, "kernel_ms": round(kernel_ms, 5)},
+                     "algorithmic_bytes_per_launch": SOFTMAX_BYTES, "kernel_ms": round(kernel_ms, 5),
+                     "cold_step_ms": round(cold_ms, 5)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": SOFTMAX_BYTES // 2,
                 "d2h_bytes_per_step": SOFTMAX_BYTES // 2, "ms_per_step": round(e2e_ms / e2e_steps, 4),
                 "path": "pinned host logits -> H2D -> mcke.softmax (C-ABI) -> D2H, 8 row chunks on 3 streams",
@@ -697,18 +748,29 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         r0, r1 = shard(BIAS_ROWS)
         gen = torch.Generator(device=dev)
         gen.manual_seed(0)
-        xb = torch.randn(BIAS_ROWS, BIAS_COLS, generator=gen, device=dev)[r0:r1].contiguous()
+        xfull = torch.randn(BIAS_ROWS, BIAS_COLS, generator=gen, device=dev)
         bb = torch.rand(BIAS_COLS, generator=gen, device=dev) * 2 - 1
-        yb = torch.empty_like(xb)
-        ms, per = timed_steps(torch, dist, lambda: mcke.bias_act(xb, bb, "gelu_tanh", out=yb), steps, warm, flush)
-        checked = check_bias_gelu(torch, xb, bb, yb)
-        kms = statistics.mean(per)
+        # 64 MiB in and out per step, less than L2: rotate over enough sets that
+        # a step's buffers were last touched >= 384 MiB of traffic earlier
+        nrot = 4
+        xbs = [xfull[r0:r1].contiguous() for _ in range(nrot)]
+        ybs = [torch.empty_like(xbs[0]) for _ in range(nrot)]
+        del xfull
+        ms = timed_back_to_back(torch, dist, lambda i: mcke.bias_act(xbs[i % nrot], bb, "gelu_tanh", out=ybs[i % nrot]),
+                                steps, warm)
+        lastb = (warm + steps - 1) % nrot
+        checked = check_bias_gelu(torch, xbs[lastb], bb, ybs[lastb])
+        kms = ms / steps
+        xb, yb = xbs[0], ybs[0]
+        cold = cold_step_ms(torch, dist, lambda: mcke.bias_act(xb, bb, "gelu_tanh", out=yb), flush)
+        del xbs[1:], ybs[1:]
         loc = (2 * (r1 - r0) * BIAS_COLS + BIAS_COLS) * 4
         ach = loc / (kms * 1e-3) / 1e9
         out["bias_gelu_fp32_4096x4096"] = {
             "value": round(BIAS_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "kernel_ms": round(kms, 5), "algorithmic_bytes": BIAS_BYTES, "checked": checked,
+            "kernel_ms": round(kms, 5), "cold_step_ms": round(cold, 5), "algorithmic_bytes": BIAS_BYTES,
+            "checked": checked, "timing": f"back to back over {nrot} rotating buffer sets",
             "traffic": traffic.get("bias_act_f32_kernel")}
         del xb, yb
 
@@ -730,15 +792,16 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             def launch_nccl():
                 mcke.reduce_full_partial(xr, r0, out=part, workspace=ws)
                 mcke.reduce_combine(mshard.exchange_partials(part, g), g, out=res)
-            ms_n, _ = timed_steps(torch, dist, launch_nccl, steps, warm, flush)
+            ms_n = timed_back_to_back(torch, dist, lambda i: launch_nccl(), steps, warm)
             nccl_ms = ms_n / steps
             nccl_result = mcke.decode_result(res)
             p2p = mshard.P2PExchange(dev)
             launch = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
-        ms, per = timed_steps(torch, dist, launch, steps, warm, flush)
+        ms = timed_back_to_back(torch, dist, lambda i: launch(), steps, warm)
         torch.cuda.synchronize()
         checked = check_reduce(torch, dist, xr, r0, res.cpu().numpy().tobytes())
-        kms = statistics.mean(per)
+        kms = ms / steps
+        cold = cold_step_ms(torch, dist, launch, flush)
         ach = (r1 - r0) * 4 / (kms * 1e-3) / 1e9
         p2p_matches = None
         if p2p is not None:
@@ -753,7 +816,8 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         out["reduce_full_fp32_2^28"] = {
             "value": round(REDUCE_BYTES * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "step_ms": round(kms, 5),
+            "step_ms": round(kms, 5), "cold_step_ms": round(cold, 5),
+            "timing": "back to back (the 2^28 / N float input is >= 128 MiB per rank)",
             "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
             "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
             "p2p_result_matches_nccl": p2p_matches, "checked": checked,
@@ -766,17 +830,23 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         r0, r1 = shard(ROWS)
         gen = torch.Generator(device=dev)
         gen.manual_seed(3)
-        xr = torch.rand(r1 - r0, COLS, generator=gen, device=dev) * 2 - 1
-        yr = torch.empty(r1 - r0, device=dev)
-        ms, per = timed_steps(torch, dist, lambda: mcke.reduce_row(xr, "sum", out=yr), steps, warm, flush)
-        checked = check_row_reduce(torch, xr, yr)
-        kms = statistics.mean(per)
+        xrs = [torch.rand(r1 - r0, COLS, generator=gen, device=dev) * 2 - 1 for _ in range(ROTATE)]
+        yrs = [torch.empty(r1 - r0, device=dev) for _ in range(ROTATE)]
+        ms = timed_back_to_back(torch, dist, lambda i: mcke.reduce_row(xrs[i % ROTATE], "sum", out=yrs[i % ROTATE]),
+                                steps, warm)
+        lastb = (warm + steps - 1) % ROTATE
+        checked = check_row_reduce(torch, xrs[lastb], yrs[lastb])
+        kms = ms / steps
+        xr, yr = xrs[0], yrs[0]
+        cold = cold_step_ms(torch, dist, lambda: mcke.reduce_row(xr, "sum", out=yr), flush)
+        del xrs[1:], yrs[1:]
         moved = ROWS * COLS * 4 + ROWS * 4
         ach = ((r1 - r0) * COLS * 4 + (r1 - r0) * 4) / (kms * 1e-3) / 1e9
         out["row_reduce_sum_fp32_32768x1024"] = {
             "value": round(moved * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
-            "kernel_ms": round(kms, 5), "algorithmic_bytes": moved, "checked": checked}
+            "kernel_ms": round(kms, 5), "cold_step_ms": round(cold, 5), "algorithmic_bytes": moved,
+            "checked": checked, "timing": f"back to back over {ROTATE} rotating buffer sets"}
         del xr, yr
 
     if "gemm_bf16" in want:
@@ -787,10 +857,10 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         gen.manual_seed(3)
         b = ((torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1)[:, n0:n1]).to(torch.bfloat16).contiguous()
         c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
-        ms, per = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c, variant="tcgen05"), steps, warm, flush)
+        ms = timed_back_to_back(torch, dist, lambda i: mcke.gemm(a, b, c, variant="tcgen05"), steps, warm)
         mcke.check_device_errors()
         checked = check_gemm(torch, a, b, c, seed=r)
-        kms = statistics.mean(per)
+        kms = ms / steps
         loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
         ach = loc_flops / (kms * 1e-3) / 1e12
         out["gemm_bf16_8192^3"] = {
@@ -945,9 +1015,9 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         b = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1)[:, n0:n1].contiguous()
         c = torch.empty(GEMM_N, n1 - n0, dtype=torch.float32, device=dev)
         ws = torch.empty(mcke.gemm_f32_tc_workspace_bytes(GEMM_N, n1 - n0, GEMM_N), dtype=torch.uint8, device=dev)
-        ms, per = timed_steps(torch, dist, lambda: mcke.gemm_f32_tc(a, b, c, workspace=ws), steps, warm, None)
+        ms = timed_back_to_back(torch, dist, lambda i: mcke.gemm_f32_tc(a, b, c, workspace=ws), steps, warm)
         checked = check_gemm(torch, a, b, c, rel=1e-6, seed=r)
-        kms = statistics.mean(per)
+        kms = ms / steps
         loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
         ach = loc_flops / (kms * 1e-3) / 1e12
         fs = max(2, min(steps, 3))

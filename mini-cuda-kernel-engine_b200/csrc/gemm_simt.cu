@@ -37,6 +37,7 @@ template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_simt_kernel(const T* __restrict__ a, const T* __restrict__ b, void* __restrict__ c,
                      int64_t M, int64_t N, int64_t K, EpilogueParams ep) {
+  pdl_entry();
   __shared__ __align__(16) float As[2][BK][BM + APAD];
   __shared__ __align__(16) float Bs[2][BK][BN];
 
@@ -145,20 +146,17 @@ int launch_gemm_simt(const void* a, const void* b, void* c, int64_t m, int64_t n
   if (bf16_in) {
     if (kernel_out) *kernel_out = reinterpret_cast<const void*>(&gemm_simt_kernel<uint16_t, false>);
     if (m > 0 && n > 0)
-      gemm_simt_kernel<uint16_t, false><<<grid, kThreads, 0, s>>>(
-          static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b), c, m, n, k, ep);
+      launch_async(gemm_simt_kernel<uint16_t, false>, grid, kThreads, 0, s, static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b), c, m, n, k, ep);
   } else {
     const bool vec = (k % 4 == 0) && (n % 4 == 0) && aligned(a, 16) && aligned(b, 16);
     if (vec) {
       if (kernel_out) *kernel_out = reinterpret_cast<const void*>(&gemm_simt_kernel<float, true>);
       if (m > 0 && n > 0)
-        gemm_simt_kernel<float, true><<<grid, kThreads, 0, s>>>(
-            static_cast<const float*>(a), static_cast<const float*>(b), c, m, n, k, ep);
+        launch_async(gemm_simt_kernel<float, true>, grid, kThreads, 0, s, static_cast<const float*>(a), static_cast<const float*>(b), c, m, n, k, ep);
     } else {
       if (kernel_out) *kernel_out = reinterpret_cast<const void*>(&gemm_simt_kernel<float, false>);
       if (m > 0 && n > 0)
-        gemm_simt_kernel<float, false><<<grid, kThreads, 0, s>>>(
-            static_cast<const float*>(a), static_cast<const float*>(b), c, m, n, k, ep);
+        launch_async(gemm_simt_kernel<float, false>, grid, kThreads, 0, s, static_cast<const float*>(a), static_cast<const float*>(b), c, m, n, k, ep);
     }
   }
   return MCKE_OK;

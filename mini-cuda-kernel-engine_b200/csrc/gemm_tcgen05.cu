@@ -584,6 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
                         const __grid_constant__ CUtensorMap tmap_c, void* __restrict__ c, int M, int N, int K,
                         EpilogueParams ep, int fast, SplitK sk) {
+  pdl_entry();
   using C = Cfg<kPair, kTf32, kWide>;
   constexpr int BK = C::BK;
   constexpr int UMMA_K = C::UMMA_K;
@@ -1293,7 +1294,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   if (!pair) {
     int grid = sm_count();
     if (tiles < grid) grid = static_cast<int>(tiles);
-    kfn<<<grid, kThreads, smem, s>>>(ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast, sk);
+    launch_async(kfn, grid, kThreads, smem, s, ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast, sk);
     return MCKE_OK;
   }
   int pairs = max_pairs(kfn);
@@ -1302,17 +1303,19 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   }
   if (sk.w == 0 && tiles < pairs) pairs = static_cast<int>(tiles);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, ta, tb, talo, tblo, tc, c, mi, ni, ki, ep, fast, sk);
   if (e != cudaSuccess) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05 pair): launch failed: %s", cudaGetErrorString(e));
   return MCKE_OK;
@@ -1321,6 +1324,7 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
 // hi = x with the low 13 mantissa bits cleared (exact in tf32), lo = x - hi.
 __global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
                                                          float* __restrict__ lo, int64_t n) {
+  pdl_entry();
   const int64_t n4 = n / 4;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -1350,6 +1354,7 @@ __global__ void __launch_bounds__(256) split_tf32_transpose_kernel(const float* 
                                                                    float* __restrict__ hi_t,
                                                                    float* __restrict__ lo_t, int64_t k,
                                                                    int64_t n) {
+  pdl_entry();
   __shared__ float tile[32][33];
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 32, k0 = static_cast<int64_t>(blockIdx.y) * 32;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
@@ -1400,10 +1405,10 @@ int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int6
   float* bhi = reinterpret_cast<float*>(w + 2 * split_bytes(m * k));
   float* blo = reinterpret_cast<float*>(w + 2 * split_bytes(m * k) + split_bytes(k * n));
   const int grid = 4 * sm_count();
-  split_tf32_kernel<<<grid, 256, 0, s>>>(a, ahi, alo, m * k);
+  launch_async(split_tf32_kernel, grid, 256, 0, s, a, ahi, alo, m * k);
   const dim3 tgrid(static_cast<unsigned>((n + 31) / 32), static_cast<unsigned>((k + 31) / 32));
   if (tgrid.y > 65535u) return fail(MCKE_INVALID_ARGUMENT, "gemm (3xTF32): K too large for the transpose grid");
-  split_tf32_transpose_kernel<<<tgrid, 256, 0, s>>>(b, bhi, blo, k, n);
+  launch_async(split_tf32_transpose_kernel, tgrid, 256, 0, s, b, bhi, blo, k, n);
   return launch_tc<true>(ahi, bhi, alo, blo, c, m, n, k, ep, s, kernel_out, smem_out);
 }
 
@@ -1412,6 +1417,7 @@ int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int6
 // kernel returns normally, so the context stays usable.
 namespace {
 __global__ void watchdog_selftest_kernel() {
+  pdl_entry();
   __shared__ uint64_t bar;
   __shared__ uint32_t abort_word;
   if (threadIdx.x != 0) return;
@@ -1423,7 +1429,7 @@ __global__ void watchdog_selftest_kernel() {
 }  // namespace
 
 int launch_watchdog_selftest(cudaStream_t s) {
-  watchdog_selftest_kernel<<<1, 32, 0, s>>>();
+  launch_async(watchdog_selftest_kernel, 1, 32, 0, s);
   return MCKE_OK;
 }
 

@@ -27,6 +27,7 @@ constexpr int kChains = 8;
 template <bool kTriad>
 __global__ void __launch_bounds__(kThreads) stream_kernel(float* __restrict__ a, const float* __restrict__ b,
                                                           const float* __restrict__ c, float s, int64_t n4) {
+  pdl_entry();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   for (; i + stride < n4; i += 2 * stride) {
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(kThreads) stream_kernel(float* __restrict__ a,
 
 __global__ void __launch_bounds__(kThreads) fma_kernel(const float* __restrict__ seed, float* __restrict__ out,
                                                        int iters) {
+  pdl_entry();
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const float s0 = seed[t];
   float acc[kChains];
@@ -84,8 +86,8 @@ int stream_launch(bool triad, float* a, const float* b, const float* c, float s,
   int64_t grid = static_cast<int64_t>(sm_count()) * 4;
   const int64_t need = (n4 + kThreads - 1) / kThreads;
   if (need < grid) grid = need;
-  if (triad) stream_kernel<true><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a, b, c, s, n4);
-  else stream_kernel<false><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(a, b, nullptr, 0.f, n4);
+  if (triad) launch_async(stream_kernel<true>, static_cast<unsigned>(grid), kThreads, 0, st, a, b, c, s, n4);
+  else launch_async(stream_kernel<false>, static_cast<unsigned>(grid), kThreads, 0, st, a, b, nullptr, 0.f, n4);
   return check_launch(who);
 }
 
@@ -117,7 +119,6 @@ extern "C" int mcke_sm100_peak_fma_f32(const float* seed, float* out, int64_t th
   if (!seed || !out) return fail(MCKE_INVALID_ARGUMENT, "%s: null pointer", who);
   if (threads % kThreads != 0 || threads / kThreads > 2147483647LL)
     return fail(MCKE_INVALID_ARGUMENT, "%s: threads must be a multiple of %d", who, kThreads);
-  fma_kernel<<<static_cast<unsigned>(threads / kThreads), kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      seed, out, iters);
+  launch_async(fma_kernel, static_cast<unsigned>(threads / kThreads), kThreads, 0, reinterpret_cast<cudaStream_t>(stream), seed, out, iters);
   return check_launch(who);
 }

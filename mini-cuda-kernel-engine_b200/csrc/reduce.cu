@@ -262,6 +262,7 @@ template <bool kP2p>
 __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
                                                                       Part* __restrict__ parts, P2pArgs p2p_in) {
+  pdl_entry();
   P2pArgs p2p = p2p_in;
   extern __shared__ __align__(16) uint8_t smem[];  // P2P: the ranks' collected partials
   __shared__ Part red[kWarps];
@@ -386,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
 template <bool kFinal>
 __global__ void __launch_bounds__(1024) reduce_full_combine_kernel(const Part* __restrict__ parts,
                                                                    int64_t count, void* out) {
+  pdl_entry();
   __shared__ Part red[32];
   Part p = part_identity();
   for (int64_t j = threadIdx.x; j < count; j += blockDim.x) p = part_combine(p, parts[j]);
@@ -411,6 +413,7 @@ __global__ void __launch_bounds__(kThreads) row_reduce_warp_kernel(const float* 
                                                                    float* __restrict__ out,
                                                                    int64_t rows, int64_t cols,
                                                                    double divisor) {
+  pdl_entry();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -459,12 +462,87 @@ __global__ void __launch_bounds__(kThreads) row_reduce_warp_kernel(const float* 
   if (lane == 0) out[row] = kMax ? m : static_cast<float>(s / divisor);
 }
 
+// Rows of at most 1024 floats (cols % 4 == 0, x 16-byte aligned; config 2's
+// 32768 x 1024 is this shape): one warp per row with every load of the row
+// issued before any arithmetic, NV float4 per lane (NV = cols / 128 rounded up
+// to a power of two).  The warp kernel above issues four loads, adds, then
+// issues the next four; here a row's 4 KB is in flight at once.  Each lane adds
+// its float4s in the same order (lane, lane + 32, ...) and the warp folds the
+// lanes with the same butterfly, so the two kernels give the same bits.
+// Measured on B200 at 32768 x 1024, 40 launches back to back: 22.7 us per
+// launch against 24.7 us.  The mean's double division is a subroutine call
+// whose calling convention took the sum kernel to 80 registers (3 CTAs per SM
+// instead of 8; 35 us instead of 23), so only the mean variant (kMean) carries
+// it, with its registers bounded for six resident CTAs.
+// Only for cols == 128 * NV (128, 256, 512, 1024), where every lane loads all NV
+// float4 with no per-load guard: with guards (other widths) the compiler widened
+// all 32 values to double at once, 80 registers and 3 CTAs per SM instead of 32
+// and 8 (35 us instead of 23 at 32768 x 1024), so those widths keep the warp
+// kernel above.
+template <bool kMax, bool kMean, int NV>
+__global__ void __launch_bounds__(kThreads) row_reduce_row_kernel(const float* __restrict__ x,
+                                                                  float* __restrict__ out, int64_t rows,
+                                                                  int64_t cols, double divisor) {
+  pdl_entry();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* xr = x + row * cols;
+  float4 q[NV];
+#pragma unroll
+  for (int u = 0; u < NV; ++u) q[u] = ld_stream_f4(xr + 4 * (lane + 32 * u));
+  double s = 0.0;
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    if (kMax) {
+      m = (m < q[u].x) ? q[u].x : m;
+      m = (m < q[u].y) ? q[u].y : m;
+      m = (m < q[u].z) ? q[u].z : m;
+      m = (m < q[u].w) ? q[u].w : m;
+    } else {
+      s += static_cast<double>(q[u].x);
+      s += static_cast<double>(q[u].y);
+      s += static_cast<double>(q[u].z);
+      s += static_cast<double>(q[u].w);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    if (kMax) {
+      const float t = __shfl_xor_sync(0xffffffffu, m, o);
+      m = (m < t) ? t : m;
+    } else {
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+  }
+  if (lane == 0) {
+    if constexpr (kMax) out[row] = m;
+    else if constexpr (kMean) out[row] = static_cast<float>(s / divisor);
+    else out[row] = static_cast<float>(s);
+  }
+}
+
+template <bool kMax, bool kMean>
+void launch_row_kernel(unsigned g, cudaStream_t s, const float* x, float* out, int64_t rows, int64_t cols,
+                       double divisor) {
+  if (cols == 128)
+    launch_async(row_reduce_row_kernel<kMax, kMean, 1>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+  else if (cols == 256)
+    launch_async(row_reduce_row_kernel<kMax, kMean, 2>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+  else if (cols == 512)
+    launch_async(row_reduce_row_kernel<kMax, kMean, 4>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+  else
+    launch_async(row_reduce_row_kernel<kMax, kMean, 8>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+}
+
 // Two-pass for few long rows: pass 1 splits each row over `split` blocks and
 // stores one double per (row, segment); pass 2 folds a row's segments in order.
 template <bool kMax>
 __global__ void __launch_bounds__(kThreads) row_reduce_split_kernel(const float* __restrict__ x,
                                                                     double* __restrict__ ws,
                                                                     int64_t cols, int64_t split) {
+  pdl_entry();
   __shared__ double red[kWarps];
   const int64_t row = blockIdx.y;
   const int64_t seg = blockIdx.x;
@@ -499,6 +577,7 @@ __global__ void __launch_bounds__(kThreads) row_reduce_fold_kernel(const double*
                                                                    float* __restrict__ out,
                                                                    int64_t rows, int64_t split,
                                                                    double divisor) {
+  pdl_entry();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   if (row >= rows) return;
   double t = kMax ? -INFINITY : 0.0;
@@ -560,8 +639,8 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (n == 0) {
     // The empty reduction still defines its output: sum 0, max -inf, argmax -1.
-    if (final_result) reduce_full_combine_kernel<true><<<1, 32, 0, s>>>(nullptr, 0, out);
-    else reduce_full_combine_kernel<false><<<1, 32, 0, s>>>(nullptr, 0, out);
+    if (final_result) launch_async(reduce_full_combine_kernel<true>, 1, 32, 0, s, nullptr, 0, out);
+    else launch_async(reduce_full_combine_kernel<false>, 1, 32, 0, s, nullptr, 0, out);
     return check_launch(who);
   }
   if (!aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
@@ -577,10 +656,10 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   Part* parts = static_cast<Part*>(workspace);
-  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, index_base, parts, P2pArgs{});
+  launch_async(reduce_full_stream_kernel<false>, static_cast<unsigned>(g), kThreads, 0, s, x, n, head, index_base, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
-  if (final_result) reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
-  else reduce_full_combine_kernel<false><<<1, 1024, 0, s>>>(parts, g, out);
+  if (final_result) launch_async(reduce_full_combine_kernel<true>, 1, 1024, 0, s, parts, g, out);
+  else launch_async(reduce_full_combine_kernel<false>, 1, 1024, 0, s, parts, g, out);
   return check_launch(who);
 }
 }  // namespace
@@ -609,7 +688,7 @@ extern "C" int mcke_sm100_reduce_combine(const mcke_reduce_partial* partials, in
   if (count < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative count", who);
   if (count > 0 && !partials) return fail(MCKE_INVALID_ARGUMENT, "%s: null partials", who);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(reinterpret_cast<const Part*>(partials), count,
+  launch_async(reduce_full_combine_kernel<true>, 1, 1024, 0, s, reinterpret_cast<const Part*>(partials), count,
                                                       out);
   return check_launch(who);
 }
@@ -652,24 +731,30 @@ extern "C" int mcke_sm100_reduce_row_f32(const float* x, float* out, int64_t row
     const dim3 g1(static_cast<unsigned>(split), static_cast<unsigned>(rows), 1u);
     const unsigned g2 = static_cast<unsigned>((rows + kThreads - 1) / kThreads);
     if (is_max) {
-      row_reduce_split_kernel<true><<<g1, kThreads, 0, s>>>(x, ws, cols, split);
+      launch_async(row_reduce_split_kernel<true>, g1, kThreads, 0, s, x, ws, cols, split);
       MCKE_RETURN_IF(check_launch(who));
-      row_reduce_fold_kernel<true><<<g2, kThreads, 0, s>>>(ws, out, rows, split, divisor);
+      launch_async(row_reduce_fold_kernel<true>, g2, kThreads, 0, s, ws, out, rows, split, divisor);
     } else {
-      row_reduce_split_kernel<false><<<g1, kThreads, 0, s>>>(x, ws, cols, split);
+      launch_async(row_reduce_split_kernel<false>, g1, kThreads, 0, s, x, ws, cols, split);
       MCKE_RETURN_IF(check_launch(who));
-      row_reduce_fold_kernel<false><<<g2, kThreads, 0, s>>>(ws, out, rows, split, divisor);
+      launch_async(row_reduce_fold_kernel<false>, g2, kThreads, 0, s, ws, out, rows, split, divisor);
     }
     return check_launch(who);
   }
   const bool vec = (cols % 4 == 0) && aligned(x, 16);
   const unsigned g = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
+  if (vec && (cols == 128 || cols == 256 || cols == 512 || cols == 1024)) {
+    if (is_max) launch_row_kernel<true, false>(g, s, x, out, rows, cols, divisor);
+    else if (kind == MCKE_REDUCE_MEAN) launch_row_kernel<false, true>(g, s, x, out, rows, cols, divisor);
+    else launch_row_kernel<false, false>(g, s, x, out, rows, cols, divisor);
+    return check_launch(who);
+  }
   if (is_max) {
-    if (vec) row_reduce_warp_kernel<true, true><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
-    else row_reduce_warp_kernel<true, false><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+    if (vec) launch_async(row_reduce_warp_kernel<true, true>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+    else launch_async(row_reduce_warp_kernel<true, false>, g, kThreads, 0, s, x, out, rows, cols, divisor);
   } else {
-    if (vec) row_reduce_warp_kernel<false, true><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
-    else row_reduce_warp_kernel<false, false><<<g, kThreads, 0, s>>>(x, out, rows, cols, divisor);
+    if (vec) launch_async(row_reduce_warp_kernel<false, true>, g, kThreads, 0, s, x, out, rows, cols, divisor);
+    else launch_async(row_reduce_warp_kernel<false, false>, g, kThreads, 0, s, x, out, rows, cols, divisor);
   }
   return check_launch(who);
 }
@@ -733,7 +818,7 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   if (n > 0 && !x) return fail(MCKE_INVALID_ARGUMENT, "%s: null input", who);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (n == 0) {
-    reduce_full_combine_kernel<true><<<1, 32, 0, s>>>(nullptr, 0, out);
+    launch_async(reduce_full_combine_kernel<true>, 1, 32, 0, s, nullptr, 0, out);
     return check_launch(who);
   }
   if (!aligned(x, 4)) return fail(MCKE_INVALID_ARGUMENT, "%s: x not 4-byte aligned", who);
@@ -752,9 +837,9 @@ extern "C" int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mck
   // array's leftover contents from an earlier call are never read and nothing
   // needs clearing.
   Part* parts = static_cast<Part*>(scratch);
-  reduce_full_stream_kernel<false><<<static_cast<unsigned>(g), kThreads, 0, s>>>(x, n, head, 0, parts, P2pArgs{});
+  launch_async(reduce_full_stream_kernel<false>, static_cast<unsigned>(g), kThreads, 0, s, x, n, head, 0, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
-  reduce_full_combine_kernel<true><<<1, 1024, 0, s>>>(parts, g, out);
+  launch_async(reduce_full_combine_kernel<true>, 1, 1024, 0, s, parts, g, out);
   return check_launch(who);
 }
 
@@ -763,6 +848,7 @@ namespace mcke_sm100 {
 namespace {
 // Only for an empty shard (no pass-1 CTA to run the exchange).
 __global__ void __launch_bounds__(kThreads) reduce_p2p_empty_kernel(P2pArgs a_in) {
+  pdl_entry();
   extern __shared__ __align__(16) uint8_t scratch[];
   P2pArgs a = a_in;
   resolve_tag(a);
@@ -797,7 +883,7 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   a.rank = rank;
   a.auto_epoch = epoch == 0 ? 1 : 0;
   if (n == 0) {
-    reduce_p2p_empty_kernel<<<1, kThreads, static_cast<size_t>(world) * sizeof(Part), s>>>(a);
+    launch_async(reduce_p2p_empty_kernel, 1, kThreads, static_cast<size_t>(world) * sizeof(Part), s, a);
     return check_launch(who);
   }
   const int64_t g = full_blocks(n);
@@ -805,8 +891,7 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   // dynamic shared memory: the ranks' collected partials (world <= 1024: 24 KB)
-  reduce_full_stream_kernel<true><<<static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s>>>(
-      x, n, head, index_base, nullptr, a);
+  launch_async(reduce_full_stream_kernel<true>, static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s, x, n, head, index_base, nullptr, a);
   return check_launch(who);
 }
 

@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_last_error_string": (ctypes.c_char_p, []),
             "mcke_sm100_check_device_errors": (i32, [vp]),
             "mcke_sm100_watchdog_selftest": (i32, [vp]),
+            "mcke_sm100_set_programmatic_launch": (i32, [i32]),
             "mcke_sm100_vector_add_f32": (i32, [vp, vp, vp, sz, vp]),
             "mcke_sm100_peak_triad_f32": (i32, [vp, vp, vp, f32, i64, vp]),
             "mcke_sm100_peak_copy_f32": (i32, [vp, vp, i64, vp]),
@@ -96,6 +97,12 @@ def lib() -> ctypes.CDLL:
             fn.restype, fn.argtypes = res, args
         _lib = l
     return _lib
+
+
+def set_programmatic_launch(enable: bool) -> bool:
+    """Launch this library's kernels with programmatic dependent launch (the
+    default) or plainly; returns the previous setting.  Results are the same."""
+    return bool(lib().mcke_sm100_set_programmatic_launch(1 if enable else 0))
 
 
 def _check(rc: int) -> None:

@@ -63,8 +63,22 @@ mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_d
 #define MCKE_EXECUTOR_CUDA_GRAPH 1u
 #define MCKE_EXECUTOR_POISON 2u
 #define MCKE_EXECUTOR_NCCL_EXCHANGE 4u
+/*   MCKE_EXECUTOR_BUDDY       take each device's arena from a BuddyAllocator of
+ *                             that device with 4 GiB slabs (mcke/memory/buddy_allocator.hpp;
+ *                             the reference's DeviceAllocator interface, executor.hpp:285),
+ *                             owned by this handle;
+ *   MCKE_EXECUTOR_VALIDATE    keep host copies of the inputs for
+ *                             mcke_executor_validate_numerics (ExecutorOptions::validate_numerics). */
+#define MCKE_EXECUTOR_BUDDY 8u
+#define MCKE_EXECUTOR_VALIDATE 16u
 mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
                                        unsigned flags);
+/* As mcke_executor_create_ex with the stream schedule (mcke::SchedulePolicy:
+ * 0 sequential, 1 level-parallel, 2 chain-greedy; schedule.hpp:49 of the
+ * reference) and the memory policy (mcke::MemoryPolicy: 0 alloc-per-tensor,
+ * 2 reuse-same-stream, 3 reuse-happens-before; memory_plan.hpp:67). */
+mcke_executor* mcke_executor_create_policy(mcke_graph* g, const int* devices, int num_devices, int num_streams,
+                                           unsigned flags, int schedule, int memory);
 void mcke_executor_destroy(mcke_executor* e);
 /* Planning only (placement, streams, memory): touches no GPU. */
 int mcke_executor_plan_dry(mcke_executor* e);
@@ -81,6 +95,22 @@ int mcke_executor_describe(mcke_executor* e, char* buf, size_t len);
 int mcke_executor_placement(mcke_executor* e, uint32_t t, int* placement_out);
 int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_out);
 int mcke_executor_num_events(mcke_executor* e, size_t* out);
+/* The numerics gate (executor.hpp:268 of the reference, GraphExecutor::validate_numerics):
+ * replays the graph under every schedule x memory policy x {eager, CUDA graph}
+ * on this executor's devices, `repeats` runs each, and compares all outputs bit
+ * for bit with a sequential, alloc-per-tensor, eager golden run and each
+ * configuration with its own first run.  Needs MCKE_EXECUTOR_VALIDATE and every
+ * input set.  *passed = 1 or 0, *configs = configurations compared; detail
+ * receives the first mismatch (configuration, output, word, both words). */
+int mcke_executor_validate_numerics(mcke_executor* e, int repeats, int* passed, int* configs, char* detail,
+                                    size_t len);
+/* Statistics of device entry `device_index`'s allocator (mcke::AllocatorStats). */
+typedef struct {
+  uint64_t alloc_calls, free_calls, raw_malloc_calls, raw_free_calls;
+  uint64_t bytes_reserved, bytes_in_use, bytes_requested, peak_bytes_in_use;
+  char name[24];
+} mcke_alloc_stats;
+int mcke_executor_alloc_stats(mcke_executor* e, int device_index, mcke_alloc_stats* out);
 
 #ifdef __cplusplus
 }

@@ -37,21 +37,47 @@
 //
 // plan_dry() runs steps 1-3 without touching CUDA, for tests on a host with
 // no GPU.
+//
+// Memory.  Each device's arena is one block taken from that device's
+// DeviceAllocator (ExecutorOptions::allocators, or the allocator passed to the
+// reference-shaped constructor; executor.hpp:285 of the reference takes one)
+// on the device's stream 0, and returned to it when the executor goes away;
+// with no allocator the executor cudaMallocs the arena itself.  Inside the
+// arena the memory plan gives every tensor its offset (MemoryPolicy).
+//
+// Launches.  plan() also builds, once, every node's per-device OpContext and
+// input/output Tensor vectors (pointers are fixed at plan time), so an eager
+// run_async only issues event waits, launches and event records.
 #pragma once
 
 #include <cstddef>
+#include <cstdint>
 #include <memory>
+#include <optional>
 #include <string>
 #include <vector>
 
+#include "mcke/core/device.hpp"
 #include "mcke/graph/graph.hpp"
+#include "mcke/graph/memory_plan.hpp"
+#include "mcke/graph/schedule.hpp"
+#include "mcke/memory/allocator.hpp"
 
 namespace mcke {
 
 struct ExecutorOptions {
+  // include/mcke/graph/executor.hpp:115 of the reference, same names:
+  SchedulePolicy schedule = SchedulePolicy::kChainGreedy;
+  MemoryPolicy memory = MemoryPolicy::kReuseHappensBefore;
+  int num_streams = 4;           // streams per device
+  bool validate_numerics = false;  // keep host copies of inputs for validate_numerics()
+  bool poison_buffers = false;     // fill intermediates with poison_pattern before each run
+  std::uint32_t poison_pattern = 0x7F7F7F7Fu;
+  // Added for one process driving a box:
   std::vector<int> devices{0};
-  int streams_per_device = 4;
-  bool poison_buffers = false;  // fill intermediates with 0xFF before each run
+  // One allocator per entry of `devices` (null or missing: the executor
+  // cudaMallocs that device's arena itself).  Not owned.
+  std::vector<DeviceAllocator*> allocators;
   // Capture the first run_async into CUDA graphs and replay them.  Needs a
   // device list that is all distinct GPUs or one GPU repeated.
   bool use_graph = false;
@@ -59,6 +85,19 @@ struct ExecutorOptions {
   // peer-to-peer combine (needs peer access between every pair; otherwise,
   // or when false, NCCL all-gathers them).
   bool p2p_exchange = true;
+};
+
+// Index of the first differing 32-bit word, or `bytes` when identical.
+// Compared as integers: a float compare calls NaN != NaN and -0 == +0.
+[[nodiscard]] std::size_t first_bit_mismatch(const void* a, const void* b, std::size_t bytes);
+
+// Outcome of the numerics gate (include/mcke/graph/executor.hpp:149 of the reference).
+struct NumericsResult {
+  bool passed = false;
+  int configs_compared = 0;
+  int repeats = 0;
+  std::size_t elements_compared = 0;
+  std::string detail;  // on failure: config, tensor, word index, both words in hex
 };
 
 struct TensorPlan {
@@ -73,6 +112,10 @@ struct TensorPlan {
 class GraphExecutor {
  public:
   explicit GraphExecutor(Graph& g, ExecutorOptions opts = {});
+  // The reference's constructor (include/mcke/graph/executor.hpp:285): the
+  // executor owns `graph`, runs on `device.index`, and takes its arena from
+  // `alloc` (which must outlive the executor).
+  GraphExecutor(Graph graph, DeviceAllocator& alloc, DeviceInfo device, ExecutorOptions opts = {});
   ~GraphExecutor();
   GraphExecutor(const GraphExecutor&) = delete;
   GraphExecutor& operator=(const GraphExecutor&) = delete;
@@ -91,10 +134,21 @@ class GraphExecutor {
   // Gathers a graph output's shards into host memory (whole tensor).
   [[nodiscard]] Status copy_output_to_host(TensorId t, void* host, std::size_t bytes);
 
+  // The numerics gate (include/mcke/graph/executor.hpp:268-278 of the
+  // reference): replays the graph under every {schedule} x {memory policy} x
+  // {eager, CUDA-graph replay} configuration on this executor's devices, each
+  // in a fresh executor fed the inputs given to set_input (which needs
+  // opts.validate_numerics), `repeats` runs each, and compares every graph
+  // output bit for bit against a golden run (kSequential, kAllocPerTensor,
+  // eager) and each configuration against its own first run.
+  [[nodiscard]] StatusOr<NumericsResult> validate_numerics(int repeats = 3);
+
   [[nodiscard]] const TensorPlan& tensor_plan(TensorId t) const { return tplan_.at(t); }
   [[nodiscard]] int stream_of(NodeId n) const { return node_stream_.at(n); }
   [[nodiscard]] std::size_t arena_bytes(int device_index) const { return arena_bytes_.at(device_index); }
   [[nodiscard]] int num_devices() const { return static_cast<int>(opts_.devices.size()); }
+  [[nodiscard]] const ExecutorOptions& options() const noexcept { return opts_; }
+  [[nodiscard]] const DeviceInfo& device_info() const noexcept { return device_; }
   [[nodiscard]] std::size_t num_events() const { return event_edges_; }
   [[nodiscard]] std::string describe() const;
 
@@ -106,9 +160,13 @@ class GraphExecutor {
   [[nodiscard]] Tensor local_tensor(TensorId t, int d) const;
   [[nodiscard]] Status enqueue(bool capturing);
   [[nodiscard]] Status capture();
+  [[nodiscard]] Status build_launches();
 
+  std::optional<Graph> owned_;  // the graph, when the executor was given it by value
   Graph& g_;
   ExecutorOptions opts_;
+  DeviceInfo device_;
+  std::vector<std::pair<TensorId, std::vector<char>>> input_cache_;  // validate_numerics only
   std::vector<TensorPlan> tplan_;
   std::vector<int> node_stream_;                 // same stream index on every device
   std::vector<std::vector<int>> waits_;          // per node: producer nodes on other streams

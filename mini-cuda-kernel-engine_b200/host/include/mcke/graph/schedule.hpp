@@ -1,0 +1,18 @@
+// mcke/graph/schedule.hpp -- how the executor spreads nodes over streams.
+//
+// Mirrors mini-cuda-kernel-engine include/mcke/graph/schedule.hpp:49
+// (SchedulePolicy, same values).  On every device of a sharded executor the
+// same node goes to the same stream index.
+#pragma once
+
+#include <cstdint>
+
+namespace mcke {
+
+enum class SchedulePolicy : std::uint8_t {
+  kSequential,     // every node on stream 0, in topological order
+  kLevelParallel,  // nodes of one topological level (longest path from an input) dealt round-robin over streams
+  kChainGreedy,    // a node inherits its first producer's stream unless a sibling already did, else the least recently used
+};
+
+}  // namespace mcke

@@ -6,11 +6,15 @@
 #include <string>
 
 #include "mcke/graph/executor.hpp"
+#include "mcke/memory/buddy_allocator.hpp"
 
 struct mcke_graph {
   mcke::Graph g;
 };
 struct mcke_executor {
+  // declared before `ex`, so the executor (which returns its arenas to them)
+  // goes first
+  std::vector<std::unique_ptr<mcke::BuddyAllocator>> allocs;
   std::unique_ptr<mcke::GraphExecutor> ex;
 };
 
@@ -105,18 +109,37 @@ int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint
 int mcke_graph_mark_output(mcke_graph* g, uint32_t t) { return g ? ret(g->g.mark_output(t)) : 2; }
 int mcke_graph_finalize(mcke_graph* g) { return g ? ret(g->g.finalize()) : 2; }
 
-mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
-                                       unsigned flags) {
-  if (!g || !devices || num_devices < 1) return nullptr;
+mcke_executor* mcke_executor_create_policy(mcke_graph* g, const int* devices, int num_devices, int num_streams,
+                                           unsigned flags, int schedule, int memory) {
+  if (!g || !devices || num_devices < 1 || schedule < 0 || schedule > 2 || memory < 0 || memory > 3) return nullptr;
   mcke::ExecutorOptions o;
   o.devices.assign(devices, devices + num_devices);
-  o.streams_per_device = streams_per_device > 0 ? streams_per_device : 4;
+  o.num_streams = num_streams > 0 ? num_streams : 4;
   o.use_graph = (flags & MCKE_EXECUTOR_CUDA_GRAPH) != 0;
   o.poison_buffers = (flags & MCKE_EXECUTOR_POISON) != 0;
   o.p2p_exchange = (flags & MCKE_EXECUTOR_NCCL_EXCHANGE) == 0;
+  o.validate_numerics = (flags & MCKE_EXECUTOR_VALIDATE) != 0;
+  o.schedule = static_cast<mcke::SchedulePolicy>(schedule);
+  o.memory = static_cast<mcke::MemoryPolicy>(memory);
   auto* e = new mcke_executor();
+  if (flags & MCKE_EXECUTOR_BUDDY) {
+    // 4 GiB slabs: config 5's ~3.6 GB arena is one buddy block of a slab
+    mcke::BuddyConfig bc;
+    bc.slab_bytes = std::size_t{1} << 32;
+    for (int d = 0; d < num_devices; ++d) {
+      e->allocs.push_back(std::make_unique<mcke::BuddyAllocator>(devices[d], bc));
+      o.allocators.push_back(e->allocs.back().get());
+    }
+  }
   e->ex = std::make_unique<mcke::GraphExecutor>(g->g, o);
   return e;
+}
+
+mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int num_devices, int streams_per_device,
+                                       unsigned flags) {
+  return mcke_executor_create_policy(g, devices, num_devices, streams_per_device, flags,
+                                     static_cast<int>(mcke::SchedulePolicy::kChainGreedy),
+                                     static_cast<int>(mcke::MemoryPolicy::kReuseHappensBefore));
 }
 
 mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device) {
@@ -173,6 +196,42 @@ int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_
 int mcke_executor_num_events(mcke_executor* e, size_t* out) {
   EX_CHECK(e);
   if (out) *out = e->ex->num_events();
+  return 0;
+}
+int mcke_executor_validate_numerics(mcke_executor* e, int repeats, int* passed, int* configs, char* detail,
+                                    size_t len) {
+  EX_CHECK(e);
+  auto r = e->ex->validate_numerics(repeats);
+  if (!r.ok()) return ret(r.status());
+  if (passed) *passed = r->passed ? 1 : 0;
+  if (configs) *configs = r->configs_compared;
+  if (detail && len) {
+    const size_t n = r->detail.size() < len - 1 ? r->detail.size() : len - 1;
+    std::memcpy(detail, r->detail.data(), n);
+    detail[n] = '\0';
+  }
+  return 0;
+}
+int mcke_executor_alloc_stats(mcke_executor* e, int device_index, mcke_alloc_stats* out) {
+  EX_CHECK(e);
+  const auto& al = e->ex->options().allocators;
+  if (device_index < 0 || device_index >= static_cast<int>(al.size()) || !al[device_index] || !out) {
+    g_err = "mcke_executor_alloc_stats: no allocator for that device entry";
+    return static_cast<int>(mcke::StatusCode::kInvalidArgument);
+  }
+  const mcke::AllocatorStats st = al[device_index]->stats();
+  out->alloc_calls = st.alloc_calls;
+  out->free_calls = st.free_calls;
+  out->raw_malloc_calls = st.raw_malloc_calls;
+  out->raw_free_calls = st.raw_free_calls;
+  out->bytes_reserved = st.bytes_reserved;
+  out->bytes_in_use = st.bytes_in_use;
+  out->bytes_requested = st.bytes_requested;
+  out->peak_bytes_in_use = st.peak_bytes_in_use;
+  const std::string_view nm = al[device_index]->name();
+  const size_t n = nm.size() < sizeof(out->name) - 1 ? nm.size() : sizeof(out->name) - 1;
+  std::memcpy(out->name, nm.data(), n);
+  out->name[n] = '\0';
   return 0;
 }
 

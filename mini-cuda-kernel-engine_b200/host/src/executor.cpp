@@ -4,6 +4,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 
 namespace mcke {
@@ -43,6 +44,8 @@ struct GraphExecutor::Impl {
   struct Dev {
     int device = 0;
     void* arena = nullptr;
+    DeviceAllocator* alloc = nullptr;  // where the arena came from (null: cudaMalloc)
+    Allocation arena_block;
     std::vector<rt::Stream> streams;
     std::vector<rt::Event> node_events;  // indexed by NodeId (only where recorded)
     std::vector<rt::Event> done;         // one per stream: end of the previous run
@@ -64,6 +67,14 @@ struct GraphExecutor::Impl {
   // the device entry whose stream 0 launches execs[i] and carries its timing.
   std::vector<cudaGraphExec_t> execs;
   std::vector<int> origins;
+  // Per node, built once by build_launches(): each device's context and
+  // tensors, and where each device gathers the exchanged partials.
+  struct NodeLaunch {
+    std::vector<OpContext> ctx;
+    std::vector<std::vector<Tensor>> ins, outs;
+    std::vector<void*> gathered;
+  };
+  std::vector<NodeLaunch> launches;
   ~Impl() {
     for (std::size_t nid = 0; nid < p2p_buf.size(); ++nid)
       for (std::size_t d = 0; d < p2p_buf[nid].size(); ++d) {
@@ -78,13 +89,42 @@ struct GraphExecutor::Impl {
     for (Dev& d : devs) {
       rt::DeviceGuard g(d.device);
       if (d.comm) ncclCommDestroy(d.comm);
-      if (d.arena) cudaFree(d.arena);
+      if (d.arena && d.alloc) {
+        // the last run's work may still be in flight on any of the streams
+        for (auto& st : d.streams) static_cast<void>(st.synchronize());
+        static_cast<void>(d.alloc->deallocate(d.arena_block, d.streams.empty() ? nullptr : d.streams[0].native()));
+      } else if (d.arena) {
+        cudaFree(d.arena);
+      }
     }
   }
 };
 
-GraphExecutor::GraphExecutor(Graph& g, ExecutorOptions opts) : g_(g), opts_(std::move(opts)) {}
+GraphExecutor::GraphExecutor(Graph& g, ExecutorOptions opts) : g_(g), opts_(std::move(opts)) {
+  device_.index = opts_.devices.empty() ? 0 : opts_.devices[0];
+}
+
+GraphExecutor::GraphExecutor(Graph graph, DeviceAllocator& alloc, DeviceInfo device, ExecutorOptions opts)
+    : owned_(std::move(graph)), g_(*owned_), opts_(std::move(opts)), device_(std::move(device)) {
+  opts_.devices = {device_.index};
+  opts_.allocators = {&alloc};
+}
+
 GraphExecutor::~GraphExecutor() = default;
+
+std::size_t first_bit_mismatch(const void* a, const void* b, std::size_t bytes) {
+  const auto* x = static_cast<const unsigned char*>(a);
+  const auto* y = static_cast<const unsigned char*>(b);
+  for (std::size_t i = 0; i + 4 <= bytes; i += 4) {
+    std::uint32_t u, v;
+    std::memcpy(&u, x + i, 4);
+    std::memcpy(&v, y + i, 4);
+    if (u != v) return i / 4;
+  }
+  for (std::size_t i = bytes / 4 * 4; i < bytes; ++i)
+    if (x[i] != y[i]) return i / 4;
+  return bytes;
+}
 
 // ------------------------------------------------------------- placement
 
@@ -203,29 +243,44 @@ Status GraphExecutor::place() {
 // ------------------------------------------------------------ streams
 
 Status GraphExecutor::assign_streams() {
-  const int S = std::max(1, opts_.streams_per_device);
+  const int S = std::max(1, opts_.num_streams);
   const std::size_t N = g_.num_nodes();
   node_stream_.assign(N, 0);
   waits_.assign(N, {});
   record_after_.assign(N, false);
-  std::vector<bool> donated(N, false);
-  std::vector<std::int64_t> last_use(S, -1);
-  std::int64_t tick = 0;
-  for (NodeId nid : g_.topo_order()) {
-    const Node& n = g_.node(nid);
-    int s = -1;
-    for (TensorId t : n.inputs) {
-      const NodeId p = g_.producer(t);
-      if (p != kInvalidNode && !donated[p]) {
-        donated[p] = true;
-        s = node_stream_[p];
-        break;
+  if (opts_.schedule == SchedulePolicy::kLevelParallel) {
+    // level = longest path from a graph input; each level dealt round-robin
+    std::vector<int> level(N, 0);
+    int max_level = 0;
+    for (NodeId nid : g_.topo_order()) {
+      for (TensorId t : g_.node(nid).inputs) {
+        const NodeId p = g_.producer(t);
+        if (p != kInvalidNode) level[nid] = std::max(level[nid], level[p] + 1);
       }
+      max_level = std::max(max_level, level[nid]);
     }
-    if (s < 0) s = static_cast<int>(std::min_element(last_use.begin(), last_use.end()) - last_use.begin());
-    node_stream_[nid] = s;
-    last_use[s] = tick++;
-  }
+    std::vector<int> next(static_cast<std::size_t>(max_level) + 1, 0);
+    for (NodeId nid : g_.topo_order()) node_stream_[nid] = next[level[nid]]++ % S;
+  } else if (opts_.schedule == SchedulePolicy::kChainGreedy) {
+    std::vector<bool> donated(N, false);
+    std::vector<std::int64_t> last_use(S, -1);
+    std::int64_t tick = 0;
+    for (NodeId nid : g_.topo_order()) {
+      const Node& n = g_.node(nid);
+      int s = -1;
+      for (TensorId t : n.inputs) {
+        const NodeId p = g_.producer(t);
+        if (p != kInvalidNode && !donated[p]) {
+          donated[p] = true;
+          s = node_stream_[p];
+          break;
+        }
+      }
+      if (s < 0) s = static_cast<int>(std::min_element(last_use.begin(), last_use.end()) - last_use.begin());
+      node_stream_[nid] = s;
+      last_use[s] = tick++;
+    }
+  }  // kSequential: every node stays on stream 0
   event_edges_ = 0;
   for (NodeId nid : g_.topo_order()) {
     const Node& n = g_.node(nid);
@@ -244,8 +299,11 @@ Status GraphExecutor::assign_streams() {
 // ------------------------------------------------------------- memory
 
 Status GraphExecutor::plan_memory() {
+  if (opts_.memory == MemoryPolicy::kReuseTopoNaive)
+    return UnimplementedError("MemoryPolicy::kReuseTopoNaive is unsafe under parallel schedules and not offered");
+  const bool reuse = opts_.memory != MemoryPolicy::kAllocPerTensor;
   const int D = num_devices();
-  const int S = std::max(1, opts_.streams_per_device);
+  const int S = std::max(1, opts_.num_streams);
   const auto& order = g_.topo_order();
   const std::size_t T = g_.num_tensors();
   std::vector<std::int64_t> pos(g_.num_nodes(), 0);
@@ -305,7 +363,7 @@ Status GraphExecutor::plan_memory() {
         if (tplan_[o].offset[d] >= 0) continue;
         const std::size_t need = align_up(std::max<std::size_t>(tplan_[o].local_bytes(d), 1));
         int best = -1;
-        if (single_stream[o])
+        if (reuse && single_stream[o])
           for (std::size_t b = 0; b < blocks.size(); ++b)
             if (blocks[b].free && blocks[b].stream == s && blocks[b].size >= need &&
                 (best < 0 || blocks[b].size < blocks[best].size))
@@ -350,18 +408,22 @@ Status GraphExecutor::plan() {
   MCKE_RETURN_IF_ERROR(plan_dry());
   impl_ = std::make_unique<Impl>();
   const int D = num_devices();
-  const int S = std::max(1, opts_.streams_per_device);
+  const int S = std::max(1, opts_.num_streams);
   impl_->devs.resize(D);
   bool any_exchange = false;
   for (NodeId nid : g_.topo_order()) any_exchange |= g_.node(nid).op->exchange_bytes() > 0;
+  if (opts_.poison_buffers) {
+    const std::uint32_t p = opts_.poison_pattern;
+    if (((p >> 8) & 0xFFu) != (p & 0xFFu) || ((p >> 16) & 0xFFu) != (p & 0xFFu) || (p >> 24) != (p & 0xFFu))
+      return InvalidArgumentError("poison_pattern must repeat one byte (e.g. 0x7F7F7F7F)");
+  }
+  if (!opts_.allocators.empty() && static_cast<int>(opts_.allocators.size()) != D)
+    return InvalidArgumentError("ExecutorOptions.allocators: one per device entry (" + std::to_string(D) +
+                                "), got " + std::to_string(opts_.allocators.size()));
   for (int d = 0; d < D; ++d) {
     auto& dv = impl_->devs[d];
     dv.device = opts_.devices[d];
     rt::DeviceGuard guard(dv.device);
-    const cudaError_t e = cudaMalloc(&dv.arena, std::max<std::size_t>(arena_bytes_[d], kAlign));
-    if (e != cudaSuccess)
-      return OutOfMemoryError("arena of " + std::to_string(arena_bytes_[d]) + " bytes on device " +
-                              std::to_string(dv.device) + ": " + cudaGetErrorString(e));
     for (int s = 0; s < S; ++s) {
       auto st = rt::Stream::create(dv.device);
       MCKE_RETURN_IF_ERROR(st.status());
@@ -369,6 +431,24 @@ Status GraphExecutor::plan() {
       auto ev = rt::Event::create(dv.device);
       MCKE_RETURN_IF_ERROR(ev.status());
       dv.done.push_back(std::move(*ev));
+    }
+    const std::size_t bytes = std::max<std::size_t>(arena_bytes_[d], kAlign);
+    dv.alloc = opts_.allocators.empty() ? nullptr : opts_.allocators[d];
+    if (dv.alloc) {
+      auto a = dv.alloc->allocate(bytes, dv.streams[0].native());
+      if (!a.ok())
+        return Status(a.status().code(), "arena of " + std::to_string(bytes) + " bytes on device " +
+                                             std::to_string(dv.device) + " from " + std::string(dv.alloc->name()) +
+                                             ": " + a.status().message());
+      if (reinterpret_cast<std::uintptr_t>(a->ptr) % kAlign != 0)
+        return InternalError(std::string(dv.alloc->name()) + " returned a block not aligned to 256 bytes");
+      dv.arena_block = *a;
+      dv.arena = a->ptr;
+    } else {
+      const cudaError_t e = cudaMalloc(&dv.arena, bytes);
+      if (e != cudaSuccess)
+        return OutOfMemoryError("arena of " + std::to_string(arena_bytes_[d]) + " bytes on device " +
+                                std::to_string(dv.device) + ": " + cudaGetErrorString(e));
     }
     if (opts_.use_graph) {
       auto f = rt::Event::create(dv.device);
@@ -457,7 +537,64 @@ Status GraphExecutor::plan() {
     MCKE_RETURN_IF_ERROR(nccl_status(ncclCommInitAll(comms.data(), D, opts_.devices.data()), "ncclCommInitAll"));
     for (int d = 0; d < D; ++d) impl_->devs[d].comm = comms[d];
   }
+  MCKE_RETURN_IF_ERROR(build_launches());
   planned_ = true;
+  return OkStatus();
+}
+
+// Every node's per-device OpContext and input/output tensors, once: the
+// pointers are fixed by the memory plan and the arenas.
+Status GraphExecutor::build_launches() {
+  const int D = num_devices();
+  impl_->launches.assign(g_.num_nodes(), {});
+  for (NodeId nid : g_.topo_order()) {
+    const Node& n = g_.node(nid);
+    const int s = node_stream_[nid];
+    auto& L = impl_->launches[nid];
+    L.ctx.resize(D);
+    L.ins.resize(D);
+    L.outs.resize(D);
+    L.gathered.assign(D, nullptr);
+    for (int d = 0; d < D; ++d) {
+      auto& dv = impl_->devs[d];
+      OpContext& c = L.ctx[d];
+      c.stream = dv.streams[s].native();
+      c.device = dv.device;
+      c.workspace = scratch_bytes_[s] ? static_cast<char*>(dv.arena) + scratch_offset_[d][s] : nullptr;
+      c.workspace_bytes = scratch_bytes_[s];
+      c.shard = d;
+      c.num_shards = D;
+      for (TensorId t : n.inputs) {
+        Tensor x = local_tensor(t, d);
+        // A replicated intermediate consumed row-wise: view this device's rows.
+        if (view_rows_[nid] && t == n.inputs[0]) {
+          const Shape& full = g_.tensor(t).shape;
+          const std::int64_t E = full.rank() >= 2 ? full.rows() : full.numel();
+          const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
+          const std::int64_t b = E * d / D, e = E * (d + 1) / D;
+          x.data = static_cast<char*>(x.data) + b * inner * static_cast<std::int64_t>(dtype_size(x.dtype));
+          x.shape = full.rank() >= 2 ? Shape{e - b, inner} : Shape{e - b};
+        }
+        L.ins[d].push_back(x);
+      }
+      for (TensorId t : n.outputs) L.outs[d].push_back(local_tensor(t, d));
+      // Range shards of a full reduce: global index of this device's first element.
+      if (!n.inputs.empty()) {
+        const TensorPlan& tp = tplan_[n.inputs[0]];
+        const Shape& full = g_.tensor(n.inputs[0]).shape;
+        const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
+        if (tp.placement == Placement::kRowSplit || view_rows_[nid])
+          c.index_base = (full.rank() >= 2 ? full.rows() : full.numel()) * d / D * inner;
+      }
+      if (exchange_offset_[d][nid] >= 0) c.exchange = static_cast<char*>(dv.arena) + exchange_offset_[d][nid];
+      if (impl_->p2p && !impl_->p2p_table.empty() && impl_->p2p_table[nid][d])
+        c.p2p_peers = static_cast<void* const*>(impl_->p2p_table[nid][d]);
+    }
+    const std::size_t eb = n.op->exchange_bytes();
+    if (eb > 0)
+      for (int d = 0; d < D; ++d)
+        L.gathered[d] = D > 1 ? static_cast<char*>(L.ctx[d].exchange) + eb : L.ctx[d].exchange;
+  }
   return OkStatus();
 }
 
@@ -494,7 +631,7 @@ Status GraphExecutor::run_async() {
 
 Status GraphExecutor::capture() {
   const int D = num_devices();
-  const int S = std::max(1, opts_.streams_per_device);
+  const int S = std::max(1, opts_.num_streams);
   std::vector<std::vector<int>> groups;
   if (D > 1 && impl_->peer_copy) {
     // Repeated GPUs exchange with event-ordered copies between the entries:
@@ -585,18 +722,17 @@ Status GraphExecutor::capture() {
   return st;
 }
 
-Status GraphExecutor::enqueue(bool capturing) {
+Status GraphExecutor::enqueue(bool /*capturing*/) {
   const int D = num_devices();
-  const int S = std::max(1, opts_.streams_per_device);
+  const int S = std::max(1, opts_.num_streams);
   // Each run starts after every stream of the previous run finished (join),
   // so a reused block is never overwritten while a reader is still running.
   // (A captured run needs no such wait: graph launches on one stream are
   // ordered.)
+  // (The previous run ended with stream 0 waiting for every other stream, so
+  // t_start, recorded on stream 0 and waited on by the others, already orders
+  // this run after all of it.)
   for (auto& dv : impl_->devs) {
-    if (impl_->ran_once && !capturing)
-      for (int s = 0; s < S; ++s)
-        for (int o = 0; o < S; ++o)
-          if (o != s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[o]));
     MCKE_RETURN_IF_ERROR(dv.t_start.record(dv.streams[0]));
     for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.t_start));
     if (opts_.poison_buffers) {
@@ -604,7 +740,8 @@ Status GraphExecutor::enqueue(bool capturing) {
       const int d = static_cast<int>(&dv - impl_->devs.data());
       for (TensorId t = 0; t < g_.num_tensors(); ++t)
         if (!g_.is_input(t))
-          MCKE_CUDA_RETURN_IF_ERROR(cudaMemsetAsync(static_cast<char*>(dv.arena) + tplan_[t].offset[d], 0xFF,
+          MCKE_CUDA_RETURN_IF_ERROR(cudaMemsetAsync(static_cast<char*>(dv.arena) + tplan_[t].offset[d],
+                                                    static_cast<int>(opts_.poison_pattern & 0xFFu),
                                                     tplan_[t].local_bytes(d), dv.streams[0].native()));
       MCKE_RETURN_IF_ERROR(dv.done[0].record(dv.streams[0]));
       for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[0]));
@@ -613,43 +750,12 @@ Status GraphExecutor::enqueue(bool capturing) {
   for (NodeId nid : g_.topo_order()) {
     Node& n = g_.node(nid);
     const int s = node_stream_[nid];
-    std::vector<OpContext> ctx(D);
-    std::vector<std::vector<Tensor>> ins(D), outs(D);
-    for (int d = 0; d < D; ++d) {
-      auto& dv = impl_->devs[d];
-      for (int p : waits_[nid]) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.node_events[p]));
-      ctx[d].stream = dv.streams[s].native();
-      ctx[d].device = dv.device;
-      ctx[d].workspace = scratch_bytes_[s] ? static_cast<char*>(dv.arena) + scratch_offset_[d][s] : nullptr;
-      ctx[d].workspace_bytes = scratch_bytes_[s];
-      ctx[d].shard = d;
-      ctx[d].num_shards = D;
-      for (TensorId t : n.inputs) {
-        Tensor x = local_tensor(t, d);
-        // A replicated intermediate consumed row-wise: view this device's rows.
-        if (view_rows_[nid] && t == n.inputs[0]) {
-          const Shape& full = g_.tensor(t).shape;
-          const std::int64_t E = full.rank() >= 2 ? full.rows() : full.numel();
-          const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
-          const std::int64_t b = E * d / D, e = E * (d + 1) / D;
-          x.data = static_cast<char*>(x.data) + b * inner * static_cast<std::int64_t>(dtype_size(x.dtype));
-          x.shape = full.rank() >= 2 ? Shape{e - b, inner} : Shape{e - b};
-        }
-        ins[d].push_back(x);
-      }
-      for (TensorId t : n.outputs) outs[d].push_back(local_tensor(t, d));
-      // Range shards of a full reduce: global index of this device's first element.
-      if (!n.inputs.empty()) {
-        const TensorPlan& tp = tplan_[n.inputs[0]];
-        const Shape& full = g_.tensor(n.inputs[0]).shape;
-        const std::int64_t inner = full.rank() >= 2 ? full.cols() : 1;
-        if (tp.placement == Placement::kRowSplit || view_rows_[nid])
-          ctx[d].index_base = (full.rank() >= 2 ? full.rows() : full.numel()) * d / D * inner;
-      }
-      if (exchange_offset_[d][nid] >= 0) ctx[d].exchange = static_cast<char*>(dv.arena) + exchange_offset_[d][nid];
-      if (impl_->p2p && !impl_->p2p_table.empty() && impl_->p2p_table[nid][d])
-        ctx[d].p2p_peers = static_cast<void* const*>(impl_->p2p_table[nid][d]);
-    }
+    auto& L = impl_->launches[nid];
+    const std::vector<OpContext>& ctx = L.ctx;
+    const auto& ins = L.ins;
+    const auto& outs = L.outs;
+    for (int d = 0; d < D; ++d)
+      for (int p : waits_[nid]) MCKE_RETURN_IF_ERROR(impl_->devs[d].streams[s].wait(impl_->devs[d].node_events[p]));
     for (int d = 0; d < D; ++d) {
       rt::DeviceGuard g(impl_->devs[d].device);
       const Status st = n.op->launch(ctx[d], ins[d], outs[d]);
@@ -657,8 +763,7 @@ Status GraphExecutor::enqueue(bool capturing) {
     }
     const std::size_t eb = n.op->exchange_bytes();
     if (eb > 0 && !(impl_->p2p && D > 1)) {
-      std::vector<void*> gathered(D);
-      for (int d = 0; d < D; ++d) gathered[d] = static_cast<char*>(ctx[d].exchange) + eb;
+      const std::vector<void*>& gathered = L.gathered;
       if (D > 1 && impl_->peer_copy) {
         // Every shard's partial lands in every device's gathered buffer, in
         // shard order; each copy waits on the event recorded after the partial.
@@ -694,8 +799,6 @@ Status GraphExecutor::enqueue(bool capturing) {
                                            "ncclAllGather"));
         }
         MCKE_RETURN_IF_ERROR(nccl_status(ncclGroupEnd(), "ncclGroupEnd"));
-      } else {
-        gathered[0] = ctx[0].exchange;
       }
       for (int d = 0; d < D; ++d) {
         rt::DeviceGuard g(impl_->devs[d].device);
@@ -744,6 +847,12 @@ Status GraphExecutor::set_input(TensorId t, const void* host, std::size_t bytes)
   const std::size_t es = dtype_size(desc.dtype);
   if (bytes != static_cast<std::size_t>(desc.shape.numel()) * es)
     return InvalidArgumentError("set_input: expected " + std::to_string(desc.shape.numel() * es) + " bytes");
+  if (opts_.validate_numerics) {
+    const char* h = static_cast<const char*>(host);
+    auto it = std::find_if(input_cache_.begin(), input_cache_.end(), [&](const auto& e) { return e.first == t; });
+    if (it == input_cache_.end()) input_cache_.push_back({t, std::vector<char>(h, h + bytes)});
+    else it->second.assign(h, h + bytes);
+  }
   const TensorPlan& tp = tplan_[t];
   for (int d = 0; d < num_devices(); ++d) {
     rt::DeviceGuard g(impl_->devs[d].device);
@@ -796,12 +905,115 @@ Status GraphExecutor::copy_output_to_host(TensorId t, void* host, std::size_t by
   return OkStatus();
 }
 
+// ------------------------------------------------------------- numerics gate
+
+namespace {
+const char* schedule_name(SchedulePolicy p) {
+  switch (p) {
+    case SchedulePolicy::kSequential: return "sequential";
+    case SchedulePolicy::kLevelParallel: return "level-parallel";
+    case SchedulePolicy::kChainGreedy: return "chain-greedy";
+  }
+  return "?";
+}
+const char* memory_name(MemoryPolicy p) {
+  switch (p) {
+    case MemoryPolicy::kAllocPerTensor: return "alloc-per-tensor";
+    case MemoryPolicy::kReuseTopoNaive: return "reuse-topo-naive";
+    case MemoryPolicy::kReuseSameStream: return "reuse-same-stream";
+    case MemoryPolicy::kReuseHappensBefore: return "reuse-happens-before";
+  }
+  return "?";
+}
+std::string hex32(const std::vector<char>& v, std::size_t word) {
+  std::uint32_t u = 0;
+  std::memcpy(&u, v.data() + word * 4, std::min<std::size_t>(4, v.size() - word * 4));
+  char buf[16];
+  std::snprintf(buf, sizeof(buf), "0x%08x", u);
+  return buf;
+}
+}  // namespace
+
+StatusOr<NumericsResult> GraphExecutor::validate_numerics(int repeats) {
+  if (!opts_.validate_numerics)
+    return FailedPreconditionError("validate_numerics: needs ExecutorOptions::validate_numerics (set_input keeps "
+                                   "host copies of the inputs only then)");
+  if (repeats < 1) repeats = 1;
+  for (TensorId t = 0; t < g_.num_tensors(); ++t)
+    if (g_.is_input(t) && std::none_of(input_cache_.begin(), input_cache_.end(), [&](const auto& e) { return e.first == t; }))
+      return FailedPreconditionError("validate_numerics: input '" + g_.tensor(t).name + "' was never set");
+  struct Config {
+    SchedulePolicy schedule;
+    MemoryPolicy memory;
+    bool graph;
+  };
+  std::vector<Config> configs{{SchedulePolicy::kSequential, MemoryPolicy::kAllocPerTensor, false}};  // golden
+  for (SchedulePolicy sp : {SchedulePolicy::kSequential, SchedulePolicy::kLevelParallel, SchedulePolicy::kChainGreedy})
+    for (MemoryPolicy mp : {MemoryPolicy::kAllocPerTensor, MemoryPolicy::kReuseSameStream, MemoryPolicy::kReuseHappensBefore})
+      for (bool gr : {false, true})
+        if (sp != SchedulePolicy::kSequential || mp != MemoryPolicy::kAllocPerTensor || gr)
+          configs.push_back({sp, mp, gr});
+  NumericsResult res;
+  res.repeats = repeats;
+  const auto& outs = g_.outputs();
+  std::vector<std::vector<char>> golden;
+  for (std::size_t ci = 0; ci < configs.size(); ++ci) {
+    const Config& c = configs[ci];
+    const std::string cname = std::string(schedule_name(c.schedule)) + "/" + memory_name(c.memory) + "/" +
+                              (c.graph ? "graph" : "eager");
+    ExecutorOptions o = opts_;
+    o.schedule = c.schedule;
+    o.memory = c.memory;
+    o.use_graph = c.graph;
+    o.validate_numerics = false;
+    GraphExecutor ex(g_, o);
+    const Status ps = ex.plan();
+    if (!ps.ok()) return Status(ps.code(), "validate_numerics [" + cname + "] plan: " + ps.message());
+    for (const auto& [t, bytes] : input_cache_) MCKE_RETURN_IF_ERROR(ex.set_input(t, bytes.data(), bytes.size()));
+    std::vector<std::vector<char>> first;
+    for (int r = 0; r < repeats; ++r) {
+      MCKE_RETURN_IF_ERROR(ex.run_async());
+      MCKE_RETURN_IF_ERROR(ex.synchronize());
+      for (std::size_t oi = 0; oi < outs.size(); ++oi) {
+        const TensorDesc& d = g_.tensor(outs[oi]);
+        std::vector<char> buf(static_cast<std::size_t>(d.shape.numel()) * dtype_size(d.dtype));
+        MCKE_RETURN_IF_ERROR(ex.copy_output_to_host(outs[oi], buf.data(), buf.size()));
+        const std::vector<char>* want = nullptr;
+        const char* against = nullptr;
+        if (r == 0 && ci > 0) {
+          want = &golden[oi];
+          against = "the golden run (sequential/alloc-per-tensor/eager)";
+        } else if (r > 0) {
+          want = &first[oi];
+          against = "its own first run";
+        }
+        if (want) {
+          const std::size_t w = first_bit_mismatch(buf.data(), want->data(), buf.size());
+          res.elements_compared += buf.size() / 4;
+          if (w != buf.size()) {
+            res.passed = false;
+            res.configs_compared = static_cast<int>(ci);
+            res.detail = "[" + cname + "] run " + std::to_string(r) + ", output '" + d.name + "', word " +
+                         std::to_string(w) + ": " + hex32(buf, w) + " against " + hex32(*want, w) + " in " + against;
+            return res;
+          }
+        }
+        if (r == 0) first.push_back(std::move(buf));
+      }
+    }
+    if (ci == 0) golden = first;
+  }
+  res.passed = true;
+  res.configs_compared = static_cast<int>(configs.size());
+  return res;
+}
+
 std::string GraphExecutor::describe() const {
   // Plain string building (no iostreams): this library is loaded next to other
   // C++ runtimes in one process, and the description must not depend on their
   // stream machinery.
   std::string s = "devices=" + std::to_string(num_devices()) +
-                  " streams_per_device=" + std::to_string(opts_.streams_per_device) +
+                  " num_streams=" + std::to_string(opts_.num_streams) +
                   " cross_stream_events=" + std::to_string(event_edges_) + "\n";
   for (NodeId nid : g_.topo_order()) {
     const Node& n = g_.node(nid);

@@ -59,6 +59,10 @@ def lib() -> ctypes.CDLL:
             "mcke_executor_arena_bytes": (i32, [vp, i32, ctypes.POINTER(ctypes.c_size_t)]),
             "mcke_executor_num_events": (i32, [vp, ctypes.POINTER(ctypes.c_size_t)]),
             "mcke_executor_last_run_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float)]),
+            "mcke_executor_create_policy": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32, ctypes.c_uint, i32, i32]),
+            "mcke_executor_validate_numerics": (i32, [vp, i32, ctypes.POINTER(ctypes.c_int),
+                                                      ctypes.POINTER(ctypes.c_int), ctypes.c_char_p, sz]),
+            "mcke_executor_alloc_stats": (i32, [vp, i32, ctypes.POINTER(AllocStats)]),
         }
         for name, (res, args) in sigs.items():
             fn = getattr(l, name)
@@ -70,6 +74,16 @@ def lib() -> ctypes.CDLL:
 def _check(rc: int) -> None:
     if rc != 0:
         raise MckeError(rc, lib().mcke_host_last_error_string().decode())
+
+
+class AllocStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("alloc_calls", "free_calls", "raw_malloc_calls", "raw_free_calls",
+                                               "bytes_reserved", "bytes_in_use", "bytes_requested",
+                                               "peak_bytes_in_use")] + [("name", ctypes.c_char * 24)]
+
+
+SCHEDULE = {"sequential": 0, "level_parallel": 1, "chain_greedy": 2}
+MEMORY = {"alloc_per_tensor": 0, "reuse_same_stream": 2, "reuse_happens_before": 3}
 
 
 class Graph:
@@ -139,13 +153,33 @@ class Executor:
     """mcke::GraphExecutor over the given CUDA device ordinals."""
 
     def __init__(self, graph: Graph, devices=(0,), streams_per_device: int = 4, cuda_graph: bool = False,
-                 poison: bool = False, nccl_exchange: bool = False):
+                 poison: bool = False, nccl_exchange: bool = False, buddy: bool = False, validate: bool = False,
+                 schedule: str = "chain_greedy", memory: str = "reuse_happens_before"):
+        """buddy: each device's arena comes from a BuddyAllocator of that device
+        (the reference's DeviceAllocator interface); validate: keep host copies of
+        the inputs for validate_numerics()."""
         self.graph = graph
         devs = (ctypes.c_int * len(devices))(*devices)
-        flags = (1 if cuda_graph else 0) | (2 if poison else 0) | (4 if nccl_exchange else 0)
-        self._h = lib().mcke_executor_create_ex(graph._h, devs, len(devices), streams_per_device, flags)
+        flags = ((1 if cuda_graph else 0) | (2 if poison else 0) | (4 if nccl_exchange else 0) |
+                 (8 if buddy else 0) | (16 if validate else 0))
+        self._h = lib().mcke_executor_create_policy(graph._h, devs, len(devices), streams_per_device, flags,
+                                                    SCHEDULE[schedule], MEMORY[memory])
         if not self._h:
             raise MckeError(2, "mcke_executor_create failed")
+
+    def validate_numerics(self, repeats: int = 3) -> dict:
+        ok, n = ctypes.c_int(), ctypes.c_int()
+        buf = ctypes.create_string_buffer(4096)
+        _check(lib().mcke_executor_validate_numerics(self._h, repeats, ctypes.byref(ok), ctypes.byref(n), buf,
+                                                     len(buf)))
+        return {"passed": bool(ok.value), "configs": n.value, "detail": buf.value.decode()}
+
+    def alloc_stats(self, device_index: int = 0) -> dict:
+        st = AllocStats()
+        _check(lib().mcke_executor_alloc_stats(self._h, device_index, ctypes.byref(st)))
+        d = {n: getattr(st, n) for n, _ in AllocStats._fields_ if n != "name"}
+        d["name"] = st.name.decode()
+        return d
 
     def __del__(self):
         h, self._h = getattr(self, "_h", None), None

@@ -1020,6 +1020,10 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         kms = ms / steps
         loc_flops = 2 * GEMM_N * GEMM_N * (n1 - n0)
         ach = loc_flops / (kms * 1e-3) / 1e12
+        # the reference's launch_gemm_f32 call (AUTO): the same 3xTF32 MMAs with
+        # the hi/lo split inside the GEMM kernel, no workspace
+        ms_auto = timed_back_to_back(torch, dist, lambda i: mcke.gemm(a, b, c), steps, warm)
+        checked_auto = check_gemm(torch, a, b, c, rel=1e-6, seed=r + 100)
         fs = max(2, min(steps, 3))
         ms_s, per_s = timed_steps(torch, dist, lambda: mcke.gemm(a, b, c, variant="simt"), fs, 1, None)
         # Library ceilings on the same shard, measured here as denominators:
@@ -1038,6 +1042,11 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "kernel_ms": round(kms, 3), "checked": checked,
             "path": "3xTF32 on tcgen05 (split pass + kind::tf32 MMAs, fp32 partial sums promoted every 128 k)",
+            "launch_gemm_f32_auto": {"value": round(GEMM_FLOPS * steps / (ms_auto * 1e-3) / 1e12, 1),
+                                     "unit": "TFLOP/s", "kernel_ms": round(ms_auto / steps, 3),
+                                     "checked": checked_auto, "workspace_bytes": 0,
+                                     "path": "mcke_sm100_gemm_f32 AUTO: hi/lo split of each smem tile by the "
+                                             "epilogue warps inside the tcgen05 kernel"},
             "tf32_mma_tflops": round(3 * ach, 1),
             "frac_of_tf32_nominal": round(3 * ach / TF32_NOMINAL_TFLOPS, 4),
             "cublas_tf32_one_pass_tflops_per_gpu": round(cublas_tf32, 1),
@@ -1103,6 +1112,12 @@ def run_profile(args) -> None:
             c = torch.empty(n, n, device=dev)
             ws = torch.empty(mcke.gemm_f32_tc_workspace_bytes(n, n, n), dtype=torch.uint8, device=dev)
             fn = lambda: mcke.gemm_f32_tc(a, b, c, workspace=ws)  # noqa: E731
+        elif name == "gemm_f32_split":
+            n = 4096
+            a = torch.rand(n, n, generator=gen, device=dev) * 2 - 1
+            b = torch.rand(n, n, generator=gen, device=dev) * 2 - 1
+            c = torch.empty(n, n, device=dev)
+            fn = lambda: mcke.gemm_f32_tc(a, b, c, in_kernel_split=True)  # noqa: E731
         elif name == "gemm_f32_ffma":
             n = 4096
             a = torch.rand(n, n, generator=gen, device=dev) * 2 - 1

@@ -59,7 +59,11 @@ typedef enum { MCKE_SOFTMAX_THREE_PASS = 0, MCKE_SOFTMAX_ONLINE = 1 } mcke_softm
  * include/mcke/kernels/gemm_tile.hpp:209 GemmVariant; its kernels are replaced,
  * so its values are not reused).  AUTO picks TCGEN05 for bf16 when the shape
  * meets the TMA rules (K % 8 == 0, N % 8 == 0, 16-byte aligned A and B),
- * else SIMT; for f32 it picks SIMT. */
+ * else SIMT.  For f32 operands and an f32 output AUTO picks the tensor cores
+ * in the 3xTF32 form with the hi/lo split inside the GEMM kernel (no
+ * workspace; fp32-level accuracy, not bit-identical to an FFMA loop) when
+ * K % 4 == 0, N % 4 == 0 and A and B are 16-byte aligned, else SIMT; SIMT
+ * always takes the FFMA kernel. */
 /* TCGEN05_WIDE / TCGEN05_NARROW: the tcgen05 kernel with its pair tile forced
  * to 256 x 512 / 256 x 256, one tile per CTA pair at a time (AUTO and TCGEN05
  * choose; shapes that cannot use the pair tile ignore the choice).  The two
@@ -250,19 +254,23 @@ int mcke_sm100_reduce_full_f32_noalloc(const float* x, int64_t n, mcke_reduce_re
 /* ---- GEMM: C[M,N] = alpha * A[M,K] @ B[K,N] + beta * C, row-major -------- */
 
 /* Replaces kernels.hpp:265 launch_gemm_f32 (kernels/gemm.cu:829).  beta == 0
- * never reads C; k == 0 writes beta * C.  variant: AUTO or SIMT. */
+ * never reads C; k == 0 writes beta * C.  variant: AUTO (tensor cores where
+ * the shape allows, see above) or SIMT. */
 int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int64_t n,
                         int64_t k, float alpha, float beta, int variant, mcke_stream_t stream);
 /* New: float32 GEMM on the tensor cores (3xTF32): A and B are each split into
- * hi (low 13 mantissa bits cleared) and lo = x - hi parts in `workspace`, and
- * the tcgen05 kernel accumulates A_hi*B_lo + A_lo*B_hi + A_hi*B_hi in fp32 --
- * fp32-level accuracy (relative error ~1e-6, not bit-identical to an FFMA loop)
- * at tensor-core speed.  c = act(alpha * A@B + beta * C + bias[col]), float32;
- * bias may be NULL.  Needs K % 4 == 0, N % 4 == 0, 16-byte aligned A and B and
- * mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k) bytes of 256-byte aligned
- * workspace (8 * (M*K + K*N) bytes, rounded); other shapes are rejected (use
- * mcke_sm100_gemm_f32).  Same contract as launch_gemm_f32 (kernels.hpp:265)
- * otherwise: beta == 0 never reads C, k == 0 writes act(beta * C + bias). */
+ * hi (low 13 mantissa bits cleared) and lo = x - hi parts, and the tcgen05
+ * kernel accumulates A_hi*B_lo + A_lo*B_hi + A_hi*B_hi in fp32 -- fp32-level
+ * accuracy (relative error ~1e-6, not bit-identical to an FFMA loop) at
+ * tensor-core speed.  c = act(alpha * A@B + beta * C + bias[col]), float32;
+ * bias may be NULL.  Needs K % 4 == 0, N % 4 == 0 and 16-byte aligned A and B;
+ * other shapes are rejected (use mcke_sm100_gemm_f32).  With a workspace of
+ * mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k) bytes (256-byte aligned;
+ * 8 * (M*K + K*N), rounded) two split passes write the parts there first; with
+ * workspace = NULL and workspace_bytes = 0 the GEMM kernel splits its tiles in
+ * shared memory itself (the same bits, no workspace, ~10% slower at 8192^3).
+ * Same contract as launch_gemm_f32 (kernels.hpp:265) otherwise: beta == 0
+ * never reads C, k == 0 writes act(beta * C + bias). */
 size_t mcke_sm100_gemm_f32_tc_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int mcke_sm100_gemm_f32_tc(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
                            float alpha, float beta, const float* bias, int act, void* workspace,

@@ -113,9 +113,17 @@ int gemm_front(const char* who, const void* a, const void* b, void* c, int64_t m
                 "%s: the tcgen05 kernel needs k > 0, K %% 8 == 0, N %% 8 == 0 and 16-byte aligned "
                 "A and B (TMA); no fallback is applied",
                 who);
+  // fp32 operands, AUTO: the tensor cores in the 3xTF32 form with the hi/lo
+  // split inside the kernel (fp32-level accuracy, no workspace) wherever TMA
+  // can describe A and B; SIMT (the FFMA kernel) otherwise or when asked for.
+  const bool tf32_ok = !bf16_in && !out_bf16 && variant == MCKE_GEMM_AUTO && k > 0 && k % 4 == 0 && n % 4 == 0 &&
+                       aligned(a, 16) && aligned(b, 16);
   if (tc_ok && variant != MCKE_GEMM_SIMT) {
     MCKE_RETURN_IF(launch_gemm_tcgen05(static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b),
                                        c, m, n, k, ep, s, nullptr, nullptr, tile));
+  } else if (tf32_ok) {
+    MCKE_RETURN_IF(launch_gemm_tf32x3_split(static_cast<const float*>(a), static_cast<const float*>(b),
+                                            static_cast<float*>(c), m, n, k, ep, s, nullptr, nullptr));
   } else {
     MCKE_RETURN_IF(launch_gemm_simt(a, b, c, m, n, k, bf16_in, ep, s, nullptr));
   }
@@ -141,9 +149,9 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site != 0) {
     static const char* const kWhere[] = {"", "producer: free stage", "mma: loaded stage", "mma: free accumulator",
                                          "epilogue: full accumulator", "drain", "split-k: previous contributor's flag",
-                                         "epilogue warps' meeting"};
+                                         "epilogue warps' meeting", "split of a stage's raw tiles"};
     return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u, %s); the kernel stopped early",
-                site, site < 8 ? kWhere[site] : "unknown");
+                site, site < 9 ? kWhere[site] : "unknown");
   }
   MCKE_RETURN_IF(read_reduce_watchdog(&site));
   if (site == 2)
@@ -201,6 +209,10 @@ extern "C" int mcke_sm100_gemm_f32_tc(const float* a, const float* b, float* c, 
     return fail(MCKE_INVALID_ARGUMENT,
                 "%s: needs K %% 4 == 0, N %% 4 == 0 and 16-byte aligned A and B (TMA rows); no fallback is applied",
                 who);
+  if (!workspace && workspace_bytes == 0) {  // split inside the GEMM kernel
+    MCKE_RETURN_IF(launch_gemm_tf32x3_split(a, b, c, m, n, k, ep, s, nullptr, nullptr));
+    return check_launch(who);
+  }
   const size_t need = gemm_tf32x3_workspace_bytes(m, n, k);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(MCKE_INVALID_ARGUMENT,

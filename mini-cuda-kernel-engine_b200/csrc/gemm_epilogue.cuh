@@ -87,5 +87,8 @@ std::size_t gemm_tf32x3_workspace_bytes(int64_t m, int64_t n, int64_t k);
 int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
                        const EpilogueParams& ep, void* workspace, cudaStream_t s, const void** kernel_out,
                        std::size_t* smem_out);
+// The same product with the hi/lo split inside the GEMM kernel (no workspace).
+int launch_gemm_tf32x3_split(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                             const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out);
 
 }  // namespace mcke_sm100

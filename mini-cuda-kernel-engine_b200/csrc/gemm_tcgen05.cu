@@ -36,20 +36,27 @@
 // a pair always meet at the final cluster barrier.
 //
 // fp32 operands (kTf32 = true) take the same template through .kind::tf32 in
-// the 3xTF32 form: each operand is split beforehand into hi = its value with
-// the low 13 mantissa bits cleared (exact in tf32) and lo = value - hi, and
-// every k-step issues A_hi*B_lo + A_lo*B_hi + A_hi*B_hi into the fp32
-// accumulator, which recovers fp32-level accuracy (the dropped lo*lo term and
-// the tf32 rounding of lo are ~2^-22 relative).  Rows of 128 bytes hold 32
-// fp32 values, so a k-block is 32 deep and an MMA step 8 deep; a stage holds
-// A, B, A_lo and B_lo (64 KB per CTA in the pair shape, 3 stages).  B is fed
-// K-major (the split pass writes B^T): on this part an N-major B operand of
-// .kind::tf32 accumulated nothing (measured with all-ones operands, where the
-// same descriptors with .kind::f16 give the right sum), so only K-major is used.
+// the 3xTF32 form: each operand is split into hi = its value with the low 13
+// mantissa bits cleared (exact in tf32) and lo = value - hi, and every k-step
+// issues A_hi*B_lo + A_lo*B_hi + A_hi*B_hi into the fp32 accumulator, which
+// recovers fp32-level accuracy (the dropped lo*lo term and the tf32 rounding
+// of lo are ~2^-22 relative).  Rows of 128 bytes hold 32 fp32 values, so a
+// k-block is 32 deep and an MMA step 8 deep; a stage holds A, B, A_lo and
+// B_lo (64 KB per CTA in the pair shape, 3 stages).  Two ways to split:
+//   * kSplit = false: a split pass writes hi and lo of A and of B^T into a
+//     caller workspace beforehand, and B is fed K-major;
+//   * kSplit = true: TMA loads the raw fp32 tiles -- A K-major, B N-major as
+//     stored in SWIZZLE_128B_BASE32B (128-byte rows of 32 floats whose 32-byte
+//     chunks are permuted by (row & 3), the layout an MN-major 32-bit operand
+//     needs; with the plain 128-byte swizzle an N-major tf32 B accumulated
+//     nothing) -- and the epilogue warps split each stage in shared memory
+//     (below) before the MMA reads it.  No workspace and no extra passes over
+//     A and B; the two give the same bits.
 //
 // Tensor-memory and descriptor encodings follow the PTX ISA for tcgen05
 // (instruction descriptor for .kind::f16 / .kind::tf32, shared-memory matrix
-// descriptor with version 1 and SWIZZLE_128B), written out by hand below.
+// descriptor with version 1 and SWIZZLE_128B or SWIZZLE_128B_BASE32B), written
+// out by hand below.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -67,9 +74,10 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // 320
 constexpr int kGroupM = 16;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 
-template <bool kPair, bool kTf32 = false, bool kWide = false>
+template <bool kPair, bool kTf32 = false, bool kWide = false, bool kSplit = false>
 struct Cfg {
   static_assert(!kWide || (kPair && !kTf32), "the wide tile is a bf16 pair shape");
+  static_assert(!kSplit || kTf32, "the in-kernel hi/lo split is a 3xTF32 shape");
   static constexpr int ELEM = kTf32 ? 4 : 2;          // operand bytes
   static constexpr int BK = 128 / ELEM;               // k-block: one 128-byte swizzle row
   static constexpr int UMMA_K = 32 / ELEM;            // k per MMA: 32 bytes of a row
@@ -92,9 +100,13 @@ struct Cfg {
   // k-blocks per tensor-memory accumulation unit: tf32 partial sums are moved
   // to registers every PROMOTE k-blocks (128 k); bf16 accumulates a whole tile.
   static constexpr int PROMOTE = kTf32 ? 4 : 0;
-  static constexpr int TX = kPair ? 2 * STAGE : STAGE;  // bytes landing on the leader's full barrier
+  // bytes landing on a full barrier: the leader's, for both CTAs' loads of a
+  // stage; with kSplit each CTA's own, for its raw A and B tiles
+  static constexpr int TX = kSplit ? (A_STAGE + B_STAGE) : (kPair ? 2 * STAGE : STAGE);
   static constexpr int EPI_ARRIVALS = kPair ? 2 * kEpiWarps : kEpiWarps;
-  static constexpr int NUM_BARS = 2 * STAGES + 6;
+  // kSplit: one "converted" barrier per stage, on the leader, one arrival per
+  // epilogue warp of either CTA
+  static constexpr int NUM_BARS = (kSplit ? 3 : 2) * STAGES + 6;
   // bf16 operands: one 32-row x 128-byte output box per epilogue warp, staged
   // for a TMA store (SWIZZLE_128B, 1024-byte aligned after the stages).
   static constexpr int EPI_BOX_BYTES = 32 * 128;
@@ -105,7 +117,9 @@ struct Cfg {
   // B N-major (bit 16 = 1; bf16) or K-major (0; tf32), N >> 3 at bits 17-22,
   // M >> 4 at bits 24-28.
   static constexpr uint32_t FMT = kTf32 ? 2u : 1u;
-  static constexpr uint32_t B_MN_MAJOR = kTf32 ? 0u : 1u;  // tf32: B^T, K-major
+  // bf16: B N-major; tf32 with a split pass: B^T, K-major; tf32 split in the
+  // kernel: B as stored, N-major (rows of 32 floats, 128B_BASE32B swizzle)
+  static constexpr uint32_t B_MN_MAJOR = kTf32 ? (kSplit ? 1u : 0u) : 1u;
   static constexpr uint32_t IDESC = (1u << 4) | (FMT << 7) | (FMT << 10) | (0u << 15) | (B_MN_MAJOR << 16) |
                                     (static_cast<uint32_t>(MMA_N >> 3) << 17) |
                                     (static_cast<uint32_t>(TILE_M >> 4) << 24);
@@ -115,6 +129,14 @@ static_assert(Cfg<false>::SMEM <= 232448 && Cfg<true>::SMEM <= 232448, "shared m
 static_assert(Cfg<false, true>::SMEM <= 232448 && Cfg<true, true>::SMEM <= 232448, "shared memory budget");
 static_assert(Cfg<true, false, true>::SMEM <= 232448, "shared memory budget");
 static_assert(Cfg<true, true>::B_STAGE % 1024 == 0 && Cfg<false, true>::A_STAGE % 1024 == 0, "stage alignment");
+static_assert(Cfg<true, true, false, true>::SMEM <= 232448 && Cfg<false, true, false, true>::SMEM <= 232448,
+              "shared memory budget");
+static_assert(Cfg<true, true, false, true>::A_STAGE % 1024 == 0 && Cfg<true, true, false, true>::B_STAGE % 1024 == 0 &&
+                  Cfg<false, true, false, true>::B_STAGE % 1024 == 0,
+              "stage alignment");
+static_assert(Cfg<true, true, false, true>::STAGES <= Cfg<true, true, false, true>::PROMOTE &&
+                  Cfg<false, true, false, true>::STAGES <= Cfg<false, true, false, true>::PROMOTE,
+              "the split runs at most one accumulation unit ahead");
 
 // Sites reported through the watchdog word (1-based).
 enum : uint32_t {
@@ -125,6 +147,7 @@ enum : uint32_t {
   kSiteDrain = 5,
   kSiteSplitFlag = 6,  // a split-k tile's flag from the previous contributor
   kSiteEpiMeet = 7,    // the epilogue warps' meeting on their mbarrier
+  kSiteConvert = 8,    // 3xTF32 split in the kernel: a stage's raw tiles
   kSiteSelfTest = 9    // mcke_sm100_watchdog_selftest only
 };
 
@@ -345,17 +368,19 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // Shared-memory matrix descriptor (tcgen05): start, leading and stride byte
-// offsets in 16-byte units, version 1 at bit 46, layout SWIZZLE_128B (2) at
-// bits 61-63, base offset 0 (every stage starts on a 1024-byte boundary).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// offsets in 16-byte units, version 1 at bit 46, the layout at bits 61-63 --
+// SWIZZLE_128B (2), or SWIZZLE_128B_BASE32B (1): 128-byte rows whose 32-byte
+// chunks are permuted by (row & 3), the layout an MN-major 32-bit operand
+// needs -- base offset 0 (every stage starts on a 1024-byte boundary).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint64_t layout = 2) {
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
          (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
-         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (layout << 61);
 }
 
-template <bool kPair, bool kTf32>
+template <bool kPair, bool kTf32, bool kSplit = false>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  constexpr uint32_t idesc = Cfg<kPair, kTf32>::IDESC;
+  constexpr uint32_t idesc = Cfg<kPair, kTf32, false, kSplit>::IDESC;
   if constexpr (kPair && kTf32) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -578,14 +603,14 @@ __device__ __forceinline__ void epi_chunk(const EpilogueParams& ep, void* c, int
 
 // ---- the kernel -------------------------------------------------------------------
 
-template <bool kPair, bool kTf32, bool kWide, bool kBf16Out, bool kBias, int kAct>
+template <bool kPair, bool kTf32, bool kWide, bool kBf16Out, bool kBias, int kAct, bool kSplit = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_alo, const __grid_constant__ CUtensorMap tmap_blo,
                         const __grid_constant__ CUtensorMap tmap_c, void* __restrict__ c, int M, int N, int K,
                         EpilogueParams ep, int fast, SplitK sk) {
   pdl_entry();
-  using C = Cfg<kPair, kTf32, kWide>;
+  using C = Cfg<kPair, kTf32, kWide, kSplit>;
   constexpr int BK = C::BK;
   constexpr int UMMA_K = C::UMMA_K;
   extern __shared__ uint8_t smem_raw[];
@@ -608,6 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
   const uint32_t drain_bar = bar0 + 8u * (2 * C::STAGES + 4);
   const uint32_t epi_bar = bar0 + 8u * (2 * C::STAGES + 5);  // the eight epilogue warps
+  auto conv_bar = [&](int s) { return bar0 + 8u * (2 * C::STAGES + 6 + s); };  // kSplit only
 
   const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
   const int lane = threadIdx.x & 31;
@@ -626,6 +652,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain_bar, 1);
     mbar_init(epi_bar, kEpiWarps);
+    if constexpr (kSplit)
+      for (int s = 0; s < C::STAGES; ++s) {
+        mbar_init(conv_bar(s), C::EPI_ARRIVALS);
+      }
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_a)) : "memory");
@@ -671,6 +701,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint32_t fb = full_bar(stage);
+          if constexpr (kSplit) {
+            // raw fp32 tiles onto this CTA's own barrier (its epilogue warps
+            // split them before the leader's MMA reads them): A K-major, B as
+            // stored, B_COLS / 32 boxes of 32 columns x 32 k
+            mbar_expect_tx(fb, C::TX);
+            tma_load_2d<false>(smem_u32(sA(stage)), &tmap_a, fb, kb * BK, row0);
+#pragma unroll
+            for (int j = 0; j < C::B_COLS / C::BOX_COLS; ++j)
+              tma_load_2d<false>(smem_u32(sB(stage) + j * C::B_BOX_BYTES), &tmap_b, fb, col0 + C::BOX_COLS * j, kb * BK);
+            issued_mask |= 1u << stage;
+            parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+            if (++stage == C::STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
+          }
           if (leader) mbar_expect_tx(fb, C::TX);
           if constexpr (kPair) fb = map_to_rank(fb, 0);
           tma_load_2d<kPair>(smem_u32(sA(stage)), &tmap_a, fb, kb * BK, row0);
@@ -698,9 +745,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok && leader) {
+      if (!ok && (leader || kSplit)) {
         // Do not leave with bulk copies still landing (their bytes complete
-        // on the leader's full barriers).
+        // on the leader's full barriers; with kSplit on this CTA's own).
         for (int s = 0; s < C::STAGES; ++s)
           if (issued_mask & (1u << s))
             wait_bounded(full_bar(s), (parity_mask >> s) & 1u, abort_flag, kSiteDrain, false);
@@ -731,7 +778,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * C::BN);
           const int kb1 = min(kb0 + unit_kb, sg.kb1);
           for (int kb = kb0; kb < kb1; ++kb) {
-            if (!wait_bounded(full_bar(stage), phase, abort_flag, kSiteMmaFull, true)) {
+            // kSplit: both CTAs' epilogue warps have split the stage
+            if (!wait_bounded(kSplit ? conv_bar(stage) : full_bar(stage), phase, abort_flag, kSiteMmaFull, true)) {
               ok = false;
               break;
             }
@@ -743,7 +791,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
               // A: K-major SW128, +32 bytes per step; SBO = 8 rows x 128 B.
               const uint64_t adesc = smem_desc(a_base + k * 32, 16, 1024);
-              if constexpr (kTf32) {
+              if constexpr (kSplit) {
+                // B as stored, N-major with the 128B_BASE32B swizzle: +8 k-rows
+                // x 128 B per step; LBO = one 32-column box (32 k-rows x 128 B),
+                // SBO = 4 k-rows x 128 B (one swizzle atom).  A_hi*B_lo,
+                // A_lo*B_hi, then A_hi*B_hi.
+                const uint64_t bdesc = smem_desc(b_base + k * 1024, C::B_BOX_BYTES, 512, 1);
+                const uint64_t aldesc = smem_desc(smem_u32(sAlo(stage)) + k * 32, 16, 1024);
+                const uint64_t bldesc = smem_desc(smem_u32(sBlo(stage)) + k * 1024, C::B_BOX_BYTES, 512, 1);
+                umma<kPair, true, true>(d_tmem, adesc, bldesc, accum);
+                umma<kPair, true, true>(d_tmem, aldesc, bdesc, 1u);
+                umma<kPair, true, true>(d_tmem, adesc, bdesc, 1u);
+              } else if constexpr (kTf32) {
                 // B^T: K-major like A.  Small terms first: A_hi*B_lo, A_lo*B_hi,
                 // then A_hi*B_hi.
                 const uint64_t bdesc = smem_desc(b_base + k * 32, 16, 1024);
@@ -817,6 +876,93 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       ++epi_uses;
+    };
+    // kSplit: these warps also split every stage of this CTA into hi (the
+    // value with its low 13 mantissa bits cleared, in place) and lo = value -
+    // hi (into the stage's lo buffers), elementwise at the same offsets, so
+    // the lo tiles have the hi tiles' swizzled layout.  A conversion cursor
+    // walks (segment, k-block) in the producer's order and runs ahead of the
+    // promotions: before waiting for accumulation unit lc the warps have split
+    // every k-block of units <= lc + 1.  (The MMA of unit lc + 1 needs its
+    // k-blocks split and the accumulator that unit lc - 1's promotion freed;
+    // splitting a k-block waits for its stage, which the MMA of a k-block of
+    // unit lc or lc + 1 frees -- STAGES <= PROMOTE -- so nothing waits on
+    // itself.)  Each warp fences its writes for the async proxy and arrives on
+    // the leader's "converted" barrier (CTA-scope release, as a TMA or MMA
+    // completion would).  Measured at 8192^3 on B200 (fp32-equivalent
+    // TFLOP/s): this form 223-241; with a cluster-scope release per arrival
+    // 186 (warps stalled on the fence); with one arrival per CTA after a
+    // local barrier 162; with 16-deep k-blocks and 6 stages 217 (twice the
+    // per-stage synchronisation); with two extra warps doing all the splits
+    // 138.  The split-pass path with a caller workspace: 264-272.
+    SegIter cit(unit, units, num_tiles, kblocks, sk);
+    Seg csg{};
+    bool cvalid = kSplit && cit.next(csg);
+    int ckb = cvalid ? csg.kb0 : 0, cunit = 0, cin = 0, cstage = 0;
+    uint32_t cphase = 0;
+    uint32_t conv_leader0 = conv_bar(0);
+    if constexpr (kPair) conv_leader0 = map_to_rank(conv_leader0, 0);
+    auto convert_stage = [&](int st, uint32_t ph) -> bool {
+      int ok = 1;
+      if (lane == 0) ok = wait_bounded(full_bar(st), ph, abort_flag, kSiteConvert, true) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      mbar_try(full_bar(st), ph);  // every lane observes the completed phase (acquire)
+      const int t = static_cast<int>(threadIdx.x) - 64;  // 0 .. 255 over the eight warps
+      auto split = [](float4* hi, float4* lo) {
+        const float4 v = *hi;
+        float4 h, l;
+        h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);
+        h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);
+        h.z = __uint_as_float(__float_as_uint(v.z) & 0xffffe000u);
+        h.w = __uint_as_float(__float_as_uint(v.w) & 0xffffe000u);
+        l.x = v.x - h.x;
+        l.y = v.y - h.y;
+        l.z = v.z - h.z;
+        l.w = v.w - h.w;
+        *hi = h;
+        *lo = l;
+      };
+      float4* a = reinterpret_cast<float4*>(sA(st)) + t;
+      float4* alo = reinterpret_cast<float4*>(sAlo(st)) + t;
+      float4* b = reinterpret_cast<float4*>(sB(st)) + t;
+      float4* blo = reinterpret_cast<float4*>(sBlo(st)) + t;
+      constexpr int kStride = 32 * kEpiWarps;
+      static_assert(C::A_STAGE % (16 * kStride) == 0 && C::B_STAGE % (16 * kStride) == 0, "whole rounds");
+#pragma unroll
+      for (int j = 0; j < C::A_STAGE / 16 / kStride; ++j) split(a + j * kStride, alo + j * kStride);
+#pragma unroll
+      for (int j = 0; j < C::B_STAGE / 16 / kStride; ++j) split(b + j * kStride, blo + j * kStride);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (kPair) mbar_arrive_cluster(conv_leader0 + 8u * st);
+        else mbar_arrive(conv_bar(st));
+      }
+      return true;
+    };
+    auto convert_through = [&](int upto) -> bool {
+      while (cvalid && cunit <= upto) {
+        if (!convert_stage(cstage, cphase)) return false;
+        if (++cstage == C::STAGES) {
+          cstage = 0;
+          cphase ^= 1u;
+        }
+        ++ckb;
+        if (++cin == C::PROMOTE) {
+          cin = 0;
+          ++cunit;
+        }
+        if (ckb == csg.kb1) {
+          if (cin != 0) {
+            cin = 0;
+            ++cunit;
+          }
+          cvalid = cit.next(csg);
+          if (cvalid) ckb = csg.kb0;
+        }
+      }
+      return true;
     };
     int lc = 0;
     SegIter it(unit, units, num_tiles, kblocks, sk);
@@ -968,6 +1114,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) sum[q][j] = 0.f;
         bool ok = true;
         for (int kb0 = sg.kb0; kb0 < sg.kb1; kb0 += C::PROMOTE, ++lc) {
+          if constexpr (kSplit) {
+            if (!convert_through(lc + 1)) {
+              ok = false;
+              break;
+            }
+          }
           if (!wait_unit(lc)) {
             ok = false;
             break;
@@ -1020,8 +1172,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Row-major [rows, cols] bf16 or fp32 matrix, box {box_cols (inner), box_rows}.
+// Swizzle: 128-byte rows (the default), or 128-byte rows with 32-byte chunks
+// permuted by row (the layout of an MN-major 32-bit MMA operand).
+enum class Sw { k128, k128Atom32 };
 int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
-             uint32_t box_rows, bool fp32 = false) {
+             uint32_t box_rows, bool fp32 = false, Sw sw = Sw::k128) {
   auto fn = encode_fn();
   if (!fn) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[2] = {cols, rows};
@@ -1030,7 +1185,8 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                         const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        sw == Sw::k128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return MCKE_OK;
@@ -1039,22 +1195,23 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
 using KernelFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                           const CUtensorMap, void*, int, int, int, EpilogueParams, int, SplitK);
 
-template <bool kPair, bool kTf32, bool kWide, bool kBf16, bool kBias>
+template <bool kPair, bool kTf32, bool kWide, bool kBf16, bool kBias, bool kSplit = false>
 KernelFn pick_act(int act) {
   switch (act) {
-    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_RELU>;
-    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_ERF>;
-    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_TANH>;
-    default: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_NONE>;
+    case MCKE_ACT_RELU: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_RELU, kSplit>;
+    case MCKE_ACT_GELU_ERF: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_ERF, kSplit>;
+    case MCKE_ACT_GELU_TANH: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_GELU_TANH, kSplit>;
+    default: return gemm_tcgen05_kernel<kPair, kTf32, kWide, kBf16, kBias, MCKE_ACT_NONE, kSplit>;
   }
 }
 
 // bf16 operands: every output type; fp32 operands (3xTF32): fp32 output.
-template <bool kPair, bool kTf32, bool kWide = false>
+template <bool kPair, bool kTf32, bool kWide = false, bool kSplit = false>
 KernelFn pick(bool bf16, bool bias, int act) {
   if constexpr (kTf32) {
     (void)bf16;
-    return bias ? pick_act<kPair, true, false, false, true>(act) : pick_act<kPair, true, false, false, false>(act);
+    return bias ? pick_act<kPair, true, false, false, true, kSplit>(act)
+                : pick_act<kPair, true, false, false, false, kSplit>(act);
   } else {
     if (bf16)
       return bias ? pick_act<kPair, false, kWide, true, true>(act) : pick_act<kPair, false, kWide, true, false>(act);
@@ -1221,7 +1378,7 @@ namespace {
 
 // Common launcher of both operand types: bf16 (a, b) or 3xTF32 (a, b = the hi
 // parts, alo, blo = the lo parts).
-template <bool kTf32>
+template <bool kTf32, bool kSplit = false>
 int launch_tc(const void* a, const void* b, const void* alo, const void* blo, void* c, int64_t m, int64_t n,
               int64_t k, const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out,
               int tile = 0) {
@@ -1255,18 +1412,30 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
       smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
     }
   } else {
-    kfn = pair ? pick<true, kTf32>(ep.out_bf16 != 0, has_bias, ep.act)
-               : pick<false, kTf32>(ep.out_bf16 != 0, has_bias, ep.act);
-    smem = pair ? Cfg<true, kTf32>::SMEM : Cfg<false, kTf32>::SMEM;
+    kfn = pair ? pick<true, kTf32, false, kSplit>(ep.out_bf16 != 0, has_bias, ep.act)
+               : pick<false, kTf32, false, kSplit>(ep.out_bf16 != 0, has_bias, ep.act);
+    smem = pair ? Cfg<true, kTf32, false, kSplit>::SMEM : Cfg<false, kTf32, false, kSplit>::SMEM;
   }
   if (kernel_out) *kernel_out = reinterpret_cast<const void*>(kfn);
   if (smem_out) *smem_out = smem;
   if (m == 0 || n == 0) return MCKE_OK;
   if (!ensure_smem_attr(kfn, smem)) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cannot set shared memory size");
-  using C1 = Cfg<false, kTf32>;
+  using C1 = Cfg<false, kTf32, false, kSplit>;
   CUtensorMap ta, tb, talo, tblo;
-  MCKE_RETURN_IF(make_map(&ta, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), C1::BK, C1::BM, kTf32));
-  if constexpr (kTf32) {
+  if constexpr (kSplit) {
+    // raw A [m, k] as for the split pass (32 k x 128 rows); raw B [k, n] as
+    // stored, boxes of 32 columns x 32 k (the kernel loads its B_COLS columns
+    // as B_COLS / 32 of them) in the 32-byte-atom swizzle
+    MCKE_RETURN_IF(make_map(&ta, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), C1::BK, C1::BM, true));
+    MCKE_RETURN_IF(make_map(&tb, b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), C1::BOX_COLS, C1::BK, true,
+                            Sw::k128Atom32));
+    talo = ta;
+    tblo = tb;
+  } else {
+    MCKE_RETURN_IF(make_map(&ta, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), C1::BK, C1::BM, kTf32));
+  }
+  if constexpr (kSplit) {
+  } else if constexpr (kTf32) {
     // b, blo are B^T [n, k]: boxes of B_COLS rows (pair: 128, single: 256) x 32 k
     const uint32_t bcols = pair ? Cfg<true, true>::B_COLS : Cfg<false, true>::B_COLS;
     MCKE_RETURN_IF(make_map(&tb, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k), C1::BK, bcols, true));
@@ -1410,6 +1579,16 @@ int launch_gemm_tf32x3(const float* a, const float* b, float* c, int64_t m, int6
   if (tgrid.y > 65535u) return fail(MCKE_INVALID_ARGUMENT, "gemm (3xTF32): K too large for the transpose grid");
   launch_async(split_tf32_transpose_kernel, tgrid, 256, 0, s, b, bhi, blo, k, n);
   return launch_tc<true>(ahi, bhi, alo, blo, c, m, n, k, ep, s, kernel_out, smem_out);
+}
+
+// fp32 on the tensor cores with the hi/lo split done inside the GEMM kernel:
+// no workspace, no split passes.  Needs K % 4 == 0 and N % 4 == 0 (TMA row
+// pitches) and 16-byte aligned A and B.
+int launch_gemm_tf32x3_split(const float* a, const float* b, float* c, int64_t m, int64_t n, int64_t k,
+                             const EpilogueParams& ep, cudaStream_t s, const void** kernel_out, std::size_t* smem_out) {
+  if (m == 0 || n == 0 || k == 0)
+    return launch_tc<true, true>(nullptr, nullptr, nullptr, nullptr, c, 0, 0, 0, ep, s, kernel_out, smem_out);
+  return launch_tc<true, true>(a, b, nullptr, nullptr, c, m, n, k, ep, s, kernel_out, smem_out);
 }
 
 // Watchdog self-test: one thread waits on an mbarrier that nothing arrives on.

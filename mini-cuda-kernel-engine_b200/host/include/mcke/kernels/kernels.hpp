@@ -33,7 +33,7 @@ enum class GemmVariant : std::uint8_t {
   kNaive, kTiledSmem, kTiledRegBlock, kWarpTile, kCublasRef,
   kWarpTileNoDbuf, kWarpTileVec4, kNaiveUncoalesced,
   kTcgen05Bf16,
-  kTcgen05Tf32x3,  // new: f32 operands on the tensor cores (3xTF32), needs workspace
+  kTcgen05Tf32x3,  // new: f32 operands on the tensor cores (3xTF32)
 };
 
 // The reference's tile descriptor; validated exactly as the reference does
@@ -93,13 +93,19 @@ struct GemmTile {
 [[nodiscard]] Status launch_row_softmax_f32(const float* x, float* y, std::int64_t rows, std::int64_t cols,
                                            SoftmaxVariant variant, rt::StreamHandle stream);
 
+// The reference's FFMA variants (kNaive .. kWarpTileVec4) run this
+// library's f32 AUTO choice: the tensor cores in the 3xTF32 form (hi/lo split
+// inside the GEMM kernel, no workspace) when K % 4 == 0, N % 4 == 0 and A, B
+// are 16-byte aligned, else the FFMA kernel; kTcgen05Tf32x3 asks for the
+// tensor-core form outright (other shapes rejected).
 [[nodiscard]] Status launch_gemm_f32(const float* a, const float* b, float* c, std::int64_t m, std::int64_t n,
                                     std::int64_t k, float alpha, float beta, GemmVariant variant,
                                     GemmTile tile, rt::StreamHandle stream);
 // bf16 A[M,K] @ B[K,N] with a fused epilogue c = act(alpha*acc + beta*C + bias[col]),
 // C float32 or bfloat16 (beta must be 0 for bf16).
 // New: f32 GEMM on the tensor cores (3xTF32), c = act(alpha * A@B + beta * C +
-// bias); the workspace holds the hi/lo split of A and B.
+// bias); the workspace holds the hi/lo split of A and B (nullptr and 0: the
+// GEMM kernel splits its tiles itself).
 [[nodiscard]] std::size_t gemm_f32_tc_workspace_bytes(std::int64_t m, std::int64_t n, std::int64_t k) noexcept;
 [[nodiscard]] Status launch_gemm_f32_tc(const float* a, const float* b, float* c, std::int64_t m, std::int64_t n,
                                         std::int64_t k, float alpha, float beta, const float* bias, Activation act,

@@ -107,8 +107,8 @@ Status launch_gemm_f32(const float* a, const float* b, float* c, std::int64_t m,
     return UnimplementedError("launch_gemm_f32: the cuBLAS comparison row is not part of this library");
   if (variant == GemmVariant::kTcgen05Bf16)
     return InvalidArgumentError("launch_gemm_f32: kTcgen05Bf16 takes bf16 operands (launch_gemm_bf16)");
-  if (variant == GemmVariant::kTcgen05Tf32x3)
-    return InvalidArgumentError("launch_gemm_f32: kTcgen05Tf32x3 needs a workspace (launch_gemm_f32_tc)");
+  if (variant == GemmVariant::kTcgen05Tf32x3)  // no workspace: the GEMM kernel splits its tiles itself
+    return from_capi(mcke_sm100_gemm_f32_tc(a, b, c, m, n, k, alpha, beta, nullptr, 0, nullptr, 0, st(stream)));
   if (!gemm_tile_is_supported(variant, tile))
     return InvalidArgumentError("launch_gemm_f32: tile is not one the variant is defined for; no fallback is applied");
   return from_capi(mcke_sm100_gemm_f32(a, b, c, m, n, k, alpha, beta, MCKE_GEMM_AUTO, st(stream)));

@@ -371,10 +371,11 @@ def gemm_f32_tc_workspace_bytes(m: int, n: int, k: int) -> int:
 
 
 def gemm_f32_tc(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, bias=None, act="none", workspace=None,
-                stream=None):
+                stream=None, in_kernel_split: bool = False):
     """float32 C = act(alpha * A @ B + beta * C + bias) on the tensor cores
     (3xTF32, mcke_sm100_gemm_f32_tc); ``workspace`` holds the hi/lo split of A
-    and B (allocated here when not given)."""
+    and B (allocated here when not given), or, with ``in_kernel_split``, no
+    workspace is passed and the GEMM kernel splits its tiles itself."""
     _need(a, torch.float32, "a"); _need(b, torch.float32, "b")
     m, k = a.shape
     k2, n = b.shape
@@ -385,6 +386,10 @@ def gemm_f32_tc(a, b, c=None, alpha: float = 1.0, beta: float = 0.0, bias=None, 
     _need(c, torch.float32, "c")
     if bias is not None:
         _need(bias, torch.float32, "bias")
+    if in_kernel_split:
+        _check(lib().mcke_sm100_gemm_f32_tc(_ptr(a), _ptr(b), _ptr(c), m, n, k, alpha, beta, _ptr(bias), _act(act),
+                                            None, 0, _stream(a, stream)))
+        return c
     need = gemm_f32_tc_workspace_bytes(m, n, k)
     if workspace is None:
         workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.device)

@@ -43,22 +43,41 @@ def _check(got, want, k, ctx, amax=1.0):
 
 # single-CTA shape (m <= 128), the 2-CTA pair shape, ragged edges in every
 # dimension, k not a multiple of the 32-deep k-block
+# in_kernel: the GEMM kernel splits its raw fp32 tiles itself (no workspace)
+SPLIT = pytest.mark.parametrize("in_kernel", [False, True], ids=["split_pass", "in_kernel_split"])
+
+
+@SPLIT
 @pytest.mark.parametrize("m,n,k", [(64, 64, 32), (128, 256, 64), (100, 260, 36), (300, 264, 516),
-                                   (1024, 1024, 1024), (257, 1028, 2052)])
-def test_matches_oracle(m, n, k):
+                                   (1024, 1024, 1024), (257, 1028, 2052), (512, 100, 64)])
+def test_matches_oracle(m, n, k, in_kernel):
     a = oracle.fill_random(m * k, 2).reshape(m, k)
     b = oracle.fill_random(k * n, 3).reshape(k, n)
-    got = host(mcke.gemm_f32_tc(dev(a), dev(b)))
+    got = host(mcke.gemm_f32_tc(dev(a), dev(b), in_kernel_split=in_kernel))
+    mcke.check_device_errors()
     _check(got, oracle.gemm(a, b), k, (m, n, k))
 
 
-def test_large_k_spot_check():
+@SPLIT
+def test_large_k_spot_check(in_kernel):
     m, n, k = 512, 768, 8192
     a = oracle.fill_random(m * k, 4).reshape(m, k)
     b = oracle.fill_random(k * n, 5).reshape(k, n)
-    got = host(mcke.gemm_f32_tc(dev(a), dev(b)))
+    got = host(mcke.gemm_f32_tc(dev(a), dev(b), in_kernel_split=in_kernel))
     r = oracle.spot_check_gemm(a, b, got, samples=1024, seed=3)
     assert r["mismatches"] == 0 and r["checked"] == 1024, r
+
+
+def test_in_kernel_split_equals_the_split_pass():
+    # the same hi/lo parts and the same MMA order: the same bits
+    m, n, k = 1000, 1032, 1028
+    a = dev(oracle.fill_random(m * k, 14).reshape(m, k))
+    b = dev(oracle.fill_random(k * n, 15).reshape(k, n))
+    u = mcke.gemm_f32_tc(a, b)
+    v = mcke.gemm_f32_tc(a, b, in_kernel_split=True)
+    torch.cuda.synchronize()
+    mcke.check_device_errors()
+    assert torch.equal(u, v)
 
 
 def test_tensor_cores_beat_the_tf32_rounding():
@@ -106,3 +125,35 @@ def test_k_zero_writes_beta_c_and_bad_shapes_are_rejected():
     with pytest.raises(mcke.MckeError, match="workspace"):
         mcke.gemm_f32_tc(a, b, workspace=torch.empty(256, dtype=torch.uint8, device=DEV))
     mcke.check_device_errors()
+
+
+def test_f32_auto_runs_the_in_kernel_split_where_the_shape_allows():
+    # mcke_sm100_gemm_f32 with AUTO (the reference's launch_gemm_f32) takes the
+    # tensor cores for K % 4 == 0, N % 4 == 0: the same bits as the in-kernel
+    # split, alpha/beta included; other shapes stay on the FFMA kernel.
+    m, n, k = 333, 516, 260
+    a = dev(oracle.fill_random(m * k, 16).reshape(m, k))
+    b = dev(oracle.fill_random(k * n, 17).reshape(k, n))
+    c0 = dev(oracle.fill_random(m * n, 18).reshape(m, n))
+    auto = mcke.gemm(a, b, c0.clone(), 0.75, 1.25)
+    split = mcke.gemm_f32_tc(a, b, c0.clone(), 0.75, 1.25, in_kernel_split=True)
+    simt = mcke.gemm(a, b, c0.clone(), 0.75, 1.25, variant="simt")
+    torch.cuda.synchronize()
+    assert torch.equal(auto, split)
+    assert not torch.equal(auto, simt)  # FFMA sums in another order
+    _check(host(auto), oracle.gemm(host(a), host(b), host(c0), 0.75, 1.25), k, "auto", 1.25)
+    a3 = dev(oracle.fill_random(m * 258, 19).reshape(m, 258))  # K % 4 != 0
+    b3 = dev(oracle.fill_random(258 * n, 20).reshape(258, n))
+    assert torch.equal(mcke.gemm(a3, b3), mcke.gemm(a3, b3, variant="simt"))
+    mcke.check_device_errors()
+
+
+def test_f32_auto_8192_cube_spot_check():
+    # the 8192^3 float32 GEMM of the reference's benchmark, through AUTO
+    n = 8192
+    g = torch.Generator(device="cpu").manual_seed(21)
+    a = torch.rand((n, n), generator=g, dtype=torch.float32) * 2 - 1
+    b = torch.rand((n, n), generator=g, dtype=torch.float32) * 2 - 1
+    got = host(mcke.gemm(a.to(DEV), b.to(DEV)))
+    r = oracle.spot_check_gemm(a.numpy(), b.numpy(), got, samples=512, seed=22)
+    assert r["mismatches"] == 0 and r["checked"] == 512, r

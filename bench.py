@@ -71,11 +71,18 @@ def load_peaks() -> tuple[dict, str]:
 
 
 def load_traffic() -> dict:
+    """kernel -> {"bytes", "read", "write", "algorithmic", "note"} from one ncu
+    capture each (profiles/traffic.json)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f)
+            return json.load(f).get("kernels", {})
     return {}
+
+
+def traffic_of(traffic: dict, kernel: str):
+    e = traffic.get(kernel)
+    return None if e is None else e["bytes"]
 
 
 # ------------------------------------------------------------------ clocks
@@ -671,7 +678,8 @@ def run_mcke(args, dist) -> None:
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks.get("hbm_gbs"),
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "peak_kind": f"{peak_kind} hbm_gbs",
-                     "traffic": traffic.get("softmax_stream_row_kernel"),
+                     "traffic": traffic_of(traffic, "softmax_warp_row_kernel"),
+                     "traffic_note": (traffic.get("softmax_warp_row_kernel") or {}).get("note"),
                      "algorithmic_bytes_per_launch": SOFTMAX_BYTES, "kernel_ms": round(kernel_ms, 5),
                      "cold_step_ms": round(cold_ms, 5)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": SOFTMAX_BYTES // 2,
@@ -771,7 +779,8 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
             "kernel_ms": round(kms, 5), "cold_step_ms": round(cold, 5), "algorithmic_bytes": BIAS_BYTES,
             "checked": checked, "timing": f"back to back over {nrot} rotating buffer sets",
-            "traffic": traffic.get("bias_act_f32_kernel")}
+            "traffic": traffic_of(traffic, "bias_act_f32_chunk_kernel"),
+            "traffic_note": (traffic.get("bias_act_f32_chunk_kernel") or {}).get("note")}
         del xb, yb
 
     if "reduce" in want:
@@ -821,7 +830,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
             "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
             "p2p_result_matches_nccl": p2p_matches, "checked": checked,
-            "traffic": traffic.get("reduce_full_stream_kernel")}
+            "traffic": traffic_of(traffic, "reduce_full_stream_kernel")}
         del xr
 
     if "row_reduce" in want:
@@ -1063,6 +1072,52 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
     return out
 
 
+def reduce_timeline(torch, mcke, dev, n: int, steps: int = 60) -> dict:
+    """Where a step of the one-kernel reduce (mcke_sm100_reduce_full_p2p_f32)
+    spends its time on one GPU: median over `steps` back-to-back calls of the
+    phases its %globaltimer stamps bound (ns -> us)."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    xs = [torch.rand(n, generator=gen, device=dev) * 2 - 1 for _ in range(3)]
+    buf = torch.zeros(mcke.lib().mcke_sm100_reduce_p2p_buffer_bytes(1), dtype=torch.uint8, device=dev)
+    table = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+    out = torch.empty(16, dtype=torch.uint8, device=dev)
+    for i in range(5):
+        mcke.reduce_full_p2p(xs[i % 3], 0, table, 1, 0, 0, out=out)
+    stamps = mcke.timeline_buffer(steps, dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(steps):
+        mcke.reduce_full_p2p_timeline(xs[i % 3], 0, table, 1, 0, 0, stamps[i], out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    mcke.check_device_errors()
+    step_us = e0.elapsed_time(e1) * 1e3 / steps
+    t = stamps.cpu().numpy().astype(np.int64)
+    first_entry, first_start, last_start, first_done, last_done, folded, exchanged = (t[:, k] for k in range(7))
+    ph = {
+        "gap_after_previous_step": first_start[1:] - exchanged[:-1],
+        "dispatch_ramp": last_start - first_start,
+        "streaming": last_done - first_start,
+        "finish_spread": last_done - first_done,
+        "fold": folded - last_done,
+        "exchange": exchanged - folded,
+        "kernel_first_start_to_result": exchanged - first_start,
+        "early_entry_before_previous_grid_done": first_start - first_entry,
+    }
+    med = {k: round(float(np.median(v)) / 1e3, 2) for k, v in ph.items()}
+    checks = bool(np.all(first_entry <= first_start) and np.all(first_start <= last_start) and
+                  np.all(last_start <= last_done) and np.all(last_done <= folded) and np.all(folded <= exchanged))
+    stream_bytes = 4 * n
+    return {"case": f"reduce_full_p2p world 1, n = {n} floats, {steps} steps back to back over 3 inputs",
+            "step_us_cuda_events": round(step_us, 2),
+            "phases_median_us": med,
+            "streaming_gbs": round(stream_bytes / (med["streaming"] * 1e-6) / 1e9, 1),
+            "step_gbs": round(stream_bytes / (step_us * 1e-6) / 1e9, 1),
+            "stamps_ordered": checks}
+
+
 def run_profile(args) -> None:
     """One full-size launch of each named kernel after two warm-ups, for ncu
     (`ncu -k regex:... -s 2 -c 1 python bench.py --profile NAME`).  Sizes are
@@ -1124,6 +1179,13 @@ def run_profile(args) -> None:
             b = torch.rand(n, n, generator=gen, device=dev) * 2 - 1
             c = torch.empty(n, n, device=dev)
             fn = lambda: mcke.gemm(a, b, c, variant="simt")  # noqa: E731
+        elif name.startswith("reduce_timeline"):
+            # Phase breakdown of the one-kernel sharded reduce at world 1
+            # (reduce_timeline or reduce_timeline:<log2 n>): K steps back to
+            # back over three rotating inputs, each step's %globaltimer stamps.
+            lg = int(name.split(":")[1]) if ":" in name else 25
+            print(json.dumps(reduce_timeline(torch, mcke, dev, 1 << lg)))
+            continue
         else:
             raise SystemExit(f"unknown profile case {name}")
         for _ in range(3):

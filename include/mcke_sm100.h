@@ -226,6 +226,19 @@ size_t mcke_sm100_reduce_p2p_buffer_bytes(int world);
 int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
                                    void* const* peer_buffers, int world, int rank, uint64_t epoch,
                                    mcke_reduce_result* out, mcke_stream_t stream);
+/* New, a measuring aid (no counterpart in the reference): the same call, which
+ * also records when its phases happened, as %globaltimer nanoseconds, into
+ * `stamps` (8 words of device memory, 8-byte aligned; n > 0).  The caller sets
+ * words 0, 1, 3 to UINT64_MAX and 2, 4 to 0 before the call:
+ *   [0] min over CTAs: entry (before waiting for the previous grid's memory)
+ *   [1] min over CTAs: streaming starts      [2] max: the last CTA starts
+ *   [3] min over CTAs: a block partial is done [4] max: the last one is done
+ *   [5] the last CTA has folded the block partials (the shard partial)
+ *   [6] the ranks' partials are combined and the result is stored.
+ * Same result and the same bits as mcke_sm100_reduce_full_p2p_f32. */
+int mcke_sm100_reduce_full_p2p_f32_timeline(const float* x, int64_t n, int64_t index_base,
+                                            void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                            mcke_reduce_result* out, uint64_t* stamps, mcke_stream_t stream);
 /* Set-up helpers for exchange buffers shared between processes (CUDA IPC).
  * create: cudaMalloc + zero + IPC handle (64 bytes written to handle_out);
  * open: map a peer's handle in this process; close: unmap (opened = 1) or free. */

@@ -101,18 +101,22 @@ __global__ void __launch_bounds__(kThreads) bias_act_f32_kernel(const float* __r
 // launch against 24.0 us for the strip kernel above (timed alone after an L2
 // flush the strip kernel is the faster, 22.5 against 24.6 us).  The reference's
 // max_row_blocks knob and the narrower vector widths keep the strip kernel.
+// The row of a chunk comes from a shift when chunks_per_row is a power of two
+// (cpr_shift >= 0; config 1: 8) and from a 32-bit division otherwise: the
+// kernel is issue-bound, and a 64-bit division per thread is a ~70-instruction
+// subroutine.
 template <class F>
 __global__ void __launch_bounds__(kThreads) bias_act_f32_chunk_kernel(const float* __restrict__ x,
                                                                       const float* __restrict__ bias,
-                                                                      float* __restrict__ y, int64_t chunks,
-                                                                      int64_t chunks_per_row) {
+                                                                      float* __restrict__ y, uint32_t chunks,
+                                                                      uint32_t chunks_per_row, int cpr_shift) {
   pdl_entry();
   const int lane = threadIdx.x & 31;
-  const int64_t w = static_cast<int64_t>(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5);
+  const uint32_t w = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
   if (w >= chunks) return;
-  const int64_t row = w / chunks_per_row;
-  const int64_t c0 = (w - row * chunks_per_row) * 512;
-  const int64_t base = row * chunks_per_row * 512 + c0;
+  const uint32_t row = cpr_shift >= 0 ? w >> cpr_shift : w / chunks_per_row;
+  const int64_t c0 = static_cast<int64_t>(w - row * chunks_per_row) * 512;
+  const int64_t base = static_cast<int64_t>(w) * 512;
   float4 v[4], b[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u) v[u] = ld_stream_f4(x + base + 4 * (lane + 32 * u));
@@ -247,14 +251,16 @@ extern "C" int mcke_sm100_bias_act_f32(const float* x, const float* bias, float*
   if (x == y) return fail(MCKE_INVALID_ARGUMENT, "%s: in-place (x == y) is not supported", who);
   if (!act_ok(act)) return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (vector_width == 4 && max_row_blocks == 0 && cols % 512 == 0 && rows * (cols / 512) / 8 < 2147483647LL) {
-    const int64_t per_row = cols / 512, chunks = rows * per_row;
-    const unsigned g = static_cast<unsigned>((chunks + 7) / 8);
+  if (vector_width == 4 && max_row_blocks == 0 && cols % 512 == 0 && rows * (cols / 512) < (int64_t{1} << 31)) {
+    const uint32_t per_row = static_cast<uint32_t>(cols / 512);
+    const uint32_t chunks = static_cast<uint32_t>(rows) * per_row;
+    const int shift = (per_row & (per_row - 1)) == 0 ? __builtin_ctz(per_row) : -1;
+    const unsigned g = (chunks + 7) / 8;
     switch (act) {
-      case MCKE_ACT_RELU: launch_async(bias_act_f32_chunk_kernel<ActRelu>, g, kThreads, 0, s, x, bias, y, chunks, per_row); break;
-      case MCKE_ACT_GELU_ERF: launch_async(bias_act_f32_chunk_kernel<ActGeluErf>, g, kThreads, 0, s, x, bias, y, chunks, per_row); break;
-      case MCKE_ACT_GELU_TANH: launch_async(bias_act_f32_chunk_kernel<ActGeluTanh>, g, kThreads, 0, s, x, bias, y, chunks, per_row); break;
-      default: launch_async(bias_act_f32_chunk_kernel<ActNone>, g, kThreads, 0, s, x, bias, y, chunks, per_row); break;
+      case MCKE_ACT_RELU: launch_async(bias_act_f32_chunk_kernel<ActRelu>, g, kThreads, 0, s, x, bias, y, chunks, per_row, shift); break;
+      case MCKE_ACT_GELU_ERF: launch_async(bias_act_f32_chunk_kernel<ActGeluErf>, g, kThreads, 0, s, x, bias, y, chunks, per_row, shift); break;
+      case MCKE_ACT_GELU_TANH: launch_async(bias_act_f32_chunk_kernel<ActGeluTanh>, g, kThreads, 0, s, x, bias, y, chunks, per_row, shift); break;
+      default: launch_async(bias_act_f32_chunk_kernel<ActNone>, g, kThreads, 0, s, x, bias, y, chunks, per_row, shift); break;
     }
     return check_launch(who);
   }

@@ -152,7 +152,27 @@ struct P2pArgs {
   int world;
   int rank;
   int auto_epoch;  // 1: the epoch is the counter after the part area, advanced by each call
+  unsigned long long* stamps;  // null, or the kStamp* phase times of this call (%globaltimer, ns)
 };
+
+// Phase times of one call of the one-kernel reduce, for the fixed-cost
+// breakdown (mcke_sm100_reduce_full_p2p_f32_timeline).  Min slots start at
+// ~0, max slots at 0; the last CTA's slots are plain stores.
+enum : int {
+  kStampFirstEntry = 0,   // min over CTAs: entry, before the wait for the previous grid
+  kStampFirstStart = 1,   // min over CTAs: the previous grid's memory is visible, streaming starts
+  kStampLastStart = 2,    // max over CTAs: the last CTA starts streaming (dispatch ramp)
+  kStampFirstDone = 3,    // min over CTAs: a CTA has its block partial
+  kStampLastDone = 4,     // max over CTAs: the last CTA has its block partial
+  kStampFolded = 5,       // the last CTA has folded all block partials (the shard partial)
+  kStampExchanged = 6,    // the ranks' partials are combined and the result stored
+  kStampWords = 8,
+};
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 // Counter of the automatic epochs: the 64-byte slot after the part area
 // (first 8 bytes); the CTAs' arrival count of the current call follows it
@@ -262,7 +282,14 @@ template <bool kP2p>
 __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
                                                                       Part* __restrict__ parts, P2pArgs p2p_in) {
+  unsigned long long* const stamps = kP2p ? p2p_in.stamps : nullptr;
+  if (kP2p && stamps && threadIdx.x == 0) atomicMin(stamps + kStampFirstEntry, global_ns());
   pdl_entry();
+  if (kP2p && stamps && threadIdx.x == 0) {
+    const unsigned long long t = global_ns();
+    atomicMin(stamps + kStampFirstStart, t);
+    atomicMax(stamps + kStampLastStart, t);
+  }
   P2pArgs p2p = p2p_in;
   extern __shared__ __align__(16) uint8_t smem[];  // P2P: the ranks' collected partials
   __shared__ Part red[kWarps];
@@ -329,26 +356,31 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
     // reduce_full_combine_kernel's 1024-thread fold (G <= kFullCtaCap < 512,
     // so the rest are the identity), which makes the shard partial
     // bit-identical to the two-launch path -- and runs the exchange.  No CTA
-    // waits for another CTA of the grid.
+    // waits for another CTA of the grid.  No fence between a CTA's slot
+    // stores and its arrival: the collector checks the epoch in every word of
+    // every slot and polls until all have landed, so the counter may overtake
+    // the stores (a fence there put one more round trip to L2 between the last
+    // CTA's partial and the result).
     resolve_tag(p2p);
     LLSlot* local = p2p.peers[p2p.rank] + 2 * p2p.world;
     __shared__ int is_last;
+    __shared__ int parts_ok;
     if (tid == 0) {
+      if (stamps) {
+        const unsigned long long t = global_ns();
+        atomicMin(stamps + kStampFirstDone, t);
+        atomicMax(stamps + kStampLastDone, t);
+      }
       ll_store(local + blockIdx.x, p, p2p.tag);
-      __threadfence();
       is_last = atomicAdd(arrival_count(p2p), 1u) == gridDim.x - 1u ? 1 : 0;
+      parts_ok = 1;
+      if (is_last) *arrival_count(p2p) = 0u;  // the next call counts from 0
     }
     __syncthreads();
     if (!is_last) return;
     __shared__ Part red32[16];
     __shared__ Part shard;
-    __shared__ int parts_ok;
     const int G = static_cast<int>(gridDim.x);
-    if (tid == 0) {
-      parts_ok = 1;
-      *arrival_count(p2p) = 0u;  // the next call counts from 0
-    }
-    __syncthreads();
     // Every slot is written (each CTA stored before counting itself in), so
     // all 256 threads read their two slots at once: one round trip.  The
     // tags are checked all the same (bounded wait).
@@ -374,11 +406,13 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
           r.i = -1;
         }
         shard = r;
+        if (stamps) stamps[kStampFolded] = global_ns();
       }
     }
     __syncthreads();
     // dynamic shared memory: the ranks' results, collected in rank order
     p2p_publish_and_combine(shard, p2p, reinterpret_cast<Part*>(smem));
+    if (stamps && tid == 0) stamps[kStampExchanged] = global_ns();
   }
 }
 
@@ -861,10 +895,10 @@ extern "C" size_t mcke_sm100_reduce_p2p_buffer_bytes(int world) {
   return world > 0 ? static_cast<size_t>(2 * world + kFullCtaCap + 1) * sizeof(LLSlot) : 0;
 }
 
-extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
-                                              void* const* peer_buffers, int world, int rank, uint64_t epoch,
-                                              mcke_reduce_result* out, mcke_stream_t stream) {
-  static const char* who = "mcke_sm100_reduce_full_p2p_f32";
+namespace {
+int reduce_full_p2p(const char* who, const float* x, int64_t n, int64_t index_base, void* const* peer_buffers,
+                    int world, int rank, uint64_t epoch, mcke_reduce_result* out, uint64_t* stamps,
+                    mcke_stream_t stream) {
   clear_error();
   if (!out || !peer_buffers) return fail(MCKE_INVALID_ARGUMENT, "%s: null output or peer table", who);
   if (world < 1 || world > 1024 || rank < 0 || rank >= world)
@@ -882,6 +916,7 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   a.world = world;
   a.rank = rank;
   a.auto_epoch = epoch == 0 ? 1 : 0;
+  a.stamps = reinterpret_cast<unsigned long long*>(stamps);
   if (n == 0) {
     launch_async(reduce_p2p_empty_kernel, 1, kThreads, static_cast<size_t>(world) * sizeof(Part), s, a);
     return check_launch(who);
@@ -893,6 +928,30 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
   // dynamic shared memory: the ranks' collected partials (world <= 1024: 24 KB)
   launch_async(reduce_full_stream_kernel<true>, static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s, x, n, head, index_base, nullptr, a);
   return check_launch(who);
+}
+}  // namespace
+
+extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
+                                              void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                              mcke_reduce_result* out, mcke_stream_t stream) {
+  return reduce_full_p2p("mcke_sm100_reduce_full_p2p_f32", x, n, index_base, peer_buffers, world, rank, epoch, out,
+                         nullptr, stream);
+}
+
+extern "C" int mcke_sm100_reduce_full_p2p_f32_timeline(const float* x, int64_t n, int64_t index_base,
+                                                       void* const* peer_buffers, int world, int rank,
+                                                       uint64_t epoch, mcke_reduce_result* out, uint64_t* stamps,
+                                                       mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_full_p2p_f32_timeline";
+  if (!stamps || !aligned(stamps, 8)) {
+    clear_error();
+    return fail(MCKE_INVALID_ARGUMENT, "%s: stamps must be 8-byte aligned device memory", who);
+  }
+  if (n == 0) {
+    clear_error();
+    return fail(MCKE_INVALID_ARGUMENT, "%s: an empty shard runs no streaming pass to time", who);
+  }
+  return reduce_full_p2p(who, x, n, index_base, peer_buffers, world, rank, epoch, out, stamps, stream);
 }
 
 // ---- CUDA IPC set-up helpers for the exchange buffers ---------------------------

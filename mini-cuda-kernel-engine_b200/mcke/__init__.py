@@ -81,6 +81,8 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_reduce_combine": (i32, [vp, i64, vp, vp]),
             "mcke_sm100_reduce_p2p_buffer_bytes": (sz, [i32]),
             "mcke_sm100_reduce_full_p2p_f32": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp]),
+            "mcke_sm100_reduce_full_p2p_f32_timeline": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp,
+                                                              vp]),
             "mcke_sm100_ipc_buffer_create": (i32, [sz, ctypes.POINTER(vp), vp]),
             "mcke_sm100_ipc_buffer_open": (i32, [vp, ctypes.POINTER(vp)]),
             "mcke_sm100_ipc_buffer_close": (i32, [vp, i32]),
@@ -276,6 +278,29 @@ def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch
         out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=x.device)
     _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), x.numel(), index_base, _ptr(peer_table), world, rank,
                                                 epoch, _ptr(out), _stream(x, stream)))
+    return out
+
+
+TIMELINE_WORDS = 8
+TIMELINE_PHASES = ("first_entry", "first_start", "last_start", "first_done", "last_done", "folded", "exchanged")
+
+
+def timeline_buffer(steps: int, device) -> "torch.Tensor":
+    """int64 [steps, 8] stamps initialised as mcke_sm100_reduce_full_p2p_f32_timeline wants."""
+    t = torch.zeros((steps, TIMELINE_WORDS), dtype=torch.int64, device=device)
+    t[:, [0, 1, 3]] = -1  # UINT64_MAX
+    return t
+
+
+def reduce_full_p2p_timeline(x, index_base: int, peer_table, world: int, rank: int, epoch: int, stamps,
+                             out=None, stream=None):
+    """reduce_full_p2p that also records its phase times into ``stamps`` (one
+    row of :func:`timeline_buffer`)."""
+    _need(x, torch.float32, "x")
+    if out is None:
+        out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=x.device)
+    _check(lib().mcke_sm100_reduce_full_p2p_f32_timeline(_ptr(x), x.numel(), index_base, _ptr(peer_table), world,
+                                                         rank, epoch, _ptr(out), _ptr(stamps), _stream(x, stream)))
     return out
 
 

@@ -68,6 +68,11 @@ def test_argument_validation_needs_no_device(mcke):
     assert l.mcke_sm100_reduce_row_f32(bogus, ctypes.c_void_p(0x2000), 4, 64, 0, 2, None, 0, None) == mcke.UNIMPLEMENTED
     assert l.mcke_sm100_reduce_full_f32(bogus, 1000, ctypes.c_void_p(0x2000), None, 0, None) == mcke.INVALID_ARGUMENT
     assert b"workspace" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_reduce_full_p2p_f32_timeline(bogus, 1000, 0, bogus, 1, 0, 1, bogus, None,
+                                                      None) == mcke.INVALID_ARGUMENT
+    assert b"stamps" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_reduce_full_p2p_f32_timeline(bogus, 1000, 0, bogus, 1, 0, 1, bogus,
+                                                      ctypes.c_void_p(0x1004), None) == mcke.INVALID_ARGUMENT
     # empty extents are OK with no launch
     assert l.mcke_sm100_softmax_f32(None, None, 0, 16, 1, None) == mcke.OK
     assert l.mcke_sm100_bias_act_f32(None, None, None, 0, 0, 3, 4, 0, None) == mcke.OK

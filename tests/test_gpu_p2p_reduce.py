@@ -183,3 +183,24 @@ def test_two_ranks_on_two_gpus():
             assert (m, i) == (1.5, 777)
             assert abs(s - ws) <= np.spacing(np.float32(abs(ws)))
         assert got[r] == got[0]
+
+
+def test_timeline_variant_same_bits_and_ordered_stamps():
+    # the measuring aid gives the same result and stamps in phase order
+    v = oracle.fill_random(5_000_011, 31)
+    x = torch.from_numpy(v).cuda()
+    buf = torch.zeros(mcke.lib().mcke_sm100_reduce_p2p_buffer_bytes(1), dtype=torch.uint8, device="cuda")
+    table = _table(buf)
+    want = mcke.reduce_full(x).cpu().numpy().tobytes()
+    stamps = mcke.timeline_buffer(3, "cuda")
+    for i in range(3):
+        got = mcke.reduce_full_p2p_timeline(x, 0, table, 1, 0, 0, stamps[i]).cpu().numpy().tobytes()
+        assert got == want
+    mcke.check_device_errors()
+    t = stamps.cpu().numpy().view(np.uint64)
+    for row in t:
+        entry, start, last_start, first_done, last_done, folded, exchanged = (int(w) for w in row[:7])
+        assert entry <= start <= last_start <= last_done <= folded <= exchanged, row
+        assert start <= first_done <= last_done, row
+        assert exchanged - start < 10_000_000  # well under 10 ms
+    assert np.all(t[1:, 1] >= t[:-1, 6])  # a step starts after the previous one stored its result

@@ -1115,20 +1115,23 @@ def reduce_timeline(torch, mcke, dev, n: int, steps: int = 60) -> dict:
     mcke.check_device_errors()
     step_us = e0.elapsed_time(e1) * 1e3 / steps
     t = stamps.cpu().numpy().astype(np.int64)
-    first_entry, first_start, last_start, first_done, last_done, folded, exchanged = (t[:, k] for k in range(7))
+    first_entry, first_start, last_start, first_done, last_done, folded, exchanged, counted = (t[:, k] for k in range(8))
     ph = {
         "gap_after_previous_step": first_start[1:] - exchanged[:-1],
         "dispatch_ramp": last_start - first_start,
         "streaming": last_done - first_start,
         "finish_spread": last_done - first_done,
         "fold": folded - last_done,
+        "fold_arrival": counted - last_done,
+        "fold_collect": folded - counted,
         "exchange": exchanged - folded,
         "kernel_first_start_to_result": exchanged - first_start,
         "early_entry_before_previous_grid_done": first_start - first_entry,
     }
     med = {k: round(float(np.median(v)) / 1e3, 2) for k, v in ph.items()}
     checks = bool(np.all(first_entry <= first_start) and np.all(first_start <= last_start) and
-                  np.all(last_start <= last_done) and np.all(last_done <= folded) and np.all(folded <= exchanged))
+                  np.all(last_start <= last_done) and np.all(last_done <= counted) and
+                  np.all(counted <= folded) and np.all(folded <= exchanged))
     stream_bytes = 4 * n
     return {"case": f"reduce_full_p2p world 1, n = {n} floats, {steps} steps back to back over 3 inputs",
             "step_us_cuda_events": round(step_us, 2),

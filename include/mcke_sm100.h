@@ -234,7 +234,8 @@ int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base
  *   [1] min over CTAs: streaming starts      [2] max: the last CTA starts
  *   [3] min over CTAs: a block partial is done [4] max: the last one is done
  *   [5] the last CTA has folded the block partials (the shard partial)
- *   [6] the ranks' partials are combined and the result is stored.
+ *   [6] the ranks' partials are combined and the result is stored
+ *   [7] the last CTA's arrival on the counter has returned (it knows it is last).
  * Same result and the same bits as mcke_sm100_reduce_full_p2p_f32. */
 int mcke_sm100_reduce_full_p2p_f32_timeline(const float* x, int64_t n, int64_t index_base,
                                             void* const* peer_buffers, int world, int rank, uint64_t epoch,
@@ -281,7 +282,7 @@ int mcke_sm100_gemm_f32(const float* a, const float* b, float* c, int64_t m, int
  * mcke_sm100_gemm_f32_tc_workspace_bytes(m, n, k) bytes (256-byte aligned;
  * 8 * (M*K + K*N), rounded) two split passes write the parts there first; with
  * workspace = NULL and workspace_bytes = 0 the GEMM kernel splits its tiles in
- * shared memory itself (the same bits, no workspace, ~10% slower at 8192^3).
+ * shared memory itself (the same bits, no workspace, ~5% slower at 8192^3).
  * Same contract as launch_gemm_f32 (kernels.hpp:265) otherwise: beta == 0
  * never reads C, k == 0 writes act(beta * C + bias). */
 size_t mcke_sm100_gemm_f32_tc_workspace_bytes(int64_t m, int64_t n, int64_t k);

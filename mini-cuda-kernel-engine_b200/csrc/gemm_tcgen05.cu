@@ -49,9 +49,13 @@
 //     stored in SWIZZLE_128B_BASE32B (128-byte rows of 32 floats whose 32-byte
 //     chunks are permuted by (row & 3), the layout an MN-major 32-bit operand
 //     needs; with the plain 128-byte swizzle an N-major tf32 B accumulated
-//     nothing) -- and the epilogue warps split each stage in shared memory
-//     (below) before the MMA reads it.  No workspace and no extra passes over
-//     A and B; the two give the same bits.
+//     nothing) -- and the epilogue warps write each stage's lo part in
+//     shared memory (below) before the MMA reads it.  The raw tile itself
+//     serves as hi: a .kind::tf32 MMA reads the top 19 bits of each 32-bit
+//     operand and ignores the low 13, which is exactly hi.  No workspace and
+//     no extra passes over A and B; the two give the same bits (a GPU test
+//     compares them bit for bit, so hardware that read the low bits would
+//     fail it).
 //
 // Tensor-memory and descriptor encodings follow the PTX ISA for tcgen05
 // (instruction descriptor for .kind::f16 / .kind::tf32, shared-memory matrix
@@ -877,10 +881,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       ++epi_uses;
     };
-    // kSplit: these warps also split every stage of this CTA into hi (the
-    // value with its low 13 mantissa bits cleared, in place) and lo = value -
-    // hi (into the stage's lo buffers), elementwise at the same offsets, so
-    // the lo tiles have the hi tiles' swizzled layout.  A conversion cursor
+    // kSplit: these warps also split every stage of this CTA: lo = value -
+    // hi, hi being the value with its low 13 mantissa bits cleared, written
+    // into the stage's lo buffers at the raw tile's offsets, so the lo tiles
+    // have the raw tiles' swizzled layout; the raw tile stays as it is and
+    // the MMA reads it as hi (the tensor core ignores a tf32 operand's low 13
+    // bits).  A conversion cursor
     // walks (segment, k-block) in the producer's order and runs ahead of the
     // promotions: before waiting for accumulation unit lc the warps have split
     // every k-block of units <= lc + 1.  (The MMA of unit lc + 1 needs its
@@ -890,11 +896,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // itself.)  Each warp fences its writes for the async proxy and arrives on
     // the leader's "converted" barrier (CTA-scope release, as a TMA or MMA
     // completion would).  Measured at 8192^3 on B200 (fp32-equivalent
-    // TFLOP/s): this form 223-241; with a cluster-scope release per arrival
-    // 186 (warps stalled on the fence); with one arrival per CTA after a
-    // local barrier 162; with 16-deep k-blocks and 6 stages 217 (twice the
-    // per-stage synchronisation); with two extra warps doing all the splits
-    // 138.  The split-pass path with a caller workspace: 264-272.
+    // TFLOP/s): this form 253-264, and 242-252 on the same boxes when hi was
+    // also written back over the raw tile (4096^3: 233 against 219); with a
+    // cluster-scope release per arrival 186 (warps stalled on the fence);
+    // with one arrival per CTA after a local barrier 162; with 16-deep
+    // k-blocks and 6 stages 217 (twice the per-stage synchronisation); with
+    // two extra warps doing all the splits 138.  The split-pass path with a
+    // caller workspace: 264-272.
     SegIter cit(unit, units, num_tiles, kblocks, sk);
     Seg csg{};
     bool cvalid = kSplit && cit.next(csg);
@@ -909,8 +917,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) return false;
       mbar_try(full_bar(st), ph);  // every lane observes the completed phase (acquire)
       const int t = static_cast<int>(threadIdx.x) - 64;  // 0 .. 255 over the eight warps
-      auto split = [](float4* hi, float4* lo) {
-        const float4 v = *hi;
+      auto split = [](const float4* raw, float4* lo) {
+        const float4 v = *raw;
         float4 h, l;
         h.x = __uint_as_float(__float_as_uint(v.x) & 0xffffe000u);
         h.y = __uint_as_float(__float_as_uint(v.y) & 0xffffe000u);
@@ -920,12 +928,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         l.y = v.y - h.y;
         l.z = v.z - h.z;
         l.w = v.w - h.w;
-        *hi = h;
         *lo = l;
       };
-      float4* a = reinterpret_cast<float4*>(sA(st)) + t;
+      const float4* a = reinterpret_cast<const float4*>(sA(st)) + t;
       float4* alo = reinterpret_cast<float4*>(sAlo(st)) + t;
-      float4* b = reinterpret_cast<float4*>(sB(st)) + t;
+      const float4* b = reinterpret_cast<const float4*>(sB(st)) + t;
       float4* blo = reinterpret_cast<float4*>(sBlo(st)) + t;
       constexpr int kStride = 32 * kEpiWarps;
       static_assert(C::A_STAGE % (16 * kStride) == 0 && C::B_STAGE % (16 * kStride) == 0, "whole rounds");

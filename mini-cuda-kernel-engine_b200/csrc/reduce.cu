@@ -166,6 +166,7 @@ enum : int {
   kStampLastDone = 4,     // max over CTAs: the last CTA has its block partial
   kStampFolded = 5,       // the last CTA has folded all block partials (the shard partial)
   kStampExchanged = 6,    // the ranks' partials are combined and the result stored
+  kStampCounted = 7,      // the last CTA's arrival has come back: it knows it is last
   kStampWords = 8,
 };
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -210,11 +211,15 @@ __device__ __forceinline__ void ll_store(LLSlot* slot, const Part& p, uint32_t t
   w[5] = t | (ib >> 32);
 }
 
-__device__ __forceinline__ bool ll_try_load(const LLSlot* slot, uint32_t tag, Part& p) {
-  const volatile unsigned long long* w = slot->w;
-  unsigned long long v[6];
-#pragma unroll
-  for (int k = 0; k < 6; ++k) v[k] = w[k];
+// A slot's six words as three 16-byte loads (each 8-byte element is read
+// single-copy atomically, which is all the format needs).
+__device__ __forceinline__ void ll_load_words(const LLSlot* slot, unsigned long long (&v)[6]) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v[0]), "=l"(v[1]) : "l"(slot->w) : "memory");
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v[2]), "=l"(v[3]) : "l"(slot->w + 2) : "memory");
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v[4]), "=l"(v[5]) : "l"(slot->w + 4) : "memory");
+}
+
+__device__ __forceinline__ bool ll_decode(const unsigned long long (&v)[6], uint32_t tag, Part& p) {
   bool ok = true;
 #pragma unroll
   for (int k = 0; k < 6; ++k) ok = ok && static_cast<uint32_t>(v[k] >> 32) == tag;
@@ -226,21 +231,25 @@ __device__ __forceinline__ bool ll_try_load(const LLSlot* slot, uint32_t tag, Pa
   return true;
 }
 
-// Bounded wait (kP2pWaitNs) until the non-null slots carry `tag`.  The waiter
-// sleeps between polls so that it takes no issue slots from the CTAs still
-// streaming on its SM.
+// Bounded wait (kP2pWaitNs) until the non-null slots carry `tag`.  Both
+// slots' words are requested before either is checked (one round trip per
+// poll, not two).  After the first polls the waiter sleeps between polls so
+// that it takes no issue slots from the CTAs still streaming on its SM.
 __device__ __forceinline__ bool ll_wait(const LLSlot* s0, const LLSlot* s1, uint32_t tag, Part& p0, Part& p1) {
   bool d0 = s0 == nullptr, d1 = s1 == nullptr;
   unsigned long long t0 = 0;
   for (uint32_t it = 0;; ++it) {
-    if (!d0) d0 = ll_try_load(s0, tag, p0);
-    if (!d1) d1 = ll_try_load(s1, tag, p1);
+    unsigned long long a[6], b[6];
+    if (!d0) ll_load_words(s0, a);
+    if (!d1) ll_load_words(s1, b);
+    if (!d0) d0 = ll_decode(a, tag, p0);
+    if (!d1) d1 = ll_decode(b, tag, p1);
     if (d0 && d1) return true;
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     if (it == 0) t0 = t;
     else if (t - t0 > kP2pWaitNs) return false;
-    __nanosleep(32);
+    if (it >= 8) __nanosleep(32);
   }
 }
 
@@ -365,7 +374,9 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
     LLSlot* local = p2p.peers[p2p.rank] + 2 * p2p.world;
     __shared__ int is_last;
     __shared__ int parts_ok;
+    __shared__ Part own;  // this CTA's partial: the collector does not read its own slot back
     if (tid == 0) {
+      own = p;
       if (stamps) {
         const unsigned long long t = global_ns();
         atomicMin(stamps + kStampFirstDone, t);
@@ -373,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
       }
       ll_store(local + blockIdx.x, p, p2p.tag);
       is_last = atomicAdd(arrival_count(p2p), 1u) == gridDim.x - 1u ? 1 : 0;
+      if (stamps && is_last) stamps[kStampCounted] = global_ns();
       parts_ok = 1;
       if (is_last) *arrival_count(p2p) = 0u;  // the next call counts from 0
     }
@@ -381,12 +393,19 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
     __shared__ Part red32[16];
     __shared__ Part shard;
     const int G = static_cast<int>(gridDim.x);
-    // Every slot is written (each CTA stored before counting itself in), so
-    // all 256 threads read their two slots at once: one round trip.  The
-    // tags are checked all the same (bounded wait).
+    // Every other CTA stored its slot before counting itself in, so all 256
+    // threads read their two slots at once: one round trip (the epochs are
+    // checked all the same, bounded wait).  This CTA's own partial comes from
+    // shared memory: its slot store may still be on its way.  Measured at
+    // 2^25 floats: 2.82 us from the count coming back to the shard partial
+    // when each poll loaded one slot, checked it, then loaded the other.
     Part v0 = part_identity(), v1 = part_identity(), q0, q1;
-    const bool got = ll_wait(tid < G ? local + tid : nullptr, tid + kThreads < G ? local + tid + kThreads : nullptr,
+    const int mine = static_cast<int>(blockIdx.x);
+    const bool got = ll_wait(tid < G && tid != mine ? local + tid : nullptr,
+                             tid + kThreads < G && tid + kThreads != mine ? local + tid + kThreads : nullptr,
                              p2p.tag, q0, q1);
+    if (tid == mine) q0 = own;
+    if (tid + kThreads == mine) q1 = own;
     if (!got) parts_ok = 0;
     if (got && tid < G) v0 = part_combine(v0, q0);
     if (got && tid + kThreads < G) v1 = part_combine(v1, q1);

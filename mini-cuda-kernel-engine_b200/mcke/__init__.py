@@ -282,7 +282,8 @@ def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch
 
 
 TIMELINE_WORDS = 8
-TIMELINE_PHASES = ("first_entry", "first_start", "last_start", "first_done", "last_done", "folded", "exchanged")
+TIMELINE_PHASES = ("first_entry", "first_start", "last_start", "first_done", "last_done", "folded", "exchanged",
+                   "counted")
 
 
 def timeline_buffer(steps: int, device) -> "torch.Tensor":

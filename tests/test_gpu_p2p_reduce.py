@@ -199,8 +199,8 @@ def test_timeline_variant_same_bits_and_ordered_stamps():
     mcke.check_device_errors()
     t = stamps.cpu().numpy().view(np.uint64)
     for row in t:
-        entry, start, last_start, first_done, last_done, folded, exchanged = (int(w) for w in row[:7])
-        assert entry <= start <= last_start <= last_done <= folded <= exchanged, row
+        entry, start, last_start, first_done, last_done, folded, exchanged, counted = (int(w) for w in row[:8])
+        assert entry <= start <= last_start <= last_done <= counted <= folded <= exchanged, row
         assert start <= first_done <= last_done, row
         assert exchanged - start < 10_000_000  # well under 10 ms
     assert np.all(t[1:, 1] >= t[:-1, 6])  # a step starts after the previous one stored its result

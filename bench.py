@@ -935,10 +935,19 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             if i == 0:
                 chk_in = (feeds[x], feeds[w1], feeds[b1], feeds[w2], feeds[b2])
         gr.finalize()
-        # replayed as a CUDA graph: the device time then excludes the host's
-        # enqueue of 12-20 nodes and their events
-        ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=True)
+        # Config 5's memory: the arena comes from a BuddyAllocator of this GPU
+        # (the reference's DeviceAllocator interface), and intermediates reuse
+        # freed blocks where stream order proves the last reader done.
+        # Replayed as a CUDA graph: the device time then excludes the host's
+        # enqueue of 12-20 nodes and their events.
+        ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=True, buddy=True,
+                            memory="reuse_happens_before")
         ex.plan()
+        no_reuse = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, memory="alloc_per_tensor")
+        no_reuse.plan_dry()
+        mem = {"allocator": ex.alloc_stats(0), "arena_bytes": ex.arena_bytes(0),
+               "arena_bytes_without_reuse": no_reuse.arena_bytes(0), "memory_policy": "reuse_happens_before"}
+        del no_reuse
         for t, arr in feeds.items():
             ex.set_input(t, arr)
         del feeds
@@ -960,7 +969,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "value": round(flops * ds / (tot * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "ms_per_run": round(tot / ds, 3), "branches": branches, "rows_per_gpu": rows,
             "frac_of_bf16_peak": round(flops / g / (tot / ds * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
-            "checked": checked,
+            "checked": checked, "memory": mem,
             "peak": peaks["bf16_tflops_sustained"], "peak_kind": "bf16_tflops_sustained (multi-kernel step)",
             "note": ("GEMM1 with fused bias+GELU (bf16 out) -> GEMM2 with fused +b2 -> softmax" if fused else
                      "GEMM1 -> bias+GELU -> GEMM2 -> +b2 -> softmax, one kernel each") +

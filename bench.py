@@ -756,20 +756,32 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         ms_f, per_f = timed_steps(torch, dist, lambda: mcke.peak_fma(seed, fo, iters), max(3, min(steps, 5)), warm,
                                   None)
         del seed, fo
+        # tcgen05 bf16: the GEMM's single-CTA MMA from shared memory, one CTA
+        # per SM, ~5 ms per step
+        mctas, miters = mcke.peak_mma_ctas(), 20000
+        ms_m, per_m = timed_steps(torch, dist, lambda: mcke.peak_mma(mctas, miters), max(3, min(steps, 5)), warm,
+                                  None)
+        mcke.check_device_errors()
         sm = torch.cuda.get_device_properties(dev).multi_processor_count
         triad = 12 * n / (min(per_t) * 1e-3) / 1e9   # best step, as a peak is taken
         copy = 8 * n / (min(per_c) * 1e-3) / 1e9
         ffma = mcke.PEAK_FMA_FLOP_PER_THREAD_STEP * nt * iters / (min(per_f) * 1e-3) / 1e12
         nominal_ffma = sm * 128 * 2 * 1.965
-        triad, copy, ffma = (dist.min(torch, v) for v in (triad, copy, ffma))
+        mma = mcke.peak_mma_flops(mctas, miters) / (min(per_m) * 1e-3) / 1e12
+        triad, copy, ffma, mma = (dist.min(torch, v) for v in (triad, copy, ffma, mma))
         out["peaks"] = {
             "triad_gbs": round(triad, 1), "copy_gbs": round(copy, 1), "ffma_tflops": round(ffma, 2),
             "driver_hbm_copy_gbs": peaks["hbm_gbs"], "triad_over_driver_copy": round(triad / peaks["hbm_gbs"], 4),
             "copy_over_driver_copy": round(copy / peaks["hbm_gbs"], 4),
             "ffma_over_nominal": round(ffma / (nominal_ffma / 1000.0), 4),
+            "tcgen05_bf16_tflops": round(mma, 1), "driver_bf16_burst_tflops": peaks["bf16_tflops"],
+            "tcgen05_over_driver_bf16": round(mma / peaks["bf16_tflops"], 4),
+            "tcgen05_over_nominal_dense": round(mma / 2250.0, 4),
             "note": "mcke_sm100_peak_{triad,copy,fma}_f32: a = b + 3c and a = b over 2^28 floats (12 and 8 B per "
                     "element), 8 FMA chains per thread x 40000 steps (16 flop per thread-step); best step, "
-                    "minimum over ranks; nominal FFMA = SMs x 128 lanes x 2 x 1.965 GHz"}
+                    "minimum over ranks; nominal FFMA = SMs x 128 lanes x 2 x 1.965 GHz; "
+                    "mcke_sm100_peak_mma_bf16: one CTA per SM, 20000 x 4 MMAs of 128 x 256 x 16 from shared "
+                    "memory (no loads), against the driver's cuBLAS burst and the nominal dense 2250 TFLOP/s"}
         ffma_peak = ffma
 
     if "bias_gelu" in want:

@@ -330,6 +330,16 @@ int mcke_sm100_peak_copy_f32(float* a, const float* b, int64_t n, mcke_stream_t 
  * seed[thread] and store one sum to out[thread]: 16 flop per thread per step. */
 int64_t mcke_sm100_peak_fma_threads(void);
 int mcke_sm100_peak_fma_f32(const float* seed, float* out, int64_t threads, int iters, mcke_stream_t stream);
+/* New (the tcgen05 bf16 peak probe): `ctas` CTAs (one per SM:
+ * mcke_sm100_peak_mma_ctas()) each issue `iters` k-blocks of four
+ * tcgen05.mma.cta_group::1.kind::f16 instructions (M = 128, N = 256, K = 16,
+ * bf16 operands, fp32 accumulator in TMEM) from one shared-memory stage, with no
+ * loads: the tensor pipe's rate for this library's own GEMM instruction.
+ * mcke_sm100_peak_mma_flops(ctas, iters) is the work of one call.  Its
+ * completion wait is bounded (site 10 in mcke_sm100_check_device_errors). */
+int64_t mcke_sm100_peak_mma_ctas(void);
+double mcke_sm100_peak_mma_flops(int64_t ctas, int iters);
+int mcke_sm100_peak_mma_bf16(int64_t ctas, int iters, mcke_stream_t stream);
 
 #ifdef __cplusplus
 }

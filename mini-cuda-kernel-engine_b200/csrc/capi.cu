@@ -149,9 +149,10 @@ extern "C" int mcke_sm100_check_device_errors(mcke_stream_t stream) {
   if (site != 0) {
     static const char* const kWhere[] = {"", "producer: free stage", "mma: loaded stage", "mma: free accumulator",
                                          "epilogue: full accumulator", "drain", "split-k: previous contributor's flag",
-                                         "epilogue warps' meeting", "split of a stage's raw tiles"};
+                                         "epilogue warps' meeting", "split of a stage's raw tiles",
+                                         "self-test", "tensor-core peak probe's completion"};
     return fail(MCKE_INTERNAL, "gemm (tcgen05): a bounded wait expired (site %u, %s); the kernel stopped early",
-                site, site < 9 ? kWhere[site] : "unknown");
+                site, site <= 10 ? kWhere[site] : "unknown");
   }
   MCKE_RETURN_IF(read_reduce_watchdog(&site));
   if (site == 2)

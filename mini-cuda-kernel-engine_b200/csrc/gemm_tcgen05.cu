@@ -152,7 +152,8 @@ enum : uint32_t {
   kSiteSplitFlag = 6,  // a split-k tile's flag from the previous contributor
   kSiteEpiMeet = 7,    // the epilogue warps' meeting on their mbarrier
   kSiteConvert = 8,    // 3xTF32 split in the kernel: a stage's raw tiles
-  kSiteSelfTest = 9    // mcke_sm100_watchdog_selftest only
+  kSiteSelfTest = 9,   // mcke_sm100_watchdog_selftest only
+  kSitePeak = 10       // mcke_sm100_peak_mma_bf16: its MMAs' completion
 };
 
 __device__ uint32_t g_tc_watchdog;
@@ -1612,7 +1613,90 @@ __global__ void watchdog_selftest_kernel() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   wait_bounded(smem_u32(&bar), 0u, &abort_word, kSiteSelfTest, false);
 }
+// ---- tensor-core peak probe ------------------------------------------------------
+//
+// The bf16 roofline denominator measured with this library's own MMAs: one CTA
+// per SM issues `iters` k-blocks of the GEMM's single-CTA instruction
+// (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 256, K = 16, fp32
+// accumulator in TMEM; four per 64-deep k-block) on one shared-memory stage laid
+// out exactly as the GEMM's (A K-major with the 128-byte swizzle, B N-major in
+// 64-column boxes), with no loads and no epilogue.  The operands are bf16
+// values of magnitude [0.5, 1) with hashed signs and mantissas, so the
+// multipliers switch as they do on real data (zeros would draw less power and
+// overstate the clock).  2 * 128 * 256 * 16 flop per MMA.
+constexpr int kPeakThreads = 128;
+constexpr std::size_t kPeakSmem = 120 * 1024;  // more than half an SM's shared memory: one CTA per SM
+
+__global__ void __launch_bounds__(kPeakThreads, 1) mma_peak_kernel(int iters) {
+  pdl_entry();
+  using C = Cfg<false>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + C::A_STAGE;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sb + C::B_STAGE);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  volatile uint32_t* abort_word = tmem_slot + 1;
+  static_assert(C::A_STAGE + C::B_STAGE + 1024 + 64 <= kPeakSmem, "probe shared memory");
+  uint32_t* w = reinterpret_cast<uint32_t*>(smem);
+  for (int i = static_cast<int>(threadIdx.x); i < (C::A_STAGE + C::B_STAGE) / 4; i += kPeakThreads) {
+    uint32_t h = static_cast<uint32_t>(i) * 2654435761u;
+    h ^= h >> 15;
+    h *= 2246822519u;
+    h ^= h >> 13;
+    const uint32_t lo = ((h & 1u) << 15) | (126u << 7) | ((h >> 1) & 0x7Fu);
+    const uint32_t hi = (((h >> 8) & 1u) << 15) | (126u << 7) | ((h >> 9) & 0x7Fu);
+    w[i] = lo | (hi << 16);
+  }
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    *abort_word = 0u;
+    mbar_init(smem_u32(bar), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x < 32) tmem_alloc<false>(smem_u32(tmem_slot));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) {
+    const uint32_t a_base = smem_u32(sa), b_base = smem_u32(sb);
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int k = 0; k < C::BK / C::UMMA_K; ++k) {
+        const uint64_t adesc = smem_desc(a_base + k * 32, 16, 1024);
+        const uint64_t bdesc = smem_desc(b_base + k * (C::UMMA_K * 128), C::B_BOX_BYTES, 1024);
+        umma<false, false>(tmem, adesc, bdesc, (it | k) != 0 ? 1u : 0u);
+      }
+    }
+    // every MMA issued above has completed once the barrier's phase 0 does;
+    // on a timeout (recorded, site 10) wait once more before TMEM is freed
+    umma_commit_self<false>(smem_u32(bar));
+    if (!wait_bounded(smem_u32(bar), 0u, abort_word, kSitePeak, false))
+      wait_bounded(smem_u32(bar), 0u, abort_word, kSitePeak, false);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc<false>(tmem);
+}
 }  // namespace
+
+double mma_peak_flops_per_cta_iter() { return 4.0 * 2.0 * 128.0 * 256.0 * 16.0; }
+
+int launch_mma_peak(int64_t ctas, int iters, cudaStream_t s) {
+  static std::once_flag once;
+  static cudaError_t attr = cudaSuccess;
+  std::call_once(once, [] {
+    attr = cudaFuncSetAttribute(mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(kPeakSmem));
+  });
+  if (attr != cudaSuccess)
+    return fail(MCKE_CUDA_ERROR, "mcke_sm100_peak_mma_bf16: shared memory attribute: %s", cudaGetErrorString(attr));
+  launch_async(mma_peak_kernel, static_cast<unsigned>(ctas), kPeakThreads, kPeakSmem, s, iters);
+  return MCKE_OK;
+}
 
 int launch_watchdog_selftest(cudaStream_t s) {
   launch_async(watchdog_selftest_kernel, 1, 32, 0, s);

@@ -15,10 +15,14 @@
 // independent chains per thread of acc = fma(acc, m, b) with m = 0.999,
 // b = 1.0 (a contraction toward 1000: never overflows, never subnormal), seeds
 // from device memory and one store per thread, so nothing folds away; 8 blocks
-// of 256 threads per SM.
+// of 256 threads per SM.  The tensor-core probe (the bf16 denominator from this
+// library's own MMAs) lives with the GEMM kernel, whose instruction and
+// descriptor helpers it uses; its entry points are here with the others.
 #include "mcke_common.cuh"
 
 namespace mcke_sm100 {
+double mma_peak_flops_per_cta_iter();
+int launch_mma_peak(int64_t ctas, int iters, cudaStream_t s);
 namespace {
 
 constexpr int kThreads = 256;
@@ -120,5 +124,21 @@ extern "C" int mcke_sm100_peak_fma_f32(const float* seed, float* out, int64_t th
   if (threads % kThreads != 0 || threads / kThreads > 2147483647LL)
     return fail(MCKE_INVALID_ARGUMENT, "%s: threads must be a multiple of %d", who, kThreads);
   launch_async(fma_kernel, static_cast<unsigned>(threads / kThreads), kThreads, 0, reinterpret_cast<cudaStream_t>(stream), seed, out, iters);
+  return check_launch(who);
+}
+
+extern "C" int64_t mcke_sm100_peak_mma_ctas(void) { return static_cast<int64_t>(sm_count()); }
+
+extern "C" double mcke_sm100_peak_mma_flops(int64_t ctas, int iters) {
+  return ctas > 0 && iters > 0 ? static_cast<double>(ctas) * iters * mma_peak_flops_per_cta_iter() : 0.0;
+}
+
+extern "C" int mcke_sm100_peak_mma_bf16(int64_t ctas, int iters, mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_peak_mma_bf16";
+  clear_error();
+  if (ctas == 0 || iters == 0) return MCKE_OK;
+  if (ctas < 0 || iters < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
+  if (ctas > 65535) return fail(MCKE_INVALID_ARGUMENT, "%s: at most 65535 CTAs", who);
+  MCKE_RETURN_IF(launch_mma_peak(ctas, iters, reinterpret_cast<cudaStream_t>(stream)));
   return check_launch(who);
 }

@@ -68,6 +68,9 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_peak_copy_f32": (i32, [vp, vp, i64, vp]),
             "mcke_sm100_peak_fma_threads": (i64, []),
             "mcke_sm100_peak_fma_f32": (i32, [vp, vp, i64, i32, vp]),
+            "mcke_sm100_peak_mma_ctas": (i64, []),
+            "mcke_sm100_peak_mma_flops": (ctypes.c_double, [i64, i32]),
+            "mcke_sm100_peak_mma_bf16": (i32, [i64, i32, vp]),
             "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
             "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),
             "mcke_sm100_activation_f32": (i32, [vp, vp, i64, i32, i32, vp]),
@@ -177,6 +180,19 @@ def peak_fma(seed, out, iters: int, stream=None):
     _need(seed, torch.float32, "seed"); _need(out, torch.float32, "out")
     _check(lib().mcke_sm100_peak_fma_f32(_ptr(seed), _ptr(out), seed.numel(), int(iters), _stream(seed, stream)))
     return out
+
+
+def peak_mma_ctas() -> int:
+    return lib().mcke_sm100_peak_mma_ctas()
+
+
+def peak_mma_flops(ctas: int, iters: int) -> float:
+    return lib().mcke_sm100_peak_mma_flops(int(ctas), int(iters))
+
+
+def peak_mma(ctas: int, iters: int, stream=None):
+    """The tcgen05 bf16 probe (mcke_sm100_peak_mma_bf16) on the current stream."""
+    _check(lib().mcke_sm100_peak_mma_bf16(int(ctas), int(iters), _stream(None, stream)))
 
 
 # ---- bias + activation -------------------------------------------------------

@@ -88,3 +88,12 @@ def test_workspace_queries(mcke):
     assert l.mcke_sm100_reduce_full_workspace_bytes(4096 * 5 + 1) == 6 * 24
     assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 1) == 0
     assert l.mcke_sm100_reduce_row_workspace_bytes(64, 1 << 19, 2) == 64 * 19 * 8
+
+
+def test_mma_probe_arguments_need_no_device(mcke):
+    l = mcke.lib()
+    assert l.mcke_sm100_peak_mma_flops(148, 10) == 148 * 10 * 4 * 2 * 128 * 256 * 16
+    assert l.mcke_sm100_peak_mma_flops(0, 10) == 0.0
+    assert l.mcke_sm100_peak_mma_bf16(-1, 10, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_peak_mma_bf16(70000, 10, None) == mcke.INVALID_ARGUMENT
+    assert l.mcke_sm100_peak_mma_bf16(0, 10, None) == mcke.OK  # nothing to launch

@@ -597,6 +597,24 @@ def test_peak_probes():
     np.testing.assert_allclose(out.cpu().numpy(), want, rtol=1e-5)
 
 
+def test_tcgen05_peak_probe_runs_at_tensor_rate():
+    # the bf16 probe completes (its bounded wait did not expire) and runs at a
+    # tensor-core rate: between a third of and 10% above the nominal dense peak
+    ctas = mcke.peak_mma_ctas()
+    assert ctas == torch.cuda.get_device_properties(DEV).multi_processor_count
+    mcke.peak_mma(ctas, 200)  # warm-up
+    mcke.check_device_errors()
+    iters = 4000
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    mcke.peak_mma(ctas, iters)
+    e1.record()
+    torch.cuda.synchronize()
+    mcke.check_device_errors()
+    tflops = mcke.peak_mma_flops(ctas, iters) / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    assert 750.0 < tflops < 2475.0, tflops
+
+
 @pytest.mark.parametrize("m,n,k", [(8192, 4096, 4096), (4096, 8192, 2048), (2048, 4096, 1024), (8192, 1024, 2048),
                                    (300, 512, 256)])
 def test_gemm_plan_matches_the_launch(m, n, k):

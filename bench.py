@@ -982,6 +982,9 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "ms_per_run": round(tot / ds, 3), "branches": branches, "rows_per_gpu": rows,
             "frac_of_bf16_peak": round(flops / g / (tot / ds * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
             "checked": checked, "memory": mem,
+            # the reference's cost-model ratio: sum over this GPU's nodes of
+            # max(flops / bf16 sustained, bytes / HBM copy) over the measured run
+            "cost_model_ratio": round(gr.roofline_ms(peaks["bf16_tflops_sustained"], peaks["hbm_gbs"]) / (tot / ds), 4),
             "peak": peaks["bf16_tflops_sustained"], "peak_kind": "bf16_tflops_sustained (multi-kernel step)",
             "note": ("GEMM1 with fused bias+GELU (bf16 out) -> GEMM2 with fused +b2 -> softmax" if fused else
                      "GEMM1 -> bias+GELU -> GEMM2 -> +b2 -> softmax, one kernel each") +

@@ -51,6 +51,11 @@ int mcke_graph_add_reduce_row(mcke_graph* g, const char* name, uint32_t x, int k
 int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint32_t* out);
 int mcke_graph_mark_output(mcke_graph* g, uint32_t t);
 int mcke_graph_finalize(mcke_graph* g);
+/* The reference's cost model (include/mcke/graph/cost_model.hpp): the sum over
+ * the graph's nodes of max(flops / peak, bytes / bandwidth) on the graph's
+ * global shapes, in ms -- a sequential lower bound for one run on one device.
+ * Peaks in TFLOP/s and GB/s, both > 0. */
+int mcke_graph_roofline_ms(const mcke_graph* g, double peak_tflops, double peak_gbs, double* ms_out);
 
 /* GraphExecutor (executor.hpp:283) over `num_devices` GPUs. */
 mcke_executor* mcke_executor_create(mcke_graph* g, const int* devices, int num_devices, int streams_per_device);

@@ -5,6 +5,7 @@
 #include <memory>
 #include <string>
 
+#include "mcke/graph/cost_model.hpp"
 #include "mcke/graph/executor.hpp"
 #include "mcke/memory/buddy_allocator.hpp"
 
@@ -108,6 +109,12 @@ int mcke_graph_add_reduce_full(mcke_graph* g, const char* name, uint32_t x, uint
 
 int mcke_graph_mark_output(mcke_graph* g, uint32_t t) { return g ? ret(g->g.mark_output(t)) : 2; }
 int mcke_graph_finalize(mcke_graph* g) { return g ? ret(g->g.finalize()) : 2; }
+
+int mcke_graph_roofline_ms(const mcke_graph* g, double peak_tflops, double peak_gbs, double* ms_out) {
+  if (!g || !ms_out || !(peak_tflops > 0.0) || !(peak_gbs > 0.0)) return 2;
+  *ms_out = mcke::graph_roofline_ms(g->g, mcke::Roofline{peak_tflops * 1e12, peak_gbs * 1e9});
+  return 0;
+}
 
 mcke_executor* mcke_executor_create_policy(mcke_graph* g, const int* devices, int num_devices, int num_streams,
                                            unsigned flags, int schedule, int memory) {

@@ -45,6 +45,7 @@ def lib() -> ctypes.CDLL:
             "mcke_graph_add_reduce_full": (i32, [vp, cp, u32, u32p]),
             "mcke_graph_mark_output": (i32, [vp, u32]),
             "mcke_graph_finalize": (i32, [vp]),
+            "mcke_graph_roofline_ms": (i32, [vp, ctypes.c_double, ctypes.c_double, ctypes.POINTER(ctypes.c_double)]),
             "mcke_executor_create": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32]),
             "mcke_executor_create_ex": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32, ctypes.c_uint]),
             "mcke_executor_destroy": (None, [vp]),
@@ -147,6 +148,13 @@ class Graph:
 
     def finalize(self) -> None:
         _check(lib().mcke_graph_finalize(self._h))
+
+    def roofline_ms(self, peak_tflops: float, peak_gbs: float) -> float:
+        """Sum over nodes of max(flops / peak, bytes / bandwidth), in ms (the
+        reference's cost-model lower bound of one sequential run)."""
+        ms = ctypes.c_double()
+        _check(lib().mcke_graph_roofline_ms(self._h, float(peak_tflops), float(peak_gbs), ctypes.byref(ms)))
+        return ms.value
 
 
 class Executor:

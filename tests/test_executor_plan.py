@@ -200,3 +200,24 @@ def test_too_few_rows_to_split(host):
     ex = host.Executor(g, devices=[0, 1, 2, 3])
     with pytest.raises(host.MckeError):
         ex.plan_dry()
+
+
+def test_graph_roofline_bound_is_the_reference_cost_model(host):
+    # sum over nodes of max(flops / peak, bytes / bandwidth): a bf16 GEMM with a
+    # fused epilogue (flop-bound here) and a softmax (byte-bound)
+    m, k, n = 512, 256, 1024
+    g = host.Graph()
+    x = g.input("x", (m, k), "bf16")
+    w = g.input("w", (k, n), "bf16")
+    b = g.input("b", (n,), "f32")
+    y = g.gemm(x, w, bias=b, name="gemm")  # f32 output
+    g.output(g.softmax(y, name="softmax"))
+    g.finalize()
+    tf, gbs = 100.0, 1000.0
+    gemm_flops = 2 * m * n * k
+    gemm_bytes = (m * k + k * n) * 2 + m * n * 4 + n * 4
+    soft_bytes = 2 * m * n * 4
+    soft_flops = 5 * m * n
+    want = (max(gemm_flops / (tf * 1e12), gemm_bytes / (gbs * 1e9)) +
+            max(soft_flops / (tf * 1e12), soft_bytes / (gbs * 1e9))) * 1e3
+    assert g.roofline_ms(tf, gbs) == pytest.approx(want, rel=1e-12)

@@ -729,6 +729,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
     steps = max(3, min(args.steps, 50))
     warm = max(3, min(args.warmup, 5))
     ffma_peak = None  # set by the peaks op
+    mma_peak = None   # the tcgen05 bf16 probe's rate, set by the peaks op
 
     from mcke import shard as mshard
 
@@ -783,6 +784,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                     "mcke_sm100_peak_mma_bf16: one CTA per SM, 20000 x 4 MMAs of 128 x 256 x 16 from shared "
                     "memory (no loads), against the driver's cuBLAS burst and the nominal dense 2250 TFLOP/s"}
         ffma_peak = ffma
+        mma_peak = mma
 
     if "bias_gelu" in want:
         r0, r1 = shard(BIAS_ROWS)
@@ -908,6 +910,7 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "value": round(GEMM_FLOPS * steps / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "scaling": "strong",
             "per_gpu_achieved": round(ach, 1), "frac_of_bf16_peak": round(ach / peaks["bf16_tflops"], 4),
             "peak": peaks["bf16_tflops"], "kernel_ms": round(kms, 4), "parallelism": f"columns of B and C over {g}",
+            "frac_of_tcgen05_probe": round(ach / mma_peak, 4) if mma_peak else None,
             "checked": checked}
         del a, b, c
 

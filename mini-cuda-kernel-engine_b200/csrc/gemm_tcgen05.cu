@@ -1255,7 +1255,7 @@ int max_pairs(KernelFn k) {
   return n;
 }
 
-bool ensure_smem_attr(KernelFn k, std::size_t bytes) {
+bool ensure_smem_attr(const void* k, std::size_t bytes) {
   // One attribute call per (kernel, device); cheap enough to keep a small table.
   static std::mutex mu;
   static const void* done_k[256];
@@ -1265,12 +1265,12 @@ bool ensure_smem_attr(KernelFn k, std::size_t bytes) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(mu);
   for (int i = 0; i < n_done; ++i)
-    if (done_k[i] == reinterpret_cast<const void*>(k) && done_d[i] == dev) return true;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(k), cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (done_k[i] == k && done_d[i] == dev) return true;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(bytes)) != cudaSuccess)
     return false;
   if (n_done < 256) {
-    done_k[n_done] = reinterpret_cast<const void*>(k);
+    done_k[n_done] = k;
     done_d[n_done] = dev;
     ++n_done;
   }
@@ -1427,7 +1427,8 @@ int launch_tc(const void* a, const void* b, const void* alo, const void* blo, vo
   if (kernel_out) *kernel_out = reinterpret_cast<const void*>(kfn);
   if (smem_out) *smem_out = smem;
   if (m == 0 || n == 0) return MCKE_OK;
-  if (!ensure_smem_attr(kfn, smem)) return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cannot set shared memory size");
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(kfn), smem))
+    return fail(MCKE_CUDA_ERROR, "gemm (tcgen05): cannot set shared memory size");
   using C1 = Cfg<false, kTf32, false, kSplit>;
   CUtensorMap ta, tb, talo, tblo;
   if constexpr (kSplit) {
@@ -1686,14 +1687,8 @@ __global__ void __launch_bounds__(kPeakThreads, 1) mma_peak_kernel(int iters) {
 double mma_peak_flops_per_cta_iter() { return 4.0 * 2.0 * 128.0 * 256.0 * 16.0; }
 
 int launch_mma_peak(int64_t ctas, int iters, cudaStream_t s) {
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(kPeakSmem));
-  });
-  if (attr != cudaSuccess)
-    return fail(MCKE_CUDA_ERROR, "mcke_sm100_peak_mma_bf16: shared memory attribute: %s", cudaGetErrorString(attr));
+  if (!ensure_smem_attr(reinterpret_cast<const void*>(mma_peak_kernel), kPeakSmem))
+    return fail(MCKE_CUDA_ERROR, "mcke_sm100_peak_mma_bf16: cannot set shared memory size");
   launch_async(mma_peak_kernel, static_cast<unsigned>(ctas), kPeakThreads, kPeakSmem, s, iters);
   return MCKE_OK;
 }

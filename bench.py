@@ -283,6 +283,7 @@ class CpuBaselines:
         return [(i, min(n, i + step)) for i in range(0, n, step)]
 
     def _time(self, work, items) -> tuple[float, int]:
+        items = list(items)
         list(self.pool.map(work, items))  # untimed first pass
         reps, total = 0, 0.0
         while reps < 2 or (total < self.budget and reps < 50):
@@ -290,11 +291,24 @@ class CpuBaselines:
             list(self.pool.map(work, items))
             total += time.perf_counter() - t0
             reps += 1
+        # the same function on one item (one thread's share, the items are equal
+        # in size) on this thread alone, best of two: the single-thread figure
+        single = float("inf")
+        for _ in range(2):
+            t0 = time.perf_counter()
+            work(items[0])
+            single = min(single, time.perf_counter() - t0)
+        self._last = (total / reps, len(items), single)
         return total / reps, reps
 
     def _entry(self, value: float, unit: str, sample: str) -> dict:
-        return {"value": round(value, 4 if value < 10 else 2), "unit": unit, "cores": self.threads,
-                "kind": self.impl, "sample": sample}
+        sec, n_items, single = self._last
+        one = value * sec / (n_items * single)  # work of one item / its single-thread time
+        nd = 4 if value < 10 else 2
+        return {"value": round(value, nd), "unit": unit, "cores": self.threads, "kind": self.impl,
+                "sample": sample,
+                "single_thread": {"value": round(one, 4 if one < 10 else 2), "unit": unit, "cores": 1,
+                                  "sample": "one thread's share of the same pass, run alone on one thread"}}
 
     def _uniform(self, *shape) -> np.ndarray:
         return self.rng.random(shape, dtype=np.float32) * np.float32(2) - np.float32(1)

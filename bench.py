@@ -304,10 +304,10 @@ class CpuBaselines:
     def _entry(self, value: float, unit: str, sample: str) -> dict:
         sec, n_items, single = self._last
         one = value * sec / (n_items * single)  # work of one item / its single-thread time
-        nd = 4 if value < 10 else 2
-        return {"value": round(value, nd), "unit": unit, "cores": self.threads, "kind": self.impl,
+        sig = lambda v: float(f"{v:.4g}")  # noqa: E731  (4 significant figures: GEMM rates are ~1e-3 TFLOP/s)
+        return {"value": sig(value), "unit": unit, "cores": self.threads, "kind": self.impl,
                 "sample": sample,
-                "single_thread": {"value": round(one, 4 if one < 10 else 2), "unit": unit, "cores": 1,
+                "single_thread": {"value": sig(one), "unit": unit, "cores": 1,
                                   "sample": "one thread's share of the same pass, run alone on one thread"}}
 
     def _uniform(self, *shape) -> np.ndarray:

@@ -116,3 +116,26 @@ def test_buddy_arena_matches_cudamalloc_arena():
         del ex
     for a, b in zip(runs[False], runs[True]):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_gate_fails_on_a_nondeterministic_op(tmp_path):
+    # The gate's failure path, as the reference tests it: a C++ program defines
+    # an op whose output changes on every launch and one that copies; the gate
+    # must fail the first (naming the output and the word) and pass the second.
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    pkg = os.path.join(root, "mini-cuda-kernel-engine_b200")
+    cuda = "/usr/local/cuda"
+    exe = str(tmp_path / "gate_check")
+    cmd = ["g++", "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror",
+           os.path.join(root, "tests", "cpp", "numerics_gate_check.cpp"), "-o", exe,
+           "-I", os.path.join(pkg, "host", "include"), "-I", os.path.join(root, "include"),
+           "-I", os.path.join(cuda, "include"), "-L", os.path.join(pkg, "lib"), "-lmcke_host",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart",
+           "-Wl,-rpath," + os.path.join(pkg, "lib"), "-Wl,-rpath," + os.path.join(cuda, "lib64")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr
+    assert "nondeterministic op: [" in r.stdout and "word" in r.stdout, r.stdout

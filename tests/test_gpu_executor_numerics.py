@@ -139,3 +139,26 @@ def test_gate_fails_on_a_nondeterministic_op(tmp_path):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr
     assert "nondeterministic op: [" in r.stdout and "word" in r.stdout, r.stdout
+
+
+def test_buddy_allocator_keeps_a_block_from_another_stream_until_its_work_is_done(tmp_path):
+    # The reference's stream-safety question for its pools, asked of this
+    # repository's BuddyAllocator over device slabs (tests/cpp/stream_reuse_check.cpp):
+    # a block freed on stream A while A still reads it goes to stream A again
+    # at once but not to stream B, and A's reader sees its data intact.
+    import os
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    pkg = os.path.join(root, "mini-cuda-kernel-engine_b200")
+    cuda = "/usr/local/cuda"
+    exe = str(tmp_path / "stream_reuse_check")
+    cmd = ["g++", "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror",
+           os.path.join(root, "tests", "cpp", "stream_reuse_check.cpp"), "-o", exe,
+           "-I", os.path.join(pkg, "host", "include"), "-I", os.path.join(root, "include"),
+           "-I", os.path.join(cuda, "include"), "-L", os.path.join(pkg, "lib"), "-lmcke_host", "-lmcke_sm100a",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart",
+           "-Wl,-rpath," + os.path.join(pkg, "lib"), "-Wl,-rpath," + os.path.join(cuda, "lib64")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr

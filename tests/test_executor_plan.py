@@ -221,3 +221,43 @@ def test_graph_roofline_bound_is_the_reference_cost_model(host):
     want = (max(gemm_flops / (tf * 1e12), gemm_bytes / (gbs * 1e9)) +
             max(soft_flops / (tf * 1e12), soft_bytes / (gbs * 1e9))) * 1e3
     assert g.roofline_ms(tf, gbs) == pytest.approx(want, rel=1e-12)
+
+
+def _flops_bytes(g):
+    # the cost model's two terms of a one-node graph: with a huge bandwidth the
+    # bound is flops / peak, with a huge peak it is bytes / bandwidth
+    big = 1e30
+    flops = g.roofline_ms(1.0, big) * 1e-3 * 1e12
+    byts = g.roofline_ms(big, 1.0) * 1e-3 * 1e9
+    return round(flops), round(byts)
+
+
+@pytest.mark.parametrize("case", ["gemm_f32", "bias_none", "bias_relu", "bias_gelu_tanh", "bias_gelu_erf",
+                                  "softmax", "reduce_sum", "reduce_max"])
+def test_op_costs_match_the_reference_formulas(host, case):
+    # The reference pins each op's cost (src/graph/ops_gemm.cpp:69-70,
+    # ops_bias_act.cpp:51-97, ops_softmax.cpp:62-63, ops_reduce.cpp:91-92);
+    # the same formulas here, through the graph-level bound.
+    m, k, n = 96, 40, 72
+    g = host.Graph()
+    if case == "gemm_f32":
+        a, b = g.input("a", (m, k)), g.input("b", (k, n))
+        g.output(g.gemm(a, b, name="op"))
+        want = (2 * m * n * k, (m * k + k * n + m * n) * 4)
+    elif case.startswith("bias"):
+        act = case[len("bias_"):]
+        x, bias = g.input("x", (m, n)), g.input("bias", (n,))
+        g.output(g.bias_act(x, bias, act, name="op"))
+        per = {"none": 1, "relu": 2, "gelu_tanh": 10, "gelu_erf": 22}[act]
+        want = (m * n * per, 2 * m * n * 4 + n * 4)
+    elif case == "softmax":
+        x = g.input("x", (m, n))
+        g.output(g.softmax(x, name="op"))
+        want = (5 * m * n, 2 * m * n * 4)
+    else:
+        kind = case[len("reduce_"):]
+        x = g.input("x", (m, n))
+        g.output(g.reduce_row(x, {"sum": 0, "max": 1}[kind], name="op"))  # ReduceParams::Kind
+        want = (0 if kind == "max" else m * (n - 1), (m * n + m) * 4)
+    g.finalize()
+    assert _flops_bytes(g) == want

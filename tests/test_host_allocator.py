@@ -91,3 +91,21 @@ def test_memory_policies(host):
     same = host.Executor(g, devices=[0], streams_per_device=2, memory="reuse_same_stream")
     same.plan_dry()
     assert reuse.arena_bytes(0) == same.arena_bytes(0) < per_tensor.arena_bytes(0)
+
+
+def test_memory_plan_fuzz_finds_no_unordered_reuse(host, tmp_path):
+    # tests/cpp/memory_plan_fuzz.cpp: 150 random DAGs x 3 schedules x 2 reuse
+    # policies x {1, 2, 4} streams, planned dry; every two tensors that share
+    # arena bytes must have one's whole life before the other's producer, on
+    # one stream (the reference's memory-plan race fuzz, run on this planner)
+    exe = str(tmp_path / "fuzz")
+    src = os.path.join(ROOT, "tests", "cpp", "memory_plan_fuzz.cpp")
+    cmd = ["g++", "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", src, "-o", exe,
+           "-I", os.path.join(PKG, "host", "include"), "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(CUDA, "include"), "-L", os.path.join(PKG, "lib"), "-lmcke_host",
+           "-Wl,-rpath," + os.path.join(PKG, "lib")]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr
+    assert "all ordered" in r.stdout

@@ -841,8 +841,12 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         part = torch.empty(24, dtype=torch.uint8, device=dev)
         nccl_ms = None
         p2p = None
+        # Timed: MCKE_REDUCE_EARLY_READ (each step's kernel reads x before
+        # waiting for the previous step's, which does not write x, so the
+        # steps overlap); the default wait-first path is timed beside it.
         if g == 1:
-            launch = lambda: mcke.reduce_full(xr, out=res, workspace=ws)  # noqa: E731
+            launch = lambda: mcke.reduce_full(xr, out=res, workspace=ws, early_read=True)  # noqa: E731
+            launch_wait = lambda: mcke.reduce_full(xr, out=res, workspace=ws)  # noqa: E731
         else:
             # the NCCL all-gather of partials, timed for comparison; the
             # reported number uses the peer-to-peer combine kernel
@@ -853,7 +857,9 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             nccl_ms = ms_n / steps
             nccl_result = mcke.decode_result(res)
             p2p = mshard.P2PExchange(dev)
-            launch = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
+            launch = lambda: p2p.reduce_full(xr, r0, out=res, early_read=True)  # noqa: E731
+            launch_wait = lambda: p2p.reduce_full(xr, r0, out=res)  # noqa: E731
+        ms_wait = timed_back_to_back(torch, dist, lambda i: launch_wait(), steps, warm)
         ms = timed_back_to_back(torch, dist, lambda i: launch(), steps, warm)
         torch.cuda.synchronize()
         checked = check_reduce(torch, dist, xr, r0, res.cpu().numpy().tobytes())
@@ -875,6 +881,9 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
             "per_gpu_achieved": round(ach, 1), "frac_of_hbm": round(ach / peaks["hbm_gbs"], 4),
             "step_ms": round(kms, 5), "cold_step_ms": round(cold, 5),
             "timing": "back to back (the 2^28 / N float input is >= 128 MiB per rank)",
+            "input_read": "MCKE_REDUCE_EARLY_READ: a step's kernel streams x before waiting for the previous "
+                          "step's kernel (which does not write x) and writes only after it",
+            "wait_first_step_ms": round(ms_wait / steps, 5),
             "exchange": "peer stores of 24-byte partials over NVLink (one kernel)" if g > 1 else None,
             "nccl_allgather_step_ms": round(nccl_ms, 5) if nccl_ms is not None else None,
             "p2p_result_matches_nccl": p2p_matches, "checked": checked,

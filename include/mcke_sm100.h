@@ -50,6 +50,17 @@ typedef enum { MCKE_ACT_NONE = 0, MCKE_ACT_RELU = 1, MCKE_ACT_GELU_ERF = 2, MCKE
 typedef enum { MCKE_REDUCE_SUM = 0, MCKE_REDUCE_MAX = 1, MCKE_REDUCE_MEAN = 2 } mcke_reduce_kind;
 /* include/mcke/kernels/kernels.hpp:180 ReduceVariant, same values. */
 typedef enum { MCKE_REDUCE_SMEM_TREE = 0, MCKE_REDUCE_WARP_SHUFFLE = 1, MCKE_REDUCE_TWO_PASS = 2 } mcke_reduce_variant;
+/* Flags of the full-vector reduce's _ex entry points (new).
+ * MCKE_REDUCE_EARLY_READ: the caller guarantees that x is not written by the
+ * kernel enqueued immediately before the call on the same stream.  The kernel
+ * then reads x before waiting for that kernel and waits only before its first
+ * write, so back-to-back reduces overlap (one call's fold and exchange with the
+ * next call's read of x).  Every earlier writer of x has completed by then:
+ * each kernel of this library lets its successor start only after its own
+ * wait, and kernels launched without programmatic serialization (torch,
+ * cuBLAS, memcpy) complete before their successor starts.  Same result, same
+ * bits as without the flag. */
+#define MCKE_REDUCE_EARLY_READ 1u
 /* include/mcke/kernels/kernels.hpp:218 SoftmaxVariant, same values.  ONLINE
  * selects the single-read register-resident kernel whenever a row fits
  * (cols % 4 == 0, 16-byte aligned rows, cols <= 16384), else the two-read
@@ -195,6 +206,11 @@ size_t mcke_sm100_reduce_full_workspace_bytes(int64_t n);
  * order depends on n only. */
 int mcke_sm100_reduce_full_f32(const float* x, int64_t n, mcke_reduce_result* out,
                                void* workspace, size_t workspace_bytes, mcke_stream_t stream);
+/* mcke_sm100_reduce_full_f32 with flags (0 or MCKE_REDUCE_EARLY_READ; other
+ * bits are rejected with MCKE_INVALID_ARGUMENT). */
+int mcke_sm100_reduce_full_f32_ex(const float* x, int64_t n, mcke_reduce_result* out,
+                                  void* workspace, size_t workspace_bytes, unsigned flags,
+                                  mcke_stream_t stream);
 /* The same over one shard x[0..n) whose first element has global index
  * index_base; writes one mcke_reduce_partial. */
 int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_base,
@@ -226,6 +242,11 @@ size_t mcke_sm100_reduce_p2p_buffer_bytes(int world);
 int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t index_base,
                                    void* const* peer_buffers, int world, int rank, uint64_t epoch,
                                    mcke_reduce_result* out, mcke_stream_t stream);
+/* mcke_sm100_reduce_full_p2p_f32 with flags (0 or MCKE_REDUCE_EARLY_READ;
+ * other bits are rejected with MCKE_INVALID_ARGUMENT). */
+int mcke_sm100_reduce_full_p2p_f32_ex(const float* x, int64_t n, int64_t index_base,
+                                      void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                      mcke_reduce_result* out, unsigned flags, mcke_stream_t stream);
 /* New, a measuring aid (no counterpart in the reference): the same call, which
  * also records when its phases happened, as %globaltimer nanoseconds, into
  * `stamps` (8 words of device memory, 8-byte aligned; n > 0).  The caller sets

@@ -287,13 +287,21 @@ __device__ void p2p_publish_and_combine(const Part& mine, const P2pArgs& a, Part
   }
 }
 
-template <bool kP2p>
+// kEarly (MCKE_REDUCE_EARLY_READ): x is not written by the kernel launched just
+// before on the stream, so the CTAs read it before waiting for that kernel and
+// wait only before their first global write (the partial slots, the arrival
+// count, the tag).  Every kernel of this library lets its successor start only
+// after its own wait, and a kernel launched without programmatic serialization
+// completes before its successor starts, so every earlier writer of x has
+// completed by then.  Consecutive calls then overlap: the next call's CTAs
+// stream while this call's last CTA folds and exchanges.
+template <bool kP2p, bool kEarly = false>
 __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const float* __restrict__ x, int64_t n,
                                                                       int64_t head, long long base,
                                                                       Part* __restrict__ parts, P2pArgs p2p_in) {
   unsigned long long* const stamps = kP2p ? p2p_in.stamps : nullptr;
   if (kP2p && stamps && threadIdx.x == 0) atomicMin(stamps + kStampFirstEntry, global_ns());
-  pdl_entry();
+  if constexpr (!kEarly) pdl_entry();
   if (kP2p && stamps && threadIdx.x == 0) {
     const unsigned long long t = global_ns();
     atomicMin(stamps + kStampFirstStart, t);
@@ -356,6 +364,7 @@ __global__ void __launch_bounds__(kThreads, 3) reduce_full_stream_kernel(const f
   }
   if (blockIdx.x == 0 && tid == 0)
     for (int64_t e = head + 4 * nv; e < n; ++e) part_add(p, x[e], base + e);
+  if constexpr (kEarly) pdl_entry();  // the previous grid has completed: writes may start
   p = block_combine(p, red);
   if (!kP2p && tid == 0) parts[blockIdx.x] = p;
   if constexpr (kP2p) {
@@ -684,7 +693,8 @@ extern "C" size_t mcke_sm100_reduce_full_workspace_bytes(int64_t n) {
 
 namespace {
 int full_common(const char* who, const float* x, int64_t n, int64_t index_base, void* out,
-                void* workspace, size_t workspace_bytes, bool final_result, mcke_stream_t stream) {
+                void* workspace, size_t workspace_bytes, bool final_result, mcke_stream_t stream,
+                bool early = false) {
   if (!out) return fail(MCKE_INVALID_ARGUMENT, "%s: null output", who);
   if (n < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: negative extent", who);
   if (n > 0 && !x) return fail(MCKE_INVALID_ARGUMENT, "%s: null input", who);
@@ -709,7 +719,8 @@ int full_common(const char* who, const float* x, int64_t n, int64_t index_base, 
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   Part* parts = static_cast<Part*>(workspace);
-  launch_async(reduce_full_stream_kernel<false>, static_cast<unsigned>(g), kThreads, 0, s, x, n, head, index_base, parts, P2pArgs{});
+  launch_async(early ? reduce_full_stream_kernel<false, true> : reduce_full_stream_kernel<false>,
+               static_cast<unsigned>(g), kThreads, 0, s, x, n, head, index_base, parts, P2pArgs{});
   MCKE_RETURN_IF(check_launch(who));
   if (final_result) launch_async(reduce_full_combine_kernel<true>, 1, 1024, 0, s, parts, g, out);
   else launch_async(reduce_full_combine_kernel<false>, 1, 1024, 0, s, parts, g, out);
@@ -723,6 +734,17 @@ extern "C" int mcke_sm100_reduce_full_f32(const float* x, int64_t n, mcke_reduce
   clear_error();
   return full_common("mcke_sm100_reduce_full_f32", x, n, 0, out, workspace, workspace_bytes, true,
                      stream);
+}
+
+extern "C" int mcke_sm100_reduce_full_f32_ex(const float* x, int64_t n, mcke_reduce_result* out,
+                                             void* workspace, size_t workspace_bytes, unsigned flags,
+                                             mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_reduce_full_f32_ex";
+  clear_error();
+  if (flags & ~static_cast<unsigned>(MCKE_REDUCE_EARLY_READ))
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown flags 0x%x", who, flags);
+  return full_common(who, x, n, 0, out, workspace, workspace_bytes, true, stream,
+                     (flags & MCKE_REDUCE_EARLY_READ) != 0);
 }
 
 extern "C" int mcke_sm100_reduce_full_partial_f32(const float* x, int64_t n, int64_t index_base,
@@ -917,8 +939,10 @@ extern "C" size_t mcke_sm100_reduce_p2p_buffer_bytes(int world) {
 namespace {
 int reduce_full_p2p(const char* who, const float* x, int64_t n, int64_t index_base, void* const* peer_buffers,
                     int world, int rank, uint64_t epoch, mcke_reduce_result* out, uint64_t* stamps,
-                    mcke_stream_t stream) {
+                    mcke_stream_t stream, unsigned flags = 0) {
   clear_error();
+  if (flags & ~static_cast<unsigned>(MCKE_REDUCE_EARLY_READ))
+    return fail(MCKE_INVALID_ARGUMENT, "%s: unknown flags 0x%x", who, flags);
   if (!out || !peer_buffers) return fail(MCKE_INVALID_ARGUMENT, "%s: null output or peer table", who);
   if (world < 1 || world > 1024 || rank < 0 || rank >= world)
     return fail(MCKE_INVALID_ARGUMENT, "%s: bad world/rank %d/%d", who, world, rank);
@@ -945,7 +969,10 @@ int reduce_full_p2p(const char* who, const float* x, int64_t n, int64_t index_ba
   int64_t head = static_cast<int64_t>(((16 - addr % 16) % 16) / 4);
   if (head > n) head = n;
   // dynamic shared memory: the ranks' collected partials (world <= 1024: 24 KB)
-  launch_async(reduce_full_stream_kernel<true>, static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s, x, n, head, index_base, nullptr, a);
+  // (the timeline entry point passes no flags: its stamps are written from entry on)
+  launch_async((flags & MCKE_REDUCE_EARLY_READ) ? reduce_full_stream_kernel<true, true> : reduce_full_stream_kernel<true>,
+               static_cast<unsigned>(g), kThreads, static_cast<size_t>(world) * sizeof(Part), s, x, n, head,
+               index_base, nullptr, a);
   return check_launch(who);
 }
 }  // namespace
@@ -955,6 +982,13 @@ extern "C" int mcke_sm100_reduce_full_p2p_f32(const float* x, int64_t n, int64_t
                                               mcke_reduce_result* out, mcke_stream_t stream) {
   return reduce_full_p2p("mcke_sm100_reduce_full_p2p_f32", x, n, index_base, peer_buffers, world, rank, epoch, out,
                          nullptr, stream);
+}
+
+extern "C" int mcke_sm100_reduce_full_p2p_f32_ex(const float* x, int64_t n, int64_t index_base,
+                                                 void* const* peer_buffers, int world, int rank, uint64_t epoch,
+                                                 mcke_reduce_result* out, unsigned flags, mcke_stream_t stream) {
+  return reduce_full_p2p("mcke_sm100_reduce_full_p2p_f32_ex", x, n, index_base, peer_buffers, world, rank, epoch,
+                         out, nullptr, stream, flags);
 }
 
 extern "C" int mcke_sm100_reduce_full_p2p_f32_timeline(const float* x, int64_t n, int64_t index_base,

@@ -80,10 +80,13 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_reduce_row_f32": (i32, [vp, vp, i64, i64, i32, i32, vp, sz, vp]),
             "mcke_sm100_reduce_full_workspace_bytes": (sz, [i64]),
             "mcke_sm100_reduce_full_f32": (i32, [vp, i64, vp, vp, sz, vp]),
+            "mcke_sm100_reduce_full_f32_ex": (i32, [vp, i64, vp, vp, sz, ctypes.c_uint, vp]),
             "mcke_sm100_reduce_full_partial_f32": (i32, [vp, i64, i64, vp, vp, sz, vp]),
             "mcke_sm100_reduce_combine": (i32, [vp, i64, vp, vp]),
             "mcke_sm100_reduce_p2p_buffer_bytes": (sz, [i32]),
             "mcke_sm100_reduce_full_p2p_f32": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp]),
+            "mcke_sm100_reduce_full_p2p_f32_ex": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp,
+                                                        ctypes.c_uint, vp]),
             "mcke_sm100_reduce_full_p2p_f32_timeline": (i32, [vp, i64, i64, vp, i32, i32, ctypes.c_uint64, vp, vp,
                                                               vp]),
             "mcke_sm100_ipc_buffer_create": (i32, [sz, ctypes.POINTER(vp), vp]),
@@ -247,9 +250,15 @@ def reduce_full_workspace_bytes(n: int) -> int:
     return lib().mcke_sm100_reduce_full_workspace_bytes(n)
 
 
-def reduce_full(x, out=None, workspace=None, stream=None):
+REDUCE_EARLY_READ = 1  # MCKE_REDUCE_EARLY_READ
+
+
+def reduce_full(x, out=None, workspace=None, stream=None, early_read: bool = False):
     """sum/max/argmax of a float32 vector; returns a 16-byte uint8 device tensor
-    holding one mcke_reduce_result (decode with :func:`decode_result`)."""
+    holding one mcke_reduce_result (decode with :func:`decode_result`).
+    ``early_read``: the caller guarantees that ``x`` is not written by the
+    kernel enqueued just before on the stream (MCKE_REDUCE_EARLY_READ), so
+    back-to-back calls overlap; same result."""
     _need(x, torch.float32, "x")
     n = x.numel()
     dev = x.device
@@ -258,8 +267,12 @@ def reduce_full(x, out=None, workspace=None, stream=None):
     need = reduce_full_workspace_bytes(n)
     if workspace is None:
         workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=dev)
-    _check(lib().mcke_sm100_reduce_full_f32(_ptr(x), n, _ptr(out), _ptr(workspace),
-                                            workspace.numel(), _stream(x, stream)))
+    if early_read:
+        _check(lib().mcke_sm100_reduce_full_f32_ex(_ptr(x), n, _ptr(out), _ptr(workspace), workspace.numel(),
+                                                   REDUCE_EARLY_READ, _stream(x, stream)))
+    else:
+        _check(lib().mcke_sm100_reduce_full_f32(_ptr(x), n, _ptr(out), _ptr(workspace),
+                                                workspace.numel(), _stream(x, stream)))
     return out
 
 
@@ -284,16 +297,23 @@ def reduce_combine(partials, count: int, out=None, stream=None):
     return out
 
 
-def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch: int, out=None, stream=None):
+def reduce_full_p2p(x, index_base: int, peer_table, world: int, rank: int, epoch: int, out=None, stream=None,
+                    early_read: bool = False):
     """One rank's step of a sharded full reduce with the peer-to-peer combine
     (mcke_sm100_reduce_full_p2p_f32).  ``peer_table``: int64 CUDA tensor of the
     ranks' exchange-buffer addresses as mapped in this process; see
-    :class:`mcke.shard.P2PExchange`, which owns the buffers and the epochs."""
+    :class:`mcke.shard.P2PExchange`, which owns the buffers and the epochs.
+    ``early_read`` as for :func:`reduce_full`."""
     _need(x, torch.float32, "x")
     if out is None:
         out = torch.empty(RESULT_BYTES, dtype=torch.uint8, device=x.device)
-    _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), x.numel(), index_base, _ptr(peer_table), world, rank,
-                                                epoch, _ptr(out), _stream(x, stream)))
+    if early_read:
+        _check(lib().mcke_sm100_reduce_full_p2p_f32_ex(_ptr(x), x.numel(), index_base, _ptr(peer_table), world,
+                                                       rank, epoch, _ptr(out), REDUCE_EARLY_READ,
+                                                       _stream(x, stream)))
+    else:
+        _check(lib().mcke_sm100_reduce_full_p2p_f32(_ptr(x), x.numel(), index_base, _ptr(peer_table), world,
+                                                    rank, epoch, _ptr(out), _stream(x, stream)))
     return out
 
 

@@ -100,11 +100,11 @@ class P2PExchange:
         self.epoch = 0
         self._group = group
 
-    def reduce_full(self, x, index_base: int, out=None, stream=None):
+    def reduce_full(self, x, index_base: int, out=None, stream=None, early_read: bool = False):
         from . import reduce_full_p2p
         self.epoch += 1
         return reduce_full_p2p(x, index_base, self.table, self.world, self.rank, self.epoch, out=out,
-                               stream=stream)
+                               stream=stream, early_read=early_read)
 
     def close(self) -> None:
         """Collective: every rank's kernels are done before any buffer goes."""

@@ -73,6 +73,19 @@ def test_argument_validation_needs_no_device(mcke):
     assert b"stamps" in l.mcke_sm100_last_error_string()
     assert l.mcke_sm100_reduce_full_p2p_f32_timeline(bogus, 1000, 0, bogus, 1, 0, 1, bogus,
                                                       ctypes.c_void_p(0x1004), None) == mcke.INVALID_ARGUMENT
+    # the _ex entry points take MCKE_REDUCE_EARLY_READ (1) and nothing else
+    assert l.mcke_sm100_reduce_full_f32_ex(bogus, 1000, ctypes.c_void_p(0x2000), bogus, 1 << 20, 2,
+                                           None) == mcke.INVALID_ARGUMENT
+    assert b"unknown flags" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_reduce_full_f32_ex(bogus, 1000, ctypes.c_void_p(0x2000), None, 0, 1,
+                                           None) == mcke.INVALID_ARGUMENT
+    assert b"workspace" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_reduce_full_p2p_f32_ex(bogus, 1000, 0, bogus, 1, 0, 1, bogus, 0x80000000,
+                                               None) == mcke.INVALID_ARGUMENT
+    assert b"unknown flags" in l.mcke_sm100_last_error_string()
+    assert l.mcke_sm100_reduce_full_p2p_f32_ex(bogus, 1000, 0, bogus, 0, 0, 1, bogus, 1,
+                                               None) == mcke.INVALID_ARGUMENT
+    assert b"world" in l.mcke_sm100_last_error_string()
     # empty extents are OK with no launch
     assert l.mcke_sm100_softmax_f32(None, None, 0, 16, 1, None) == mcke.OK
     assert l.mcke_sm100_bias_act_f32(None, None, None, 0, 0, 3, 4, 0, None) == mcke.OK

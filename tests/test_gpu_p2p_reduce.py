@@ -151,8 +151,8 @@ def _rank_main(rank, world, port, n, q):
         x = torch.from_numpy(v[a:b]).cuda()
         ex = shard.P2PExchange(torch.device("cuda", rank))
         res = []
-        for _ in range(5):
-            res.append(mcke.decode_result(ex.reduce_full(x, a)))
+        for i in range(5):  # the last three read x before waiting (MCKE_REDUCE_EARLY_READ)
+            res.append(mcke.decode_result(ex.reduce_full(x, a, early_read=i >= 2)))
         torch.cuda.synchronize()
         mcke.check_device_errors()
         ex.close()

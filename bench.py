@@ -146,6 +146,9 @@ class ClockSampler:
         for k, name in enumerate(names):
             if any(r[6 + k].lower().startswith("active") for r in use):
                 out["reasons"].append(name)
+        out["window"] = ("one sampler over the headline's timed steps, the e2e pipeline and every ops entry "
+                         "(the headline's steps alone last less than the 200 ms sampling period); the median "
+                         "under load is set by the longest entries, the GEMMs, which run at the power cap")
         if not load:
             out["note"] = "no sample caught the GPU busy (timed region shorter than the 200 ms sampling period)"
         return out

@@ -1194,6 +1194,51 @@ def reduce_timeline(torch, mcke, dev, n: int, steps: int = 60) -> dict:
             "stamps_ordered": checks}
 
 
+def reduce_steps(torch, mcke, dev, lgs=(25, 28), steps: int = 60, reps: int = 2) -> dict:
+    """Back-to-back step time of the full reduce, waiting first against
+    MCKE_REDUCE_EARLY_READ, for the one-kernel peer-to-peer path at world 1
+    and the two-launch path: CUDA events around `steps` calls on one input
+    (which no call writes), the best of `reps` rounds that alternate the four
+    cases; every output checked against the default path's bits."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    buf = torch.zeros(mcke.lib().mcke_sm100_reduce_p2p_buffer_bytes(1), dtype=torch.uint8, device=dev)
+    table = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
+    out = torch.empty(16, dtype=torch.uint8, device=dev)
+    rows, same = {}, True
+    for lg in lgs:
+        x = torch.rand(1 << lg, generator=gen, device=dev) * 2 - 1
+        ws = torch.empty(mcke.reduce_full_workspace_bytes(x.numel()), dtype=torch.uint8, device=dev)
+        want = mcke.reduce_full(x).cpu().numpy().tobytes()
+        cases = {
+            "p2p_wait_first": lambda: mcke.reduce_full_p2p(x, 0, table, 1, 0, 0, out=out),
+            "p2p_early_read": lambda: mcke.reduce_full_p2p(x, 0, table, 1, 0, 0, out=out, early_read=True),
+            "two_launch_wait_first": lambda: mcke.reduce_full(x, out=out, workspace=ws),
+            "two_launch_early_read": lambda: mcke.reduce_full(x, out=out, workspace=ws, early_read=True),
+        }
+        best = {}
+        for _ in range(reps):
+            for name, fn in cases.items():
+                for _ in range(5):
+                    fn()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                for _ in range(steps):
+                    fn()
+                e1.record()
+                torch.cuda.synchronize()
+                same = same and out.cpu().numpy().tobytes() == want
+                us = e0.elapsed_time(e1) * 1e3 / steps
+                best[name] = min(best.get(name, us), us)
+        rows[f"2^{lg}"] = {k: {"step_us": round(v, 2), "gbs": round(4 * x.numel() / (v * 1e-6) / 1e9, 1)}
+                           for k, v in best.items()}
+        del x, ws
+    mcke.check_device_errors()
+    return {"case": f"full reduce, {steps} steps back to back on one input, best of {reps}", "steps": rows,
+            "same_bits_as_default": same}
+
+
 def run_profile(args) -> None:
     """One full-size launch of each named kernel after two warm-ups, for ncu
     (`ncu -k regex:... -s 2 -c 1 python bench.py --profile NAME`).  Sizes are
@@ -1261,6 +1306,10 @@ def run_profile(args) -> None:
             # back over three rotating inputs, each step's %globaltimer stamps.
             lg = int(name.split(":")[1]) if ":" in name else 25
             print(json.dumps(reduce_timeline(torch, mcke, dev, 1 << lg)))
+            continue
+        elif name == "reduce_steps":
+            # waiting first against MCKE_REDUCE_EARLY_READ, back to back
+            print(json.dumps(reduce_steps(torch, mcke, dev)))
             continue
         else:
             raise SystemExit(f"unknown profile case {name}")

@@ -1029,7 +1029,9 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         cpu = torch.Generator()
         cpu.manual_seed(7)
         modes = {}
-        for mode in ("eager", "graph"):
+        # eager and graph: the reference's per-node launches (chain-greedy over
+        # 4 streams); eager_level_grouped: one grouped launch per level
+        for mode in ("eager", "graph", "eager_level_grouped"):
             gr = mhost.Graph()
             x = gr.input("x", (fr, fc))
             feeds = {x: torch.randn(fr, fc, generator=cpu).numpy()}
@@ -1046,7 +1048,8 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
                 if b == 0:
                     last = h
             gr.finalize()
-            ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=(mode == "graph"))
+            ex = mhost.Executor(gr, devices=[dist.local], streams_per_device=4, cuda_graph=(mode == "graph"),
+                                schedule="level_grouped" if mode == "eager_level_grouped" else "chain_greedy")
             ex.plan()
             for t, arr in feeds.items():
                 ex.set_input(t, arr)
@@ -1081,10 +1084,15 @@ def run_ops(args, dist, torch, mcke, dev, flush, peaks, traffic) -> dict:
         gms = modes["graph"]["device_ms_per_run"]
         out["dag_fanout_4x4_2048x2048_f32"] = {
             "value": round(moved * g / (gms * 1e-3) / 1e9, 1), "unit": "GB/s", "scaling": "weak",
-            "checked": modes["eager"]["checked"] and modes["graph"]["checked"],
+            "checked": all(m["checked"] for m in modes.values()),
             "algorithmic_bytes_per_gpu": moved, "eager": modes["eager"], "graph": modes["graph"],
-            "note": "16 bias+GELU nodes on 4 streams of the C++ GraphExecutor; value from the CUDA-graph replay's "
-                    "device time (events around each launch, max over ranks); back_to_back is host wall clock"}
+            "eager_level_grouped": modes["eager_level_grouped"],
+            "host_enqueue_us_per_node": {k: round(m["host_enqueue_us_per_run"] / (fb * fd), 2) for k, m in modes.items()},
+            "note": "16 bias+GELU nodes of the C++ GraphExecutor: eager and graph on 4 streams (chain-greedy, one "
+                    "launch per node); eager_level_grouped on one stream with one grouped launch per level "
+                    "(SchedulePolicy::kLevelGrouped, mcke_sm100_bias_act_f32_group); value from the CUDA-graph "
+                    "replay's device time (events around each launch, max over ranks); back_to_back is host wall "
+                    "clock"}
 
     if "gemm_f32" in want:
         # fp32 operands: the tensor-core 3xTF32 kernel (reported), and the

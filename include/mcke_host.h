@@ -80,7 +80,8 @@ mcke_executor* mcke_executor_create_ex(mcke_graph* g, const int* devices, int nu
                                        unsigned flags);
 /* As mcke_executor_create_ex with the stream schedule (mcke::SchedulePolicy:
  * 0 sequential, 1 level-parallel, 2 chain-greedy; schedule.hpp:49 of the
- * reference) and the memory policy (mcke::MemoryPolicy: 0 alloc-per-tensor,
+ * reference; 3 level-grouped, added: stream 0 level by level, a level's fp32
+ * bias + activation nodes in grouped launches) and the memory policy (mcke::MemoryPolicy: 0 alloc-per-tensor,
  * 2 reuse-same-stream, 3 reuse-happens-before; memory_plan.hpp:67). */
 mcke_executor* mcke_executor_create_policy(mcke_graph* g, const int* devices, int num_devices, int num_streams,
                                            unsigned flags, int schedule, int memory);
@@ -100,6 +101,10 @@ int mcke_executor_describe(mcke_executor* e, char* buf, size_t len);
 int mcke_executor_placement(mcke_executor* e, uint32_t t, int* placement_out);
 int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_out);
 int mcke_executor_num_events(mcke_executor* e, size_t* out);
+/* Launch items of the plan, in enqueue order (after plan_dry or plan): their
+ * number, and the number of nodes in the largest (1 unless the schedule is
+ * level-grouped). */
+int mcke_executor_launch_items(mcke_executor* e, size_t* items_out, size_t* largest_out);
 /* The numerics gate (executor.hpp:268 of the reference, GraphExecutor::validate_numerics):
  * replays the graph under every schedule x memory policy x {eager, CUDA graph}
  * on this executor's devices, `repeats` runs each, and compares all outputs bit

@@ -169,6 +169,24 @@ int mcke_sm100_vector_add_f32(const float* a, const float* b, float* out, size_t
 int mcke_sm100_bias_act_f32(const float* x, const float* bias, float* y, int64_t rows,
                             int64_t cols, int act, int vector_width, int max_row_blocks,
                             mcke_stream_t stream);
+/* New (no counterpart in the reference): `count` independent fp32 bias +
+ * activation jobs in one launch, as the executor's grouped level schedule
+ * issues them.  Each job is mcke_sm100_bias_act_f32(x, bias, y, rows, cols,
+ * act, vector_width 4, max_row_blocks 0) with cols % 512 == 0 and x, bias, y
+ * 16-byte aligned; same bits as one such call per job.  The jobs run at the
+ * same time, so no job's y may overlap any job's x, bias or y (its own x
+ * included).  `jobs` is a host array; count 1 .. MCKE_BIAS_ACT_GROUP_MAX;
+ * empty jobs (rows or cols 0) are skipped.  Anything else is
+ * MCKE_INVALID_ARGUMENT, checked before any launch. */
+#define MCKE_BIAS_ACT_GROUP_MAX 16
+typedef struct {
+  const float* x;
+  const float* bias;
+  float* y;
+  int64_t rows;
+  int64_t cols;
+} mcke_bias_act_job;
+int mcke_sm100_bias_act_f32_group(const mcke_bias_act_job* jobs, int count, int act, mcke_stream_t stream);
 /* Replaces kernels.hpp:129 launch_bias_add_f32 (bias_act with MCKE_ACT_NONE). */
 int mcke_sm100_bias_add_f32(const float* x, const float* bias, float* y, int64_t rows,
                             int64_t cols, int vector_width, mcke_stream_t stream);

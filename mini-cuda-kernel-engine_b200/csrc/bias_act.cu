@@ -105,15 +105,12 @@ __global__ void __launch_bounds__(kThreads) bias_act_f32_kernel(const float* __r
 // (cpr_shift >= 0; config 1: 8) and from a 32-bit division otherwise: the
 // kernel is issue-bound, and a 64-bit division per thread is a ~70-instruction
 // subroutine.
+// One warp's 512-float chunk w of x[rows, chunks_per_row * 512].
 template <class F>
-__global__ void __launch_bounds__(kThreads) bias_act_f32_chunk_kernel(const float* __restrict__ x,
-                                                                      const float* __restrict__ bias,
-                                                                      float* __restrict__ y, uint32_t chunks,
-                                                                      uint32_t chunks_per_row, int cpr_shift) {
-  pdl_entry();
+__device__ __forceinline__ void bias_act_chunk(const float* __restrict__ x, const float* __restrict__ bias,
+                                               float* __restrict__ y, uint32_t w, uint32_t chunks_per_row,
+                                               int cpr_shift) {
   const int lane = threadIdx.x & 31;
-  const uint32_t w = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
-  if (w >= chunks) return;
   const uint32_t row = cpr_shift >= 0 ? w >> cpr_shift : w / chunks_per_row;
   const int64_t c0 = static_cast<int64_t>(w - row * chunks_per_row) * 512;
   const int64_t base = static_cast<int64_t>(w) * 512;
@@ -125,6 +122,42 @@ __global__ void __launch_bounds__(kThreads) bias_act_f32_chunk_kernel(const floa
 #pragma unroll
   for (int u = 0; u < 4; ++u)
     st_stream_f4(y + base + 4 * (lane + 32 * u), Vec<4>::template act_bias<F>(v[u], b[u]));
+}
+
+template <class F>
+__global__ void __launch_bounds__(kThreads) bias_act_f32_chunk_kernel(const float* __restrict__ x,
+                                                                      const float* __restrict__ bias,
+                                                                      float* __restrict__ y, uint32_t chunks,
+                                                                      uint32_t chunks_per_row, int cpr_shift) {
+  pdl_entry();
+  const uint32_t w = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  if (w >= chunks) return;
+  bias_act_chunk<F>(x, bias, y, w, chunks_per_row, cpr_shift);
+}
+
+// Up to kGroupMax independent jobs of the chunk kernel in one grid: job k
+// owns blocks [first_block[k], first_block[k + 1]).  Each chunk runs the same
+// code as in bias_act_f32_chunk_kernel, so the bits are the same.
+constexpr int kGroupMax = MCKE_BIAS_ACT_GROUP_MAX;
+struct BiasActGroup {
+  const float* x[kGroupMax];
+  const float* bias[kGroupMax];
+  float* y[kGroupMax];
+  uint32_t chunks[kGroupMax];
+  uint32_t per_row[kGroupMax];
+  int32_t shift[kGroupMax];
+  uint32_t first_block[kGroupMax + 1];
+  int count;
+};
+
+template <class F>
+__global__ void __launch_bounds__(kThreads) bias_act_f32_group_kernel(const __grid_constant__ BiasActGroup G) {
+  pdl_entry();
+  int k = 0;
+  while (k + 1 < G.count && G.first_block[k + 1] <= blockIdx.x) ++k;
+  const uint32_t w = (blockIdx.x - G.first_block[k]) * (kThreads / 32) + (threadIdx.x >> 5);
+  if (w >= G.chunks[k]) return;
+  bias_act_chunk<F>(G.x[k], G.bias[k], G.y[k], w, G.per_row[k], G.shift[k]);
 }
 
 // Activation only (the unfused half): flat grid-stride over n / VW vectors.
@@ -269,6 +302,72 @@ extern "C" int mcke_sm100_bias_act_f32(const float* x, const float* bias, float*
     case 4: launch_bias_act<4>(act, g, s, x, bias, y, rows, cols); break;
     case 2: launch_bias_act<2>(act, g, s, x, bias, y, rows, cols); break;
     default: launch_bias_act<1>(act, g, s, x, bias, y, rows, cols); break;
+  }
+  return check_launch(who);
+}
+
+namespace {
+bool overlaps(const void* a, std::size_t an, const void* b, std::size_t bn) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return an && bn && pa < pb + bn && pb < pa + an;
+}
+}  // namespace
+
+extern "C" int mcke_sm100_bias_act_f32_group(const mcke_bias_act_job* jobs, int count, int act,
+                                             mcke_stream_t stream) {
+  static const char* who = "mcke_sm100_bias_act_f32_group";
+  clear_error();
+  if (!jobs) return fail(MCKE_INVALID_ARGUMENT, "%s: null job array", who);
+  if (count < 1 || count > kGroupMax)
+    return fail(MCKE_INVALID_ARGUMENT, "%s: count must be 1..%d, got %d", who, kGroupMax, count);
+  if (!act_ok(act)) return fail(MCKE_INVALID_ARGUMENT, "%s: unknown activation %d", who, act);
+  BiasActGroup G{};
+  G.count = count;
+  uint64_t blocks = 0;
+  for (int k = 0; k < count; ++k) {
+    const mcke_bias_act_job& j = jobs[k];
+    if (j.rows < 0 || j.cols < 0) return fail(MCKE_INVALID_ARGUMENT, "%s: job %d: negative extent", who, k);
+    G.first_block[k] = static_cast<uint32_t>(blocks);
+    if (j.rows == 0 || j.cols == 0) continue;  // nothing to do, as for one call
+    if (!j.x || !j.bias || !j.y) return fail(MCKE_INVALID_ARGUMENT, "%s: job %d: null pointer", who, k);
+    if (j.cols % 512 != 0)
+      return fail(MCKE_INVALID_ARGUMENT, "%s: job %d: cols must be a multiple of 512, got %lld", who, k,
+                  static_cast<long long>(j.cols));
+    if (!aligned(j.x, 16) || !aligned(j.y, 16) || !aligned(j.bias, 16))
+      return fail(MCKE_INVALID_ARGUMENT, "%s: job %d: x, bias and y must be 16-byte aligned", who, k);
+    const uint64_t per_row = static_cast<uint64_t>(j.cols / 512);
+    const uint64_t chunks = static_cast<uint64_t>(j.rows) * per_row;
+    if (chunks >= (uint64_t{1} << 31)) return fail(MCKE_INVALID_ARGUMENT, "%s: job %d: too large", who, k);
+    G.x[k] = j.x;
+    G.bias[k] = j.bias;
+    G.y[k] = j.y;
+    G.chunks[k] = static_cast<uint32_t>(chunks);
+    G.per_row[k] = static_cast<uint32_t>(per_row);
+    G.shift[k] = (per_row & (per_row - 1)) == 0 ? __builtin_ctzll(per_row) : -1;
+    blocks += (chunks + 7) / 8;
+    if (blocks >= (uint64_t{1} << 31)) return fail(MCKE_INVALID_ARGUMENT, "%s: too many blocks", who);
+  }
+  G.first_block[count] = static_cast<uint32_t>(blocks);
+  // The jobs run at the same time: a job's output may overlap no job's
+  // input, bias or output (its own input included: no in-place).
+  for (int k = 0; k < count; ++k) {
+    const std::size_t yb = static_cast<std::size_t>(G.chunks[k]) * 512 * sizeof(float);
+    for (int i = 0; i < count; ++i) {
+      const std::size_t xb = static_cast<std::size_t>(G.chunks[i]) * 512 * sizeof(float);
+      const std::size_t bb = static_cast<std::size_t>(G.per_row[i]) * 512 * sizeof(float);
+      if (overlaps(G.y[k], yb, G.x[i], xb) || overlaps(G.y[k], yb, G.bias[i], bb) ||
+          (i != k && overlaps(G.y[k], yb, G.y[i], static_cast<std::size_t>(G.chunks[i]) * 512 * sizeof(float))))
+        return fail(MCKE_INVALID_ARGUMENT, "%s: job %d's output overlaps job %d's operands", who, k, i);
+    }
+  }
+  if (blocks == 0) return MCKE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned g = static_cast<unsigned>(blocks);
+  switch (act) {
+    case MCKE_ACT_RELU: launch_async(bias_act_f32_group_kernel<ActRelu>, g, kThreads, 0, s, G); break;
+    case MCKE_ACT_GELU_ERF: launch_async(bias_act_f32_group_kernel<ActGeluErf>, g, kThreads, 0, s, G); break;
+    case MCKE_ACT_GELU_TANH: launch_async(bias_act_f32_group_kernel<ActGeluTanh>, g, kThreads, 0, s, G); break;
+    default: launch_async(bias_act_f32_group_kernel<ActNone>, g, kThreads, 0, s, G); break;
   }
   return check_launch(who);
 }

@@ -145,6 +145,12 @@ class GraphExecutor {
 
   [[nodiscard]] const TensorPlan& tensor_plan(TensorId t) const { return tplan_.at(t); }
   [[nodiscard]] int stream_of(NodeId n) const { return node_stream_.at(n); }
+  // Launch items in enqueue order: one node each, or (kLevelGrouped) the
+  // nodes one grouped launch runs together.  The memory plan treats an item
+  // as one step: its nodes run at the same time.
+  [[nodiscard]] std::size_t num_launch_items() const { return items_.size(); }
+  [[nodiscard]] const std::vector<NodeId>& launch_item(std::size_t i) const { return items_.at(i); }
+  [[nodiscard]] int launch_item_of(NodeId n) const { return item_of_.at(n); }
   [[nodiscard]] std::size_t arena_bytes(int device_index) const { return arena_bytes_.at(device_index); }
   [[nodiscard]] int num_devices() const { return static_cast<int>(opts_.devices.size()); }
   [[nodiscard]] const ExecutorOptions& options() const noexcept { return opts_; }
@@ -156,6 +162,7 @@ class GraphExecutor {
   struct Impl;
   [[nodiscard]] Status place();
   [[nodiscard]] Status assign_streams();
+  [[nodiscard]] int groupable_act(NodeId nid) const;
   [[nodiscard]] Status plan_memory();
   [[nodiscard]] Tensor local_tensor(TensorId t, int d) const;
   [[nodiscard]] Status enqueue(bool capturing);
@@ -176,6 +183,8 @@ class GraphExecutor {
   std::vector<std::size_t> scratch_bytes_;                   // per stream index
   std::vector<std::vector<std::int64_t>> exchange_offset_;  // [device][node] (or -1)
   std::vector<bool> view_rows_;  // per node: input 0 is a replicated tensor read as local rows
+  std::vector<std::vector<NodeId>> items_;  // launch items in enqueue order
+  std::vector<int> item_of_;                // per node: its launch item
   std::size_t event_edges_ = 0;
   bool planned_ = false;
   std::unique_ptr<Impl> impl_;

@@ -131,6 +131,7 @@ class BiasActOp final : public Op {
  public:
   explicit BiasActOp(BiasActParams p) : p_(p) {}
   [[nodiscard]] std::string_view type_name() const override { return "BiasAct"; }
+  [[nodiscard]] const BiasActParams& params() const noexcept { return p_; }
   [[nodiscard]] Status launch(const OpContext&, const std::vector<Tensor>&, const std::vector<Tensor>&) override;
   [[nodiscard]] StatusOr<std::vector<TensorDesc>> infer(const std::vector<TensorDesc>&) const override;
   [[nodiscard]] OpCost cost(const std::vector<TensorDesc>&) const override;

@@ -59,6 +59,25 @@ struct GemmTile {
     if (cols % w == 0 && addr % (sizeof(float) * static_cast<std::size_t>(w)) == 0) return w;
   return 1;
 }
+// Independent fp32 bias + activation jobs in one launch (no counterpart in
+// the reference; the executor's grouped level schedule): each job is
+// launch_bias_act_f32 with vector width 4 on cols % 512 == 0 and 16-byte
+// aligned operands, and no job's y overlaps any job's operands.
+struct BiasActJob {
+  const float* x = nullptr;
+  const float* bias = nullptr;
+  float* y = nullptr;
+  std::int64_t rows = 0, cols = 0;
+};
+inline constexpr int kBiasActGroupMax = 16;
+[[nodiscard]] Status launch_bias_act_f32_group(const BiasActJob* jobs, int count, Activation act,
+                                              rt::StreamHandle stream);
+// True when a job qualifies for launch_bias_act_f32_group.
+[[nodiscard]] inline bool bias_act_groupable(const void* x, const void* bias, const void* y,
+                                             std::int64_t cols) noexcept {
+  const auto a = [](const void* p) { return reinterpret_cast<std::uintptr_t>(p) % 16 == 0; };
+  return cols > 0 && cols % 512 == 0 && a(x) && a(bias) && a(y);
+}
 // bf16 x/y (raw 16-bit patterns), float bias.
 [[nodiscard]] Status launch_bias_act_bf16(const std::uint16_t* x, const float* bias, std::uint16_t* y,
                                          std::int64_t rows, std::int64_t cols, Activation act,

@@ -1,6 +1,7 @@
 // capi_host.cpp -- extern "C" wrappers of the C++ host layer (include/mcke_host.h).
 #include "mcke_host.h"
 
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -118,7 +119,7 @@ int mcke_graph_roofline_ms(const mcke_graph* g, double peak_tflops, double peak_
 
 mcke_executor* mcke_executor_create_policy(mcke_graph* g, const int* devices, int num_devices, int num_streams,
                                            unsigned flags, int schedule, int memory) {
-  if (!g || !devices || num_devices < 1 || schedule < 0 || schedule > 2 || memory < 0 || memory > 3) return nullptr;
+  if (!g || !devices || num_devices < 1 || schedule < 0 || schedule > 3 || memory < 0 || memory > 3) return nullptr;
   mcke::ExecutorOptions o;
   o.devices.assign(devices, devices + num_devices);
   o.num_streams = num_streams > 0 ? num_streams : 4;
@@ -203,6 +204,15 @@ int mcke_executor_arena_bytes(mcke_executor* e, int device_index, size_t* bytes_
 int mcke_executor_num_events(mcke_executor* e, size_t* out) {
   EX_CHECK(e);
   if (out) *out = e->ex->num_events();
+  return 0;
+}
+int mcke_executor_launch_items(mcke_executor* e, size_t* items_out, size_t* largest_out) {
+  EX_CHECK(e);
+  std::size_t largest = 0;
+  for (std::size_t i = 0; i < e->ex->num_launch_items(); ++i)
+    largest = std::max(largest, e->ex->launch_item(i).size());
+  if (items_out) *items_out = e->ex->num_launch_items();
+  if (largest_out) *largest_out = largest;
   return 0;
 }
 int mcke_executor_validate_numerics(mcke_executor* e, int repeats, int* passed, int* configs, char* detail,

@@ -293,7 +293,67 @@ Status GraphExecutor::assign_streams() {
       ++event_edges_;
     }
   }
+  // Launch items: one node each in topological order, or (kLevelGrouped) level
+  // by level with the groupable bias + activation nodes of a level gathered,
+  // per activation, into items of up to kBiasActGroupMax nodes.
+  items_.clear();
+  item_of_.assign(N, -1);
+  if (opts_.schedule != SchedulePolicy::kLevelGrouped) {
+    for (NodeId nid : g_.topo_order()) {
+      item_of_[nid] = static_cast<int>(items_.size());
+      items_.push_back({nid});
+    }
+    return OkStatus();
+  }
+  std::vector<int> level(N, 0);
+  int max_level = 0;
+  for (NodeId nid : g_.topo_order()) {
+    for (TensorId t : g_.node(nid).inputs) {
+      const NodeId p = g_.producer(t);
+      if (p != kInvalidNode) level[nid] = std::max(level[nid], level[p] + 1);
+    }
+    max_level = std::max(max_level, level[nid]);
+  }
+  std::vector<std::vector<NodeId>> by_level(static_cast<std::size_t>(max_level) + 1);
+  for (NodeId nid : g_.topo_order()) by_level[level[nid]].push_back(nid);
+  for (const auto& nodes : by_level) {
+    int open[4] = {-1, -1, -1, -1};  // the item still taking nodes, per activation
+    for (NodeId nid : nodes) {
+      const int act = groupable_act(nid);
+      if (act < 0) {
+        item_of_[nid] = static_cast<int>(items_.size());
+        items_.push_back({nid});
+        continue;
+      }
+      int& it = open[act];
+      if (it < 0 || static_cast<int>(items_[it].size()) == kernels::kBiasActGroupMax) {
+        it = static_cast<int>(items_.size());
+        items_.emplace_back();
+      }
+      item_of_[nid] = it;
+      items_[it].push_back(nid);
+    }
+  }
   return OkStatus();
+}
+
+// The activation (0-3) of a bias + activation node the grouped kernel can run
+// on every device -- fp32, vector width 4 or automatic, no row-block limit,
+// local rows x cols with cols % 512 == 0 -- else -1.  (Operand alignment is
+// checked again at launch; a group that fails it runs node by node.)
+int GraphExecutor::groupable_act(NodeId nid) const {
+  const Node& n = g_.node(nid);
+  const auto* op = dynamic_cast<const BiasActOp*>(n.op.get());
+  if (!op || n.inputs.size() != 2 || n.outputs.size() != 1 || view_rows_[nid]) return -1;
+  const BiasActParams& p = op->params();
+  if ((p.vector_width != 0 && p.vector_width != 4) || p.max_row_blocks != 0) return -1;
+  const TensorId x = n.inputs[0];
+  if (g_.tensor(x).dtype != DType::kF32 || g_.tensor(n.outputs[0]).dtype != DType::kF32) return -1;
+  for (int d = 0; d < num_devices(); ++d) {
+    const Shape& sh = tplan_[x].local_shape[d];
+    if (sh.rank() != 2 || sh.rows() <= 0 || sh.cols() <= 0 || sh.cols() % 512 != 0) return -1;
+  }
+  return static_cast<int>(p.act);
 }
 
 // ------------------------------------------------------------- memory
@@ -306,8 +366,9 @@ Status GraphExecutor::plan_memory() {
   const int S = std::max(1, opts_.num_streams);
   const auto& order = g_.topo_order();
   const std::size_t T = g_.num_tensors();
+  // Positions are launch items: the nodes of one item run at the same time.
   std::vector<std::int64_t> pos(g_.num_nodes(), 0);
-  for (std::size_t i = 0; i < order.size(); ++i) pos[order[i]] = static_cast<std::int64_t>(i);
+  for (NodeId nid : order) pos[nid] = item_of_[nid];
   // Last use and the set of streams touching each tensor.
   std::vector<std::int64_t> last(T, -1);
   std::vector<bool> single_stream(T, true);
@@ -356,8 +417,11 @@ Status GraphExecutor::plan_memory() {
     };
     for (TensorId t = 0; t < T; ++t)  // inputs and outputs own their bytes
       if (g_.is_input(t) || g_.is_output(t)) tplan_[t].offset[d] = static_cast<std::int64_t>(fresh(tplan_[t].local_bytes(d)));
-    for (std::size_t i = 0; i < order.size(); ++i) {
-      const Node& n = g_.node(order[i]);
+    for (std::size_t i = 0; i < items_.size(); ++i) {
+     // every output of the item first, then the frees: no node of an item
+     // may take a block another node of the same item still reads
+     for (NodeId nid : items_[i]) {
+      const Node& n = g_.node(nid);
       const int s = node_stream_[n.id];
       for (TensorId o : n.outputs) {
         if (tplan_[o].offset[d] >= 0) continue;
@@ -376,13 +440,17 @@ Status GraphExecutor::plan_memory() {
         block_of[o] = best;
         tplan_[o].offset[d] = static_cast<std::int64_t>(blocks[best].off);
       }
-      // Free intermediates whose last use was this node (same-stream blocks only).
+     }
+     for (NodeId nid : items_[i]) {
+      const Node& n = g_.node(nid);
+      // Free intermediates whose last use was this item (same-stream blocks only).
       for (TensorId t : n.inputs)
         if (block_of[t] >= 0 && last[t] == static_cast<std::int64_t>(i) && blocks[block_of[t]].stream >= 0)
           blocks[block_of[t]].free = true;
       for (TensorId o : n.outputs)
         if (block_of[o] >= 0 && last[o] == static_cast<std::int64_t>(i) && blocks[block_of[o]].stream >= 0)
           blocks[block_of[o]].free = true;
+     }
     }
     // Exchange buffers: own partial + all devices' partials, per exchanging node.
     for (NodeId nid : order) {
@@ -747,20 +815,63 @@ Status GraphExecutor::enqueue(bool /*capturing*/) {
       for (int s = 1; s < S; ++s) MCKE_RETURN_IF_ERROR(dv.streams[s].wait(dv.done[0]));
     }
   }
-  for (NodeId nid : g_.topo_order()) {
+  // One device's launch of one node.
+  auto launch_one = [&](NodeId nid, int d) -> Status {
+    Node& n = g_.node(nid);
+    const auto& L = impl_->launches[nid];
+    rt::DeviceGuard g(impl_->devs[d].device);
+    const Status st = n.op->launch(L.ctx[d], L.ins[d], L.outs[d]);
+    if (!st.ok())
+      return Status(st.code(), "node '" + n.name + "' on device " + std::to_string(L.ctx[d].device) + ": " + st.message());
+    return OkStatus();
+  };
+  for (const std::vector<NodeId>& item : items_) {
+    const NodeId nid = item[0];
     Node& n = g_.node(nid);
     const int s = node_stream_[nid];
     auto& L = impl_->launches[nid];
     const std::vector<OpContext>& ctx = L.ctx;
-    const auto& ins = L.ins;
     const auto& outs = L.outs;
-    for (int d = 0; d < D; ++d)
-      for (int p : waits_[nid]) MCKE_RETURN_IF_ERROR(impl_->devs[d].streams[s].wait(impl_->devs[d].node_events[p]));
-    for (int d = 0; d < D; ++d) {
-      rt::DeviceGuard g(impl_->devs[d].device);
-      const Status st = n.op->launch(ctx[d], ins[d], outs[d]);
-      if (!st.ok()) return Status(st.code(), "node '" + n.name + "' on device " + std::to_string(ctx[d].device) + ": " + st.message());
+    for (NodeId m : item)
+      for (int d = 0; d < D; ++d)
+        for (int p : waits_[m]) MCKE_RETURN_IF_ERROR(impl_->devs[d].streams[s].wait(impl_->devs[d].node_events[p]));
+    if (item.size() > 1) {
+      // A grouped item (kLevelGrouped): the bias + activation nodes of one
+      // level, one launch per device; node by node if an operand turns out
+      // misaligned (the plan already treats the nodes as concurrent, so
+      // running them in turn is safe too).
+      const auto act = static_cast<const BiasActOp*>(n.op.get())->params().act;
+      const kernels::Activation ka = act == BiasActParams::Act::kRelu      ? kernels::Activation::kRelu
+                                     : act == BiasActParams::Act::kGeluErf  ? kernels::Activation::kGeluErf
+                                     : act == BiasActParams::Act::kGeluTanh ? kernels::Activation::kGeluTanh
+                                                                             : kernels::Activation::kNone;
+      for (int d = 0; d < D; ++d) {
+        kernels::BiasActJob jobs[kernels::kBiasActGroupMax];
+        bool grouped = item.size() <= static_cast<std::size_t>(kernels::kBiasActGroupMax);
+        for (std::size_t k = 0; grouped && k < item.size(); ++k) {
+          const auto& Lk = impl_->launches[item[k]];
+          const Tensor& x = Lk.ins[d][0];
+          jobs[k] = {x.data_as<float>(), Lk.ins[d][1].data_as<float>(), Lk.outs[d][0].data_as<float>(),
+                     x.shape.rows(), x.shape.cols()};
+          grouped = jobs[k].x && jobs[k].bias && jobs[k].y &&
+                    kernels::bias_act_groupable(jobs[k].x, jobs[k].bias, jobs[k].y, jobs[k].cols);
+        }
+        if (grouped) {
+          rt::DeviceGuard g(impl_->devs[d].device);
+          const Status st = kernels::launch_bias_act_f32_group(jobs, static_cast<int>(item.size()), ka, ctx[d].stream);
+          if (!st.ok())
+            return Status(st.code(), "group of " + std::to_string(item.size()) + " nodes from '" + n.name +
+                                         "' on device " + std::to_string(ctx[d].device) + ": " + st.message());
+        } else {
+          for (NodeId m : item) MCKE_RETURN_IF_ERROR(launch_one(m, d));
+        }
+      }
+      for (NodeId m : item)
+        if (record_after_[m])
+          for (auto& dv : impl_->devs) MCKE_RETURN_IF_ERROR(dv.node_events[m].record(dv.streams[s]));
+      continue;
     }
+    for (int d = 0; d < D; ++d) MCKE_RETURN_IF_ERROR(launch_one(nid, d));
     const std::size_t eb = n.op->exchange_bytes();
     if (eb > 0 && !(impl_->p2p && D > 1)) {
       const std::vector<void*>& gathered = L.gathered;
@@ -913,6 +1024,7 @@ const char* schedule_name(SchedulePolicy p) {
     case SchedulePolicy::kSequential: return "sequential";
     case SchedulePolicy::kLevelParallel: return "level-parallel";
     case SchedulePolicy::kChainGreedy: return "chain-greedy";
+    case SchedulePolicy::kLevelGrouped: return "level-grouped";
   }
   return "?";
 }
@@ -948,7 +1060,8 @@ StatusOr<NumericsResult> GraphExecutor::validate_numerics(int repeats) {
     bool graph;
   };
   std::vector<Config> configs{{SchedulePolicy::kSequential, MemoryPolicy::kAllocPerTensor, false}};  // golden
-  for (SchedulePolicy sp : {SchedulePolicy::kSequential, SchedulePolicy::kLevelParallel, SchedulePolicy::kChainGreedy})
+  for (SchedulePolicy sp : {SchedulePolicy::kSequential, SchedulePolicy::kLevelParallel, SchedulePolicy::kChainGreedy,
+                            SchedulePolicy::kLevelGrouped})
     for (MemoryPolicy mp : {MemoryPolicy::kAllocPerTensor, MemoryPolicy::kReuseSameStream, MemoryPolicy::kReuseHappensBefore})
       for (bool gr : {false, true})
         if (sp != SchedulePolicy::kSequential || mp != MemoryPolicy::kAllocPerTensor || gr)

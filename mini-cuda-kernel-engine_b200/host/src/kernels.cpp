@@ -38,6 +38,15 @@ Status launch_bias_act_f32(const float* x, const float* bias, float* y, std::int
                                            max_row_blocks, st(stream)));
 }
 
+Status launch_bias_act_f32_group(const BiasActJob* jobs, int count, Activation act, rt::StreamHandle stream) {
+  static_assert(sizeof(BiasActJob) == sizeof(mcke_bias_act_job) && kBiasActGroupMax == MCKE_BIAS_ACT_GROUP_MAX,
+                "the job layout is the C-ABI's");
+  if (count < 1 || count > kBiasActGroupMax || !jobs) return InvalidArgumentError("launch_bias_act_f32_group: count");
+  mcke_bias_act_job c[kBiasActGroupMax];
+  for (int k = 0; k < count; ++k) c[k] = {jobs[k].x, jobs[k].bias, jobs[k].y, jobs[k].rows, jobs[k].cols};
+  return from_capi(mcke_sm100_bias_act_f32_group(c, count, static_cast<int>(act), st(stream)));
+}
+
 Status launch_bias_add_f32(const float* x, const float* bias, float* y, std::int64_t rows, std::int64_t cols,
                            int vector_width, rt::StreamHandle stream) {
   return from_capi(mcke_sm100_bias_add_f32(x, bias, y, rows, cols, vector_width, st(stream)));

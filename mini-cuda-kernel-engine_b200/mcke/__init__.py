@@ -72,6 +72,7 @@ def lib() -> ctypes.CDLL:
             "mcke_sm100_peak_mma_flops": (ctypes.c_double, [i64, i32]),
             "mcke_sm100_peak_mma_bf16": (i32, [i64, i32, vp]),
             "mcke_sm100_bias_act_f32": (i32, [vp, vp, vp, i64, i64, i32, i32, i32, vp]),
+            "mcke_sm100_bias_act_f32_group": (i32, [vp, i32, i32, vp]),
             "mcke_sm100_bias_add_f32": (i32, [vp, vp, vp, i64, i64, i32, vp]),
             "mcke_sm100_activation_f32": (i32, [vp, vp, i64, i32, i32, vp]),
             "mcke_sm100_bias_act_bf16": (i32, [vp, vp, vp, i64, i64, i32, vp]),
@@ -199,6 +200,29 @@ def peak_mma(ctas: int, iters: int, stream=None):
 
 
 # ---- bias + activation -------------------------------------------------------
+
+class BiasActJob(ctypes.Structure):
+    """mcke_bias_act_job: one job of mcke_sm100_bias_act_f32_group."""
+    _fields_ = [("x", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p),
+                ("rows", ctypes.c_int64), ("cols", ctypes.c_int64)]
+
+
+BIAS_ACT_GROUP_MAX = 16  # MCKE_BIAS_ACT_GROUP_MAX
+
+
+def bias_act_group(jobs, act="gelu_tanh", stream=None):
+    """Independent float32 y = act(x + bias) jobs in one launch
+    (mcke_sm100_bias_act_f32_group); ``jobs``: (x [rows, cols], bias [cols],
+    y [rows, cols]) triples with cols % 512 == 0.  Returns the outputs."""
+    arr = (BiasActJob * max(len(jobs), 1))()
+    for k, (x, b, y) in enumerate(jobs):
+        _need(x, torch.float32, "x"); _need(b, torch.float32, "bias"); _need(y, torch.float32, "y")
+        arr[k] = BiasActJob(_ptr(x), _ptr(b), _ptr(y), x.shape[0], x.shape[1])
+    dev_t = jobs[0][0] if jobs else None
+    _check(lib().mcke_sm100_bias_act_f32_group(ctypes.cast(arr, ctypes.c_void_p), len(jobs), _act(act),
+                                               _stream(dev_t, stream) if dev_t is not None else None))
+    return [y for _, _, y in jobs]
+
 
 def bias_act(x, bias, act="gelu_tanh", vector_width: int = 4, out=None, max_row_blocks: int = 0,
              stream=None):

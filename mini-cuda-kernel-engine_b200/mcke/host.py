@@ -59,6 +59,7 @@ def lib() -> ctypes.CDLL:
             "mcke_executor_placement": (i32, [vp, u32, ctypes.POINTER(ctypes.c_int)]),
             "mcke_executor_arena_bytes": (i32, [vp, i32, ctypes.POINTER(ctypes.c_size_t)]),
             "mcke_executor_num_events": (i32, [vp, ctypes.POINTER(ctypes.c_size_t)]),
+            "mcke_executor_launch_items": (i32, [vp, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
             "mcke_executor_last_run_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float)]),
             "mcke_executor_create_policy": (vp, [vp, ctypes.POINTER(ctypes.c_int), i32, i32, ctypes.c_uint, i32, i32]),
             "mcke_executor_validate_numerics": (i32, [vp, i32, ctypes.POINTER(ctypes.c_int),
@@ -83,7 +84,7 @@ class AllocStats(ctypes.Structure):
                                                "peak_bytes_in_use")] + [("name", ctypes.c_char * 24)]
 
 
-SCHEDULE = {"sequential": 0, "level_parallel": 1, "chain_greedy": 2}
+SCHEDULE = {"sequential": 0, "level_parallel": 1, "chain_greedy": 2, "level_grouped": 3}
 MEMORY = {"alloc_per_tensor": 0, "reuse_same_stream": 2, "reuse_happens_before": 3}
 
 
@@ -243,3 +244,9 @@ class Executor:
         b = ctypes.c_size_t()
         _check(lib().mcke_executor_num_events(self._h, ctypes.byref(b)))
         return b.value
+
+    def launch_items(self) -> tuple[int, int]:
+        """(number of launch items, nodes in the largest) of the plan."""
+        n, big = ctypes.c_size_t(), ctypes.c_size_t()
+        _check(lib().mcke_executor_launch_items(self._h, ctypes.byref(n), ctypes.byref(big)))
+        return n.value, big.value

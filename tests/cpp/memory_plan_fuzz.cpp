@@ -5,8 +5,11 @@
 // bytes overlap in the arena, stream order must put one tensor's whole life
 // (its producer and every reader) before the other's producer:
 //   * both lives on one stream, and
-//   * the earlier life's last step before the later producer in topological
-//     order.
+//   * the earlier life's last step in an earlier launch item than the later
+//     producer (the nodes of one grouped launch run at the same time, so the
+//     same item does not count as before).
+// Half the graphs have 512-column tensors, so the level-grouped schedule
+// forms grouped launches; the run fails if none formed.
 // Graph inputs and outputs must overlap nothing.  No GPU is touched.
 // Prints "OK" and exits 0, or prints the first violation and exits 1.
 #include <cstdint>
@@ -32,7 +35,8 @@ struct Built {
 // through bias+act or softmax; every tensor nobody reads becomes an output.
 void build(Built& b, std::mt19937& rng, int n) {
   const std::int64_t rows = 16 + static_cast<std::int64_t>(rng() % 8) * 16;
-  const std::int64_t cols = 64 + static_cast<std::int64_t>(rng() % 4) * 64;
+  const std::int64_t cols = rng() % 2 ? 512 * (1 + static_cast<std::int64_t>(rng() % 2))
+                                      : 64 + static_cast<std::int64_t>(rng() % 4) * 64;
   TensorDesc xd;
   xd.shape = Shape{rows, cols};
   xd.name = "x";
@@ -69,8 +73,7 @@ namespace {
 // 0 when every overlap is ordered; else prints the first violation.
 int check(const Graph& g, const GraphExecutor& ex, const std::string& what, long* overlaps) {
   std::vector<int> pos(g.num_nodes());
-  const auto& topo = g.topo_order();
-  for (std::size_t i = 0; i < topo.size(); ++i) pos[topo[i]] = static_cast<int>(i);
+  for (NodeId n = 0; n < static_cast<NodeId>(g.num_nodes()); ++n) pos[n] = ex.launch_item_of(n);
   auto life = [&](TensorId t) {
     std::vector<NodeId> l{g.producer(t)};
     for (NodeId c : g.consumers(t)) l.push_back(c);
@@ -109,9 +112,9 @@ int check(const Graph& g, const GraphExecutor& ex, const std::string& what, long
 }  // namespace
 
 int main() {
-  long overlaps = 0, plans = 0;
+  long overlaps = 0, plans = 0, grouped = 0;
   const SchedulePolicy schedules[] = {SchedulePolicy::kSequential, SchedulePolicy::kLevelParallel,
-                                      SchedulePolicy::kChainGreedy};
+                                      SchedulePolicy::kChainGreedy, SchedulePolicy::kLevelGrouped};
   const MemoryPolicy memories[] = {MemoryPolicy::kReuseSameStream, MemoryPolicy::kReuseHappensBefore};
   for (unsigned seed = 0; seed < 150; ++seed) {
     std::mt19937 rng(seed);
@@ -143,13 +146,15 @@ int main() {
             return 1;
           }
           ++plans;
+          for (std::size_t i = 0; i < ex.num_launch_items(); ++i) grouped += ex.launch_item(i).size() > 1;
           if (check(b.g, ex, what, &overlaps)) return 1;
         }
   }
-  if (overlaps == 0) {
-    std::printf("no plan reused memory: the fuzz exercised nothing\n");
+  if (overlaps == 0 || grouped == 0) {
+    std::printf("no plan reused memory or grouped a launch: the fuzz exercised nothing\n");
     return 1;
   }
-  std::printf("%ld plans, %ld overlapping tensor pairs, all ordered\nOK\n", plans, overlaps);
+  std::printf("%ld plans, %ld grouped launches, %ld overlapping tensor pairs, all ordered\nOK\n", plans, grouped,
+              overlaps);
   return 0;
 }

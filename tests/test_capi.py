@@ -73,6 +73,25 @@ def test_argument_validation_needs_no_device(mcke):
     assert b"stamps" in l.mcke_sm100_last_error_string()
     assert l.mcke_sm100_reduce_full_p2p_f32_timeline(bogus, 1000, 0, bogus, 1, 0, 1, bogus,
                                                       ctypes.c_void_p(0x1004), None) == mcke.INVALID_ARGUMENT
+    # grouped bias + activation: count, shape, alignment and overlap checks
+    J = mcke.BiasActJob
+    jobs = (J * 17)()
+    grp = lambda n: l.mcke_sm100_bias_act_f32_group(ctypes.cast(jobs, ctypes.c_void_p), n, 3, None)  # noqa: E731
+    assert l.mcke_sm100_bias_act_f32_group(None, 1, 3, None) == mcke.INVALID_ARGUMENT
+    assert grp(0) == mcke.INVALID_ARGUMENT and grp(17) == mcke.INVALID_ARGUMENT
+    jobs[0] = J(0x100000, 0x200000, 0x300000, 4, 256)
+    assert grp(1) == mcke.INVALID_ARGUMENT and b"multiple of 512" in l.mcke_sm100_last_error_string()
+    jobs[0] = J(0x100004, 0x200000, 0x300000, 4, 512)
+    assert grp(1) == mcke.INVALID_ARGUMENT and b"aligned" in l.mcke_sm100_last_error_string()
+    jobs[0] = J(0x100000, 0x200000, 0x300000, 4, 512)  # x: 8 KB from 0x100000
+    jobs[1] = J(0x400000, 0x200000, 0x100800, 4, 512)  # y inside job 0's x
+    assert grp(2) == mcke.INVALID_ARGUMENT and b"overlaps" in l.mcke_sm100_last_error_string()
+    jobs[1] = J(0x400000, 0x200000, 0x300000, 4, 512)  # same y as job 0
+    assert grp(2) == mcke.INVALID_ARGUMENT and b"overlaps" in l.mcke_sm100_last_error_string()
+    jobs[0] = J(0x100000, 0x200000, 0x100000, 4, 512)  # in place
+    assert grp(1) == mcke.INVALID_ARGUMENT and b"overlaps" in l.mcke_sm100_last_error_string()
+    jobs[0] = J(None, None, None, 0, 512)  # one empty job: nothing to launch
+    assert grp(1) == mcke.OK
     # the _ex entry points take MCKE_REDUCE_EARLY_READ (1) and nothing else
     assert l.mcke_sm100_reduce_full_f32_ex(bogus, 1000, ctypes.c_void_p(0x2000), bogus, 1 << 20, 2,
                                            None) == mcke.INVALID_ARGUMENT

@@ -118,6 +118,40 @@ def test_fanout_join_records_events(host):
     assert ex2.num_events() == 1
 
 
+def _fanout(host, cols, branches=4, depth=4, acts=("gelu_tanh",)):
+    g = host.Graph()
+    x = g.input("x", (64, cols))
+    for br in range(branches):
+        h = x
+        for k in range(depth):
+            b = g.input(f"b{br}_{k}", (cols,))
+            h = g.bias_act(h, b, acts[br % len(acts)], name=f"n{br}_{k}")
+        g.output(h)
+    g.finalize()
+    return g
+
+
+def test_level_grouped_schedule_groups_a_level_of_bias_nodes(host):
+    # 4 branches x 4 bias+GELU nodes: one grouped launch per level, no events
+    ex = host.Executor(_fanout(host, 512), devices=[0], streams_per_device=4, schedule="level_grouped")
+    ex.plan_dry()
+    assert ex.launch_items() == (4, 4)
+    assert ex.num_events() == 0
+    # two activations: a level splits into one group per activation
+    ex = host.Executor(_fanout(host, 1024, acts=("gelu_tanh", "relu")), devices=[0, 1], schedule="level_grouped")
+    ex.plan_dry()
+    assert ex.launch_items() == (8, 2)
+    # 256 columns: the grouped kernel does not take them, one launch per node
+    ex = host.Executor(_fanout(host, 256), devices=[0], schedule="level_grouped")
+    ex.plan_dry()
+    assert ex.launch_items() == (16, 1)
+    # the other schedules never group
+    for sched in ("sequential", "level_parallel", "chain_greedy"):
+        ex = host.Executor(_fanout(host, 512), devices=[0], schedule=sched)
+        ex.plan_dry()
+        assert ex.launch_items() == (16, 1), sched
+
+
 def test_column_split_gemm_and_range_split_reduce(host):
     g = host.Graph()
     a = g.input("A", (512, 256))

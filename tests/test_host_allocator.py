@@ -94,10 +94,11 @@ def test_memory_policies(host):
 
 
 def test_memory_plan_fuzz_finds_no_unordered_reuse(host, tmp_path):
-    # tests/cpp/memory_plan_fuzz.cpp: 150 random DAGs x 3 schedules x 2 reuse
-    # policies x {1, 2, 4} streams, planned dry; every two tensors that share
-    # arena bytes must have one's whole life before the other's producer, on
-    # one stream (the reference's memory-plan race fuzz, run on this planner)
+    # tests/cpp/memory_plan_fuzz.cpp: 150 random DAGs x 4 schedules (grouped
+    # launches included) x 2 reuse policies x {1, 2, 4} streams, planned dry;
+    # every two tensors that share arena bytes must have one's whole life in
+    # earlier launch items than the other's producer, on one stream (the
+    # reference's memory-plan race fuzz, run on this planner)
     exe = str(tmp_path / "fuzz")
     src = os.path.join(ROOT, "tests", "cpp", "memory_plan_fuzz.cpp")
     cmd = ["g++", "-std=c++20", "-O1", "-Wall", "-Wextra", "-Werror", src, "-o", exe,
@@ -108,4 +109,4 @@ def test_memory_plan_fuzz_finds_no_unordered_reuse(host, tmp_path):
     assert r.returncode == 0, r.stderr[-4000:]
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("OK"), r.stdout + r.stderr
-    assert "all ordered" in r.stdout
+    assert "all ordered" in r.stdout and " 0 grouped" not in r.stdout

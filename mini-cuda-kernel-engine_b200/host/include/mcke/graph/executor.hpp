@@ -19,11 +19,16 @@
 //           2. streams: per device, a node inherits the stream of its first
 //              producer unless a sibling already did (chain-greedy), else the
 //              least-recently-used stream; an event is recorded after a
-//              producer and waited on by each consumer on another stream;
+//              producer and waited on by each consumer on another stream.
+//              Launch items: one node each in topological order, or
+//              (kLevelGrouped) stream 0 level by level, a level's groupable
+//              fp32 bias + activation nodes gathered into grouped launches;
 //           3. memory: per device one arena; graph inputs and outputs own
 //              their bytes, intermediates reuse a freed block of the same
-//              stream (stream order makes that reuse race-free), scratch is
-//              one block per stream sized by the largest workspace_bytes();
+//              stream (stream order makes that reuse race-free), counting in
+//              launch items (an item's outputs are placed before anything it
+//              reads is freed); scratch is one block per stream sized by the
+//              largest workspace_bytes();
 //           4. allocation (one cudaMalloc per device), NCCL communicators
 //              (only if some node exchanges), streams and events.
 //   run_async()  enqueues every node on every device; never synchronises.

@@ -1284,6 +1284,15 @@ def run_profile(args) -> None:
             b = torch.rand(16384, generator=gen, device=dev) * 2 - 1
             y = torch.empty_like(x)
             fn = lambda: mcke.bias_act(x, b, "gelu_tanh", out=y)  # noqa: E731
+        elif name == "bias_group":
+            # one level of the reference's fan-out as one grouped launch:
+            # four 2048 x 2048 bias + GELU jobs (mcke_sm100_bias_act_f32_group)
+            jobs = []
+            for _ in range(4):
+                xj = torch.randn(2048, 2048, generator=gen, device=dev)
+                bj = torch.rand(2048, generator=gen, device=dev) * 2 - 1
+                jobs.append((xj, bj, torch.empty_like(xj)))
+            fn = lambda: mcke.bias_act_group(jobs, "gelu_tanh")  # noqa: E731
         elif name == "gemm_bf16":
             a = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
             b = (torch.rand(GEMM_N, GEMM_N, generator=gen, device=dev) * 2 - 1).to(torch.bfloat16)
